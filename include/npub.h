@@ -1,0 +1,177 @@
+/*
+ * npub.h -- C ABI of libnpub, the sm_100a (B200) implementation of the compute
+ * that KwanyoungCho/NPU_COMP lowers onto its NPU: the W8A16 matmul and the
+ * Llama-layer vector ops (RMSNorm, SwiGLU, softmax/exp, RoPE, attention),
+ * plus the NPU's elementwise instruction semantics.
+ *
+ * Conventions
+ *   - Every pointer argument named as a tensor is a DEVICE pointer owned by
+ *     the caller.  fp16 tensors are passed as `void*` (IEEE binary16), int8
+ *     weights as `int8_t*`, fp32 buffers as `float*`.
+ *   - Leading dimensions (`ld*`) are in elements.  Matrices are row-major.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call is
+ *     stream-ordered and asynchronous; nothing allocates device memory.
+ *     Calls that need scratch take a caller-provided workspace and report its
+ *     size through the matching *_workspace() query.
+ *   - Every call returns an int status: NPUB_OK (0) or a negative NPUB_ERR_*.
+ *     No C++ exception crosses this boundary.  npub_strerror() names a status.
+ *   - Entry points are thread-safe; the per-device state (driver entry point,
+ *     SM count, device error word) is created once under a lock.
+ *
+ * Reference interface replaced (paths inside KwanyoungCho/NPU_COMP):
+ *   b_program_examples/npu.py:41-47   matmul(asm, aAddr, bAddr, cAddr, M, K, N, act)
+ *   b_program_examples/npu.py:62-71   run(asm, gbuf, gn, rundir, maxrun)
+ *   _poc/mysim.cpp:83-145             the cmodel's execute loop that run() drives
+ *   b_program_examples/llama_layer.py:71-152   vec/unary/rmsnorm/rope/attention/FFN macros
+ *   d_compiler/npu_compiler/legalize.py:20-149 the compiler's op recipes
+ */
+#ifndef NPUB_H
+#define NPUB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  Failures of the reference's CPU path surface as a
+ * CalledProcessError from subprocess.run(check=True) (npu.py:66-69) or a
+ * CodegenError (d_compiler/npu_compiler/codegen.py:21-22); here they are
+ * return codes. */
+#define NPUB_OK 0
+#define NPUB_ERR_INVALID_ARG (-1)    /* bad shape, stride, alignment or null pointer */
+#define NPUB_ERR_UNSUPPORTED (-2)    /* valid request outside what the kernels implement */
+#define NPUB_ERR_CUDA (-3)           /* a CUDA runtime/driver call failed (see npub_last_cuda_error) */
+#define NPUB_ERR_WORKSPACE (-4)      /* workspace missing or smaller than *_workspace() */
+#define NPUB_ERR_DEVICE_TIMEOUT (-5) /* a bounded device-side wait gave up (npub_device_error) */
+#define NPUB_ERR_NO_DEVICE (-6)      /* no sm_100 device current */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int npub_version(void);
+/* Text for a status code (static storage). */
+const char* npub_strerror(int status);
+/* The cudaError_t of the last NPUB_ERR_CUDA on this thread (0 if none). */
+int npub_last_cuda_error(void);
+/* Reads (and with clear != 0 resets) the current device's error word, which
+ * kernels set when a bounded wait gives up.  Synchronises the device.
+ * Returns 0 when no kernel reported an error. */
+int npub_device_error(int clear);
+
+/* ------------------------------------------------------------------ GEMM --
+ * W8A16 matmul (replaces the matmul macro b_program_examples/npu.py:41-47
+ * executed by m_mul, _poc/mysim.cpp:109-113, with the weights int8 and a
+ * per-output-channel scale):
+ *
+ *   C[m, n] = fp16( alpha * scale[n] * sum_k A[m, k] * Wq[n, k] )  (+ R[m, n])
+ *
+ * A    fp16 [M, K] (lda >= K, lda % 8 == 0, 16-byte aligned)
+ * Wq   int8 [N, K] K-major (ldw >= K, ldw % 16 == 0, 16-byte aligned)
+ * scale fp16 [N] (NULL = 1)
+ * C    fp16 [M, N] (ldc >= N);  R fp16 [M, N] residual added after scaling (NULL = none)
+ * K % 16 == 0.  Accumulation is fp32 on the tensor cores (tcgen05).
+ * workspace: npub_w8a16_gemm_workspace(M, N, K) bytes (split-K partials);
+ * may be NULL when that query returns 0. */
+int npub_w8a16_gemm(const void* A, int64_t lda, const int8_t* Wq, int64_t ldw, const void* scale, void* C,
+                    int64_t ldc, const void* R, int64_t ldr, int M, int N, int K, float alpha, void* workspace,
+                    size_t workspace_bytes, void* stream);
+size_t npub_w8a16_gemm_workspace(int M, int N, int K);
+
+/* Same contract with fp16 weights W [N, K] (ldw % 8 == 0): the plain fp16
+ * matmul of npu.py:41-47 / mysim.cpp:109-113 on tensor cores (used for the
+ * fp16 lm_head and for matmuls whose weights are not quantised). */
+int npub_f16_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C, int64_t ldc,
+                  const void* R, int64_t ldr, int M, int N, int K, float alpha, void* workspace,
+                  size_t workspace_bytes, void* stream);
+size_t npub_f16_gemm_workspace(int M, int N, int K);
+
+/* Quantise fp32 weights W [K, N] (row-major, x @ W convention of
+ * llama_layer.py:27-31) to int8 Wq [N, K] K-major with fp16 per-output-channel
+ * scales:  s[n] = fp16(max_k |W[k,n]| / 127),  Wq[n,k] = clip(rint(W[k,n] / s[n]), -127, 127);
+ * a column of zeros gets s = 0 and Wq = 0.  (The reference has no quantiser;
+ * this is the symmetric per-channel scheme its W8A16 target is defined by.) */
+int npub_quantize_w8(const float* W, int64_t ldw, int K, int N, int8_t* Wq, int64_t ldq, void* scale, void* stream);
+
+/* ---------------------------------------------------------- vector ops --
+ * RMSNorm, d_compiler/npu_compiler/legalize.py:30-47, b_program_examples/llama_layer.py:79-89:
+ *   y[r, :] = fp16( x[r, :] / sqrt(mean(x[r, :]^2) + eps) * gamma )   (fp32 math)
+ * x, y fp16 [rows, d] (ld % 8 == 0), gamma fp16 [d]; d % 8 == 0.
+ * If `residual` is not NULL, x + residual is normalised and also written back
+ * to `x_out` (fp16, may alias x) -- the residual add of llama_layer.py:139. */
+int npub_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr, void* x_out, int64_t ldxo,
+                 const void* gamma, void* y, int64_t ldy, int rows, int d, float eps, void* stream);
+
+/* SwiGLU, legalize.py:130-149, llama_layer.py:143-151:
+ *   h = fp16( g / (1 + exp(-g)) * u )   (fp32 math), g, u, h fp16 [rows, cols]. */
+int npub_swiglu(const void* g, int64_t ldg, const void* u, int64_t ldu, void* h, int64_t ldh, int rows, int cols,
+                void* stream);
+
+/* Row softmax, legalize.py:97-114 (mask -30000), stable form of
+ * d_compiler/npu_compiler/model.py:149-150:
+ *   p[b, r, c] = exp(scale*s - max) / sum(...) over c <= r + causal_offset
+ * (all c when causal_offset < 0 is NPUB_NO_CAUSAL); masked entries are written
+ * as 0 up to the next multiple of 128 past the diagonal (what the causal
+ * context GEMM reads) or to the row end when zero_full != 0.
+ * s, p fp16 [batch, rows, ld] (may alias). */
+#define NPUB_NO_CAUSAL (-1)
+int npub_softmax_rows(const void* s, void* p, int64_t ld, int64_t batch_stride, int batch, int rows, int cols,
+                      float scale, int causal_offset, int zero_full, void* stream);
+
+/* RoPE (rotate_half convention), llama_layer.py:33-40,96-112, legalize.py:67-94:
+ *   x'[d] = x[d]*cos(p*th_i) + rh[d]*sin(p*th_i),  th_i = theta^(-2i/hd), i = d mod hd/2,
+ *   rh = [-x[hd/2:], x[:hd/2]],  p = pos0 + t  (or positions[t] when not NULL).
+ * In place on x fp16 [tokens, heads*head_dim] with row stride ldx; head_dim even, % 8 == 0. */
+int npub_rope(void* x, int64_t ldx, int tokens, int heads, int head_dim, const int32_t* positions, int pos0,
+              float theta, void* stream);
+
+/* -------------------------------------------------------- attention ----
+ * Causal prefill attention, llama_layer.py:114-137, legalize.py:117-127 for
+ * every sequence b and head h: S = Q K^T * scale + mask; P = softmax(S); O = P V.
+ * q, k, v: fp16 rows of `batch` sequences of `tokens` rows each (sequence b at
+ * rows [b*tokens, (b+1)*tokens)), row strides ldq/ldk/ldv; head h reads
+ * columns [h*head_dim, (h+1)*head_dim) of q and kv head h / (heads/kv_heads)
+ * of k and v (grouped-query heads).  out fp16 [batch*tokens, heads*head_dim] (ldo).
+ * head_dim % 16 == 0, head_dim <= 256; batch*heads <= 65535.
+ * Scratch: npub_attention_workspace() bytes, 256-byte aligned. */
+int npub_attention_prefill(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                           void* out, int64_t ldo, int batch, int tokens, int heads, int kv_heads, int head_dim,
+                           float scale, int causal, void* workspace, size_t workspace_bytes, void* stream);
+size_t npub_attention_workspace(int batch, int tokens, int heads, int head_dim);
+
+/* Decode attention over a KV cache (one new query token per sequence):
+ *   out[b, h, :] = softmax(q[b,h,:] . K[b, kvh, :len[b], :]^T * scale) V[b, kvh, :len[b], :]
+ * q fp16 [batch, heads*head_dim] (ldq); caches fp16 [batch, kv_heads, cap, head_dim]
+ * (contiguous per head); lens int32 [batch] (NULL = all `ctx_len`).
+ * head_dim == 128.  Flash-decoding split over the context; scratch:
+ * npub_attention_decode_workspace(). */
+int npub_attention_decode(const void* q, int64_t ldq, const void* k_cache, const void* v_cache, int64_t cap,
+                          const int32_t* lens, int ctx_len, void* out, int64_t ldo, int batch, int heads,
+                          int kv_heads, int head_dim, float scale, void* workspace, size_t workspace_bytes,
+                          void* stream);
+size_t npub_attention_decode_workspace(int batch, int heads, int ctx_len, int head_dim);
+
+/* Append one token's K and V rows per sequence to the caches at position
+ * pos[b] (or pos0 when pos is NULL): cache[b, h, pos, :] = src[b, h*hd : (h+1)*hd]. */
+int npub_kv_append(const void* k_new, int64_t ldk, const void* v_new, int64_t ldv, void* k_cache, void* v_cache,
+                   int64_t cap, const int32_t* pos, int pos0, int batch, int kv_heads, int head_dim, void* stream);
+
+/* ------------------------------------------------- NPU ISA semantics ----
+ * One compute instruction of the NPU over PE buffers (_poc/mysim.cpp:114-141):
+ * `word` is the 32-bit instruction (opcodes 0x01-0x13 vector, 0x40-0x43
+ * matrix elementwise; 0x42 with mode 2 is the matrix multiply and is not
+ * taken here).  in1/in2/prev_out/out are fp32 device arrays of n elements
+ * (in2 read only in vector mode; prev_out is the previous PE output, read by
+ * mul-add 0x0C).  Float32 arithmetic as the cmodel does it; logical, shift,
+ * compare and convert results are bit-exact with the cmodel on x86-64. */
+int npub_isa_vector(uint32_t word, const float* in1, const float* in2, const float* prev_out, float* out, int64_t n,
+                    void* stream);
+/* The cmodel's store rounding (mysim.cpp:19-38, applied by save 0x98):
+ * fp32 -> fp16 round-to-nearest-even, NaN -> sign|0x7C00|0x200. */
+int npub_f32_to_f16(const float* x, uint16_t* y, int64_t n, void* stream);
+/* fp16 -> fp32 (the cmodel's load of the G-buffer). */
+int npub_f16_to_f32(const uint16_t* x, float* y, int64_t n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NPUB_H */

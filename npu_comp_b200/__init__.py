@@ -1,0 +1,11 @@
+"""npu_comp_b200 -- B200 (sm_100a) implementation of the compute that the
+KwanyoungCho/NPU_COMP compiler lowers onto its NPU: the W8A16 matmul and the
+Llama-layer ops, behind an operator surface named after
+b_program_examples/npu.py.  Kernels live in libnpub.so (C ABI: include/npub.h).
+"""
+from .npu import (  # noqa: F401
+    NpubError, attention, attention_decode, f16_bits_to_f32, f32_to_f16_bits, fp16, isa_vector, kv_append, matmul,
+    quantize_w8, rmsnorm, rope, softmax, swiglu,
+)
+
+__version__ = "1.0.0"

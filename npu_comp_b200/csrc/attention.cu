@@ -1,0 +1,411 @@
+// Attention for sm_100a.
+//
+// Prefill (llama_layer.py:114-137, legalize.py:117-127): per head
+//   S = Q K^T * scale (tcgen05 GEMM, tiles above the causal diagonal skipped)
+//   P = softmax(S) in place (vector_ops.cu)
+//   O = P V (tcgen05 GEMM, K loop cut at the diagonal), V transposed once so
+//   both GEMM operands are K-major.
+// Decode: flash-decoding over an fp16 KV cache [batch, kv_heads, cap, 128],
+// HBM-bound; 4 lanes per key with 128-bit loads, online softmax in fp32,
+// split over the context when there are too few (sequence, head) pairs.
+#include "common.cuh"
+#include "gemm_tc.h"
+
+namespace npub {
+
+// V rows of `batch` sequences [batch*T, ldv] (kv head h at columns h*hd) ->
+// Vt [batch*kvh, hd, tp] (tokens contiguous, zero past T).
+__global__ void transpose_heads_kernel(const __half* __restrict__ v, int64_t ldv, int T, int kvh, int hd,
+                                       __half* __restrict__ vt, int64_t tp) {
+    __shared__ __half tile[64][64 + 2];
+    const int bz = blockIdx.z;  // b * kvh + h
+    const int b = bz / kvh, h = bz % kvh;
+    const int t0 = blockIdx.x * 64, d0 = blockIdx.y * 64;
+    for (int i = threadIdx.y; i < 64; i += blockDim.y) {
+        for (int j = threadIdx.x; j < 64; j += blockDim.x) {
+            const int t = t0 + i, d = d0 + j;
+            tile[i][j] = (t < T && d < hd) ? v[((int64_t)b * T + t) * ldv + (int64_t)h * hd + d] : __float2half(0.0f);
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 64; i += blockDim.y) {
+        for (int j = threadIdx.x; j < 64; j += blockDim.x) {
+            const int d = d0 + i, t = t0 + j;
+            if (d < hd && t < (int)tp) vt[((int64_t)bz * hd + d) * tp + t] = tile[j][i];
+        }
+    }
+}
+
+// ---------------------------------------------------------------- decode
+constexpr int kDecHd = 128;
+constexpr int kDecWarps = 4;
+
+struct DecodeArgs {
+    const __half* q;
+    int64_t ldq;
+    const __half* kc;
+    const __half* vc;
+    int64_t cap;
+    const int32_t* lens;
+    int ctx;
+    __half* out;
+    int64_t ldo;
+    int heads, kv_heads, splits, chunk;
+    float scale_log2;  // scale * log2(e)
+    float* part;       // [bh, splits, hd + 2] when splits > 1
+};
+
+__device__ __forceinline__ void ld8f(const __half* p, float (&f)[8]) {
+    uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float2 t = __half22float2(h[i]);
+        f[2 * i] = t.x;
+        f[2 * i + 1] = t.y;
+    }
+}
+
+// Lane l of a warp: key slot g = l / 4 (8 keys per step), part j = l % 4 owning
+// dims {8*(j + 4*i) .. +8 : i = 0..3}, so each 16-byte load instruction of the
+// four lanes of a key covers 64 contiguous bytes of the row.
+__global__ void __launch_bounds__(kDecWarps * 32) decode_attn_kernel(const DecodeArgs a) {
+    const int bh = blockIdx.x;
+    const int b = bh / a.heads, h = bh % a.heads;
+    const int kvh = h / (a.heads / a.kv_heads);
+    const int split = blockIdx.y;
+    const int len = min((int64_t)(a.lens ? a.lens[b] : a.ctx), a.cap);
+    const int c0 = split * a.chunk;
+    const int c1 = min(len, c0 + a.chunk);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, j = lane & 3;
+
+    float q[32];
+    const __half* qrow = a.q + (int64_t)b * a.ldq + (int64_t)h * kDecHd;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float f[8];
+        ld8f(qrow + 8 * (j + 4 * i), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q[8 * i + e] = f[e] * a.scale_log2;
+    }
+    const __half* kbase = a.kc + ((int64_t)b * a.kv_heads + kvh) * a.cap * kDecHd;
+    const __half* vbase = a.vc + ((int64_t)b * a.kv_heads + kvh) * a.cap * kDecHd;
+
+    float m = -INFINITY, l = 0.0f, acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+
+    // keys handled by this warp: c0 + warp*8 + g, stepping by kDecWarps*8
+    for (int key = c0 + warp * 8 + g; key - g < c1; key += kDecWarps * 8) {
+        const bool ok = key < c1;
+        float kf[32], vf[32];
+        const __half* kr = kbase + (int64_t)(ok ? key : c0) * kDecHd;
+        const __half* vr = vbase + (int64_t)(ok ? key : c0) * kDecHd;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float f[8];
+            ld8f(kr + 8 * (j + 4 * i), f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) kf[8 * i + e] = f[e];
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float f[8];
+            ld8f(vr + 8 * (j + 4 * i), f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) vf[8 * i + e] = f[e];
+        }
+        float sdot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sdot += q[i] * kf[i];
+        sdot += __shfl_xor_sync(0xffffffffu, sdot, 1);
+        sdot += __shfl_xor_sync(0xffffffffu, sdot, 2);
+        if (ok) {
+            const float mn = fmaxf(m, sdot);
+            const float corr = exp2f(m - mn);
+            const float pk = exp2f(sdot - mn);
+            l = l * corr + pk;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[i] = acc[i] * corr + pk * vf[i];
+            m = mn;
+        }
+    }
+    // combine the 8 key slots of the warp (lanes with equal j)
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        const float mo = __shfl_xor_sync(0xffffffffu, m, o);
+        const float lo = __shfl_xor_sync(0xffffffffu, l, o);
+        const float mn = fmaxf(m, mo);
+        const float ca = (m == -INFINITY) ? 0.0f : exp2f(m - mn);
+        const float cb = (mo == -INFINITY) ? 0.0f : exp2f(mo - mn);
+        l = l * ca + lo * cb;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const float ao = __shfl_xor_sync(0xffffffffu, acc[i], o);
+            acc[i] = acc[i] * ca + ao * cb;
+        }
+        m = mn;
+    }
+    // combine warps through shared memory
+    __shared__ float sm_m[kDecWarps], sm_l[kDecWarps];
+    __shared__ float sm_acc[kDecWarps][kDecHd];
+    if (g == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) sm_acc[warp][8 * (j + 4 * i) + e] = acc[8 * i + e];
+        if (j == 0) {
+            sm_m[warp] = m;
+            sm_l[warp] = l;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < kDecHd) {
+        const int d = threadIdx.x;
+        float M = -INFINITY;
+        for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, sm_m[w]);
+        float L = 0.0f, A = 0.0f;
+        for (int w = 0; w < kDecWarps; ++w) {
+            const float c = (sm_m[w] == -INFINITY) ? 0.0f : exp2f(sm_m[w] - M);
+            L += sm_l[w] * c;
+            A += sm_acc[w][d] * c;
+        }
+        if (a.splits == 1) {
+            a.out[(int64_t)b * a.ldo + (int64_t)h * kDecHd + d] = __float2half_rn(L > 0.0f ? A / L : 0.0f);
+        } else {
+            float* pp = a.part + ((int64_t)bh * a.splits + split) * (kDecHd + 2);
+            pp[d] = A;
+            if (d == 0) {
+                pp[kDecHd] = M;
+                pp[kDecHd + 1] = L;
+            }
+        }
+    }
+}
+
+__global__ void decode_combine_kernel(const float* __restrict__ part, int splits, int heads, __half* __restrict__ out,
+                                      int64_t ldo) {
+    const int bh = blockIdx.x;
+    const int b = bh / heads, h = bh % heads;
+    const int d = threadIdx.x;
+    const float* pp = part + (int64_t)bh * splits * (kDecHd + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < splits; ++s) M = fmaxf(M, pp[s * (kDecHd + 2) + kDecHd]);
+    float L = 0.0f, A = 0.0f;
+    for (int s = 0; s < splits; ++s) {
+        const float ms = pp[s * (kDecHd + 2) + kDecHd];
+        const float c = (ms == -INFINITY) ? 0.0f : exp2f(ms - M);
+        L += pp[s * (kDecHd + 2) + kDecHd + 1] * c;
+        A += pp[s * (kDecHd + 2) + d] * c;
+    }
+    out[(int64_t)b * ldo + (int64_t)h * kDecHd + d] = __float2half_rn(L > 0.0f ? A / L : 0.0f);
+}
+
+__global__ void kv_append_kernel(const __half* __restrict__ kn, int64_t ldk, const __half* __restrict__ vn,
+                                 int64_t ldv, __half* kc, __half* vc, int64_t cap, const int32_t* __restrict__ pos,
+                                 int pos0, int kvh, int hd) {
+    const int b = blockIdx.x;
+    const int p = pos ? pos[b] : pos0;
+    for (int i = threadIdx.x; i < kvh * hd; i += blockDim.x) {
+        const int h = i / hd, d = i % hd;
+        const int64_t dst = (((int64_t)b * kvh + h) * cap + p) * hd + d;
+        kc[dst] = kn[(int64_t)b * ldk + i];
+        vc[dst] = vn[(int64_t)b * ldv + i];
+    }
+}
+
+static int64_t pad8(int64_t x) { return (x + 7) / 8 * 8; }
+
+static int decode_splits(int bh, int ctx) {
+    const int sms = num_sms();
+    int s = 1;
+    while (bh * s < sms * 6 && ctx / (s * 2) >= 256 && s < 32) s *= 2;
+    return s;
+}
+
+}  // namespace npub
+
+using namespace npub;
+
+static size_t attn_s_bytes(int batch, int tokens, int heads) {
+    const int64_t tp = pad8(tokens);
+    return ((size_t)batch * heads * tokens * tp * 2 + 255) / 256 * 256;
+}
+
+extern "C" size_t npub_attention_workspace(int batch, int tokens, int heads, int head_dim) {
+    if (batch <= 0 || tokens <= 0 || heads <= 0 || head_dim <= 0) return 0;
+    const int64_t tp = pad8(tokens);
+    // S/P [batch*heads, tokens, tp] + Vt [batch*heads, head_dim, tp] (kv_heads <= heads)
+    const size_t v_bytes = ((size_t)batch * heads * head_dim * tp * 2 + 255) / 256 * 256;
+    return attn_s_bytes(batch, tokens, heads) + v_bytes;
+}
+
+extern "C" int npub_attention_prefill(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                                      int64_t ldv, void* out, int64_t ldo, int batch, int tokens, int heads,
+                                      int kv_heads, int head_dim, float scale, int causal, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+    NPUB_CHECK_ARG(batch >= 0 && tokens >= 0 && heads > 0 && kv_heads > 0 && heads % kv_heads == 0);
+    if (tokens == 0 || batch == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(q && k && v && out);
+    NPUB_CHECK_ARG(head_dim % 16 == 0 && head_dim > 0 && head_dim <= 256);
+    NPUB_CHECK_ARG(ldq % 8 == 0 && ldk % 8 == 0 && ldv % 8 == 0);
+    NPUB_CHECK_ARG(ldq >= (int64_t)heads * head_dim && ldk >= (int64_t)kv_heads * head_dim &&
+                   ldv >= (int64_t)kv_heads * head_dim && ldo >= (int64_t)heads * head_dim);
+    NPUB_CHECK_ARG(npub_aligned(q, 16) && npub_aligned(k, 16) && npub_aligned(v, 16));
+    NPUB_CHECK_ARG((int64_t)batch * heads <= 65535 && (int64_t)batch * tokens <= 0x7fffffffLL);
+    const size_t need = npub_attention_workspace(batch, tokens, heads, head_dim);
+    if (!workspace || workspace_bytes < need) return NPUB_ERR_WORKSPACE;
+    NPUB_CHECK_ARG(npub_aligned(workspace, 256));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int64_t tp = pad8(tokens);
+    __half* S = reinterpret_cast<__half*>(workspace);
+    __half* Vt = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(workspace) + attn_s_bytes(batch, tokens, heads));
+    const int group = heads / kv_heads;
+    const int off = causal ? 0 : NPUB_NO_CAUSAL;
+    const int rows_all = batch * tokens;
+
+    // 1) S[b*H + h] = Q_{b,h} K_{b,h/group}^T, fp16, row stride tp.  z = b*H + h.
+    {
+        GemmParams p;
+        memset(&p, 0, sizeof(p));
+        int rc = make_tmap_3d(&p.tmA, false, q, (uint64_t)head_dim, (uint64_t)heads, (uint64_t)rows_all,
+                              (uint64_t)head_dim, (uint64_t)ldq, 1, 128, true);
+        if (rc) return rc;
+        const int bt = pick_bt(tokens);
+        rc = make_tmap_3d(&p.tmB, false, k, (uint64_t)head_dim, (uint64_t)kv_heads, (uint64_t)rows_all,
+                          (uint64_t)head_dim, (uint64_t)ldk, 1, (uint32_t)bt, true);
+        if (rc) return rc;
+        p.a_rows = tokens;
+        p.b_rows = tokens;
+        p.k_tiles = (head_dim + 63) / 64;
+        p.a_row_dim = 2;
+        p.b_row_dim = 2;
+        p.zmod = heads;
+        p.za = ZMap{1, 0, tokens, 0};
+        p.zb = ZMap{group, 0, tokens, 0};
+        p.splits = 1;
+        p.k_tiles_per_split = p.k_tiles;
+        p.causal_mode = causal ? 1 : 0;
+        p.causal_off = 0;
+        p.out = S;
+        p.o_sa = tp;
+        p.o_sb = 1;
+        p.o_zl = (int64_t)tokens * tp;
+        p.o_zh = (int64_t)heads * tokens * tp;
+        p.alpha = 1.0f;
+        rc = run_gemm(p, false, bt, (tokens + 127) / 128, (tokens + bt - 1) / bt, batch * heads, st);
+        if (rc) return rc;
+    }
+    // 2) P = softmax(S * scale) in place
+    {
+        int rc = npub_softmax_rows(S, S, tp, (int64_t)tokens * tp, batch * heads, tokens, tokens, scale, off, 0,
+                                   stream);
+        if (rc) return rc;
+    }
+    // 3) Vt[b*KVH + kvh] = V_{b,kvh}^T
+    {
+        dim3 grid((unsigned)((tp + 63) / 64), (unsigned)((head_dim + 63) / 64), (unsigned)(batch * kv_heads));
+        transpose_heads_kernel<<<grid, dim3(32, 8), 0, st>>>(reinterpret_cast<const __half*>(v), ldv, tokens,
+                                                             kv_heads, head_dim, Vt, tp);
+        int rc = npub_internal_launch_status();
+        if (rc) return rc;
+    }
+    // 4) O[b*T + t, h*hd + d] = P_{b,h} Vt_{b,h/group}^T
+    {
+        GemmParams p;
+        memset(&p, 0, sizeof(p));
+        int rc = make_tmap_3d(&p.tmA, false, S, (uint64_t)tokens, (uint64_t)tokens, (uint64_t)batch * heads,
+                              (uint64_t)tp, (uint64_t)tokens * tp, 128, 1, true);
+        if (rc) return rc;
+        const int bt = pick_bt(head_dim);
+        rc = make_tmap_3d(&p.tmB, false, Vt, (uint64_t)tokens, (uint64_t)head_dim, (uint64_t)batch * kv_heads,
+                          (uint64_t)tp, (uint64_t)head_dim * tp, (uint32_t)bt, 1, true);
+        if (rc) return rc;
+        p.a_rows = tokens;
+        p.b_rows = head_dim;
+        p.k_tiles = (tokens + 63) / 64;
+        p.a_row_dim = 1;
+        p.b_row_dim = 1;
+        p.zmod = heads;
+        p.za = ZMap{1, heads, 0, 0};
+        p.zb = ZMap{group, kv_heads, 0, 0};
+        p.splits = 1;
+        p.k_tiles_per_split = p.k_tiles;
+        p.causal_mode = causal ? 2 : 0;
+        p.causal_off = 0;
+        p.out = out;
+        p.o_sa = ldo;
+        p.o_sb = 1;
+        p.o_zl = head_dim;
+        p.o_zh = (int64_t)tokens * ldo;
+        p.alpha = 1.0f;
+        rc = run_gemm(p, false, bt, (tokens + 127) / 128, (head_dim + bt - 1) / bt, batch * heads, st);
+        if (rc) return rc;
+    }
+    return NPUB_OK;
+}
+
+extern "C" size_t npub_attention_decode_workspace(int batch, int heads, int ctx_len, int head_dim) {
+    if (batch <= 0 || heads <= 0 || ctx_len <= 0 || head_dim != kDecHd) return 0;
+    const int s = decode_splits(batch * heads, ctx_len);
+    return s > 1 ? (size_t)batch * heads * s * (kDecHd + 2) * sizeof(float) : 0;
+}
+
+extern "C" int npub_attention_decode(const void* q, int64_t ldq, const void* k_cache, const void* v_cache, int64_t cap,
+                                     const int32_t* lens, int ctx_len, void* out, int64_t ldo, int batch, int heads,
+                                     int kv_heads, int head_dim, float scale, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
+    NPUB_CHECK_ARG(batch >= 0 && heads > 0 && kv_heads > 0 && heads % kv_heads == 0);
+    if (batch == 0) return NPUB_OK;
+    if (head_dim != kDecHd) return NPUB_ERR_UNSUPPORTED;
+    NPUB_CHECK_ARG(q && k_cache && v_cache && out && ctx_len >= 0 && cap >= ctx_len);
+    NPUB_CHECK_ARG(ldq % 8 == 0 && ldq >= (int64_t)heads * head_dim && ldo >= (int64_t)heads * head_dim);
+    NPUB_CHECK_ARG(npub_aligned(q, 16) && npub_aligned(k_cache, 16) && npub_aligned(v_cache, 16));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int bh = batch * heads;
+    const int ctx_max = ctx_len > 0 ? ctx_len : 1;
+    const int splits = decode_splits(bh, ctx_max);
+    DecodeArgs a;
+    a.q = reinterpret_cast<const __half*>(q);
+    a.ldq = ldq;
+    a.kc = reinterpret_cast<const __half*>(k_cache);
+    a.vc = reinterpret_cast<const __half*>(v_cache);
+    a.cap = cap;
+    a.lens = lens;
+    a.ctx = ctx_len;
+    a.out = reinterpret_cast<__half*>(out);
+    a.ldo = ldo;
+    a.heads = heads;
+    a.kv_heads = kv_heads;
+    a.splits = splits;
+    a.chunk = (ctx_max + splits - 1) / splits;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.part = nullptr;
+    if (splits > 1) {
+        const size_t need = (size_t)bh * splits * (kDecHd + 2) * sizeof(float);
+        if (!workspace || workspace_bytes < need) return NPUB_ERR_WORKSPACE;
+        a.part = reinterpret_cast<float*>(workspace);
+    }
+    decode_attn_kernel<<<dim3(bh, splits), kDecWarps * 32, 0, st>>>(a);
+    int rc = npub_internal_launch_status();
+    if (rc || splits == 1) return rc;
+    decode_combine_kernel<<<bh, kDecHd, 0, st>>>(a.part, splits, heads, a.out, ldo);
+    return npub_internal_launch_status();
+}
+
+extern "C" int npub_kv_append(const void* k_new, int64_t ldk, const void* v_new, int64_t ldv, void* k_cache,
+                              void* v_cache, int64_t cap, const int32_t* pos, int pos0, int batch, int kv_heads,
+                              int head_dim, void* stream) {
+    NPUB_CHECK_ARG(batch >= 0 && kv_heads > 0 && head_dim > 0);
+    if (batch == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(k_new && v_new && k_cache && v_cache);
+    NPUB_CHECK_ARG(pos || (pos0 >= 0 && pos0 < cap));
+    NPUB_CHECK_ARG(ldk >= (int64_t)kv_heads * head_dim && ldv >= (int64_t)kv_heads * head_dim);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    kv_append_kernel<<<batch, 256, 0, st>>>(reinterpret_cast<const __half*>(k_new), ldk,
+                                            reinterpret_cast<const __half*>(v_new), ldv,
+                                            reinterpret_cast<__half*>(k_cache), reinterpret_cast<__half*>(v_cache), cap,
+                                            pos, pos0, kv_heads, head_dim);
+    return npub_internal_launch_status();
+}

@@ -1,0 +1,68 @@
+// Library-wide C ABI pieces: version, status strings, CUDA error capture and
+// the per-device error word that kernels set when a bounded wait gives up.
+#include "common.cuh"
+
+// One int per device context (module globals are instantiated per device).
+__device__ int g_npub_device_error;
+
+static thread_local int t_last_cuda_error = 0;
+
+void npub_internal_set_cuda_error(cudaError_t e) { t_last_cuda_error = (int)e; }
+
+int npub_internal_launch_status() {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        t_last_cuda_error = (int)e;
+        return NPUB_ERR_CUDA;
+    }
+    return NPUB_OK;
+}
+
+int* npub_internal_device_error_word() {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_npub_device_error) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return reinterpret_cast<int*>(p);
+}
+
+extern "C" int npub_version(void) { return 10000; }
+
+extern "C" const char* npub_strerror(int status) {
+    switch (status) {
+        case NPUB_OK: return "ok";
+        case NPUB_ERR_INVALID_ARG: return "invalid argument (shape, stride, alignment or null pointer)";
+        case NPUB_ERR_UNSUPPORTED: return "unsupported configuration";
+        case NPUB_ERR_CUDA: return "CUDA error";
+        case NPUB_ERR_WORKSPACE: return "workspace missing or too small";
+        case NPUB_ERR_DEVICE_TIMEOUT: return "a device-side wait timed out";
+        case NPUB_ERR_NO_DEVICE: return "no sm_100 device";
+        default: return "unknown status";
+    }
+}
+
+extern "C" int npub_last_cuda_error(void) { return t_last_cuda_error; }
+
+extern "C" int npub_device_error(int clear) {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        t_last_cuda_error = (int)e;
+        return NPUB_ERR_CUDA;
+    }
+    int v = 0;
+    e = cudaMemcpyFromSymbol(&v, g_npub_device_error, sizeof(int));
+    if (e != cudaSuccess) {
+        t_last_cuda_error = (int)e;
+        return NPUB_ERR_CUDA;
+    }
+    if (clear) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_npub_device_error, &zero, sizeof(int));
+        if (e != cudaSuccess) {
+            t_last_cuda_error = (int)e;
+            return NPUB_ERR_CUDA;
+        }
+    }
+    return v;
+}

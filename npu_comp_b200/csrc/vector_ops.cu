@@ -1,0 +1,378 @@
+// Bandwidth-bound Llama-layer vector kernels for sm_100a: RMSNorm (with the
+// fused residual add), SwiGLU, causal row softmax, RoPE, and the W8
+// quantiser.  All use 128-bit coalesced loads/stores of fp16 and fp32 math
+// with warp-shuffle reductions.
+#include "common.cuh"
+
+#include <math.h>
+
+namespace npub {
+
+constexpr int kVec = 8;  // fp16 elements per 128-bit access
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float2 t = __half22float2(h[i]);
+        f[2 * i] = t.x;
+        f[2 * i + 1] = t.y;
+    }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+    uint4 u;
+    __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    return u;
+}
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NT / 32; ++i) t += red[i];
+    return t;
+}
+
+template <int NT>
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float t = red[0];
+#pragma unroll
+    for (int i = 1; i < NT / 32; ++i) t = fmaxf(t, red[i]);
+    return t;
+}
+
+// ------------------------------------------------------------ RMSNorm
+// One CTA per row; up to CH chunks of 8 elements per thread kept in registers.
+template <int NT, int CH>
+__global__ void __launch_bounds__(NT) rmsnorm_kernel(const __half* __restrict__ x, int64_t ldx,
+                                                     const __half* __restrict__ r, int64_t ldr, __half* xo,
+                                                     int64_t ldxo, const __half* __restrict__ gamma,
+                                                     __half* __restrict__ y, int64_t ldy, int d, float eps) {
+    __shared__ float red[NT / 32];
+    const int row = blockIdx.x;
+    const int nch = d / kVec;
+    const __half* xr = x + (int64_t)row * ldx;
+    float v[CH][8];
+    float ss = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        const int ch = threadIdx.x + c * NT;
+        if (ch < nch) {
+            uint4 u = *reinterpret_cast<const uint4*>(xr + ch * kVec);
+            unpack8(u, v[c]);
+            if (r) {
+                float rv[8];
+                unpack8(*reinterpret_cast<const uint4*>(r + (int64_t)row * ldr + ch * kVec), rv);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[c][i] = __half2float(__float2half_rn(v[c][i] + rv[i]));
+                *reinterpret_cast<uint4*>(xo + (int64_t)row * ldxo + ch * kVec) = pack8(v[c]);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ss += v[c][i] * v[c][i];
+        }
+    }
+    const float tot = block_sum<NT>(ss, red);
+    const float inv = 1.0f / sqrtf(tot / (float)d + eps);
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        const int ch = threadIdx.x + c * NT;
+        if (ch < nch) {
+            float g[8], o[8];
+            unpack8(*reinterpret_cast<const uint4*>(gamma + ch * kVec), g);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = (v[c][i] * inv) * g[i];
+            *reinterpret_cast<uint4*>(y + (int64_t)row * ldy + ch * kVec) = pack8(o);
+        }
+    }
+}
+
+// ------------------------------------------------------------ SwiGLU
+__global__ void swiglu_vec_kernel(const __half* __restrict__ g, int64_t ldg, const __half* __restrict__ u,
+                                  int64_t ldu, __half* __restrict__ h, int64_t ldh, int rows, int cols) {
+    const int cpr = cols / kVec;
+    const int64_t total = (int64_t)rows * cpr;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int rr = (int)(i / cpr), c = (int)(i - (int64_t)rr * cpr) * kVec;
+        float gv[8], uv[8], o[8];
+        unpack8(*reinterpret_cast<const uint4*>(g + (int64_t)rr * ldg + c), gv);
+        unpack8(*reinterpret_cast<const uint4*>(u + (int64_t)rr * ldu + c), uv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = gv[k] / (1.0f + expf(-gv[k])) * uv[k];
+        *reinterpret_cast<uint4*>(h + (int64_t)rr * ldh + c) = pack8(o);
+    }
+}
+
+__global__ void swiglu_scalar_kernel(const __half* __restrict__ g, int64_t ldg, const __half* __restrict__ u,
+                                     int64_t ldu, __half* __restrict__ h, int64_t ldh, int rows, int cols) {
+    const int64_t total = (int64_t)rows * cols;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int rr = (int)(i / cols), c = (int)(i - (int64_t)rr * cols);
+        const float gv = __half2float(g[(int64_t)rr * ldg + c]), uv = __half2float(u[(int64_t)rr * ldu + c]);
+        h[(int64_t)rr * ldh + c] = __float2half_rn(gv / (1.0f + expf(-gv)) * uv);
+    }
+}
+
+// ------------------------------------------------------------ softmax
+// One CTA per row.  Valid columns: [0, min(cols, r + off + 1)) when causal.
+// Masked columns are written as zero up to zend.
+template <int NT, int CH>
+__global__ void __launch_bounds__(NT) softmax_kernel(const __half* s, __half* p, int64_t ld, int64_t bstride,
+                                                     int rows, int cols, float scale, int off, int zero_full) {
+    __shared__ float red[NT / 32];
+    const int rr = blockIdx.x % rows;
+    const int b = blockIdx.x / rows;
+    const __half* sr = s + (int64_t)b * bstride + (int64_t)rr * ld;
+    __half* pr = p + (int64_t)b * bstride + (int64_t)rr * ld;
+    int valid = cols, zend = cols;
+    if (off >= 0) {
+        valid = min(cols, rr + off + 1);
+        if (!zero_full) {
+            const int a0 = (rr / 128) * 128;
+            zend = min(cols, ((a0 + 128 + off + 63) / 64) * 64);
+        }
+    }
+    const float l2e = 1.4426950408889634f;
+    const float sc = scale * l2e;  // work in base 2: exp(x) = exp2(x * log2 e)
+    float v[CH][8];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        const int e0 = (threadIdx.x + c * NT) * kVec;
+        if (e0 < valid) {
+            unpack8(*reinterpret_cast<const uint4*>(sr + e0), v[c]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                v[c][i] = (e0 + i < valid) ? v[c][i] * sc : -INFINITY;
+                mx = fmaxf(mx, v[c][i]);
+            }
+        }
+    }
+    mx = block_max<NT>(mx, red);
+    float sum = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        const int e0 = (threadIdx.x + c * NT) * kVec;
+        if (e0 < valid) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                v[c][i] = (e0 + i < valid) ? exp2f(v[c][i] - mx) : 0.0f;
+                sum += v[c][i];
+            }
+        }
+    }
+    sum = block_sum<NT>(sum, red);
+    const float inv = 1.0f / sum;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        const int e0 = (threadIdx.x + c * NT) * kVec;
+        if (e0 < zend) {
+            float o[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = (e0 < valid) ? v[c][i] * inv : 0.0f;
+            if (e0 + 8 <= zend) {
+                *reinterpret_cast<uint4*>(pr + e0) = pack8(o);
+            } else {
+                for (int i = 0; i < 8 && e0 + i < zend; ++i) pr[e0 + i] = __float2half_rn(o[i]);
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------ RoPE
+__global__ void rope_kernel(__half* x, int64_t ldx, int tokens, int heads, int hd, const int32_t* __restrict__ pos,
+                            int pos0, float log2_theta) {
+    const int half = hd / 2;
+    const int64_t total = (int64_t)tokens * heads * half;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int k = (int)(i % half);
+        const int64_t th = i / half;
+        const int h = (int)(th % heads), t = (int)(th / heads);
+        const int p = pos ? pos[t] : pos0 + t;
+        const float inv_freq = exp2f(-(2.0f * (float)k / (float)hd) * log2_theta);
+        float sn, cs;
+        sincosf((float)p * inv_freq, &sn, &cs);
+        __half* row = x + (int64_t)t * ldx + (int64_t)h * hd;
+        const float x1 = __half2float(row[k]), x2 = __half2float(row[k + half]);
+        row[k] = __float2half_rn(x1 * cs - x2 * sn);
+        row[k + half] = __float2half_rn(x2 * cs + x1 * sn);
+    }
+}
+
+// ------------------------------------------------------------ quantiser
+// W [K, N] fp32 -> Wq [N, K] int8 + s [N] fp16.  One CTA per 32 columns:
+// pass 1 column absmax (coalesced over n), pass 2 writes K-major rows via smem.
+__global__ void quantize_w8_kernel(const float* __restrict__ W, int64_t ldw, int K, int N, int8_t* __restrict__ q,
+                                   int64_t ldq, __half* __restrict__ s) {
+    __shared__ float colmax[8][32];
+    __shared__ float sinv[32];
+    __shared__ int8_t tile[32][64 + 4];
+    const int n0 = blockIdx.x * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+    const int n = n0 + tx;
+    float m = 0.0f;
+    if (n < N)
+        for (int k = ty; k < K; k += 8) m = fmaxf(m, fabsf(W[(int64_t)k * ldw + n]));
+    colmax[ty][tx] = m;
+    __syncthreads();
+    if (ty == 0) {
+        float mm = colmax[0][tx];
+        for (int i = 1; i < 8; ++i) mm = fmaxf(mm, colmax[i][tx]);
+        const __half sh = __float2half_rn(mm / 127.0f);
+        const float sf = __half2float(sh);
+        sinv[tx] = sf;
+        if (n < N) s[n] = sh;
+    }
+    __syncthreads();
+    for (int k0 = 0; k0 < K; k0 += 64) {
+        // load 64 x 32 block, quantise, transpose through smem
+        for (int kk = ty; kk < 64; kk += 8) {
+            const int k = k0 + kk;
+            int8_t qv = 0;
+            if (n < N && k < K) {
+                const float sf = sinv[tx];
+                if (sf > 0.0f) {
+                    float t = rintf(W[(int64_t)k * ldw + n] / sf);
+                    t = fminf(127.0f, fmaxf(-127.0f, t));
+                    qv = (int8_t)(int)t;
+                }
+            }
+            tile[tx][kk] = qv;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < 32 * 64; i += 256) {
+            const int nn = i / 64, kk = i % 64;
+            if (n0 + nn < N && k0 + kk < K) q[(int64_t)(n0 + nn) * ldq + k0 + kk] = tile[nn][kk];
+        }
+        __syncthreads();
+    }
+}
+
+static int grid_for(int64_t work, int threads) {
+    int64_t b = (work + threads - 1) / threads;
+    const int64_t cap = 148LL * 16;
+    if (b > cap) b = cap;
+    if (b < 1) b = 1;
+    return (int)b;
+}
+
+}  // namespace npub
+
+using namespace npub;
+
+extern "C" int npub_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr, void* x_out, int64_t ldxo,
+                            const void* gamma, void* y, int64_t ldy, int rows, int d, float eps, void* stream) {
+    NPUB_CHECK_ARG(rows >= 0 && d > 0);
+    if (rows == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(x && gamma && y);
+    NPUB_CHECK_ARG(d % kVec == 0 && ldx % kVec == 0 && ldy % kVec == 0 && ldx >= d && ldy >= d);
+    NPUB_CHECK_ARG(npub_aligned(x, 16) && npub_aligned(y, 16) && npub_aligned(gamma, 16));
+    if (residual) {
+        NPUB_CHECK_ARG(x_out && ldr % kVec == 0 && ldxo % kVec == 0 && ldr >= d && ldxo >= d);
+        NPUB_CHECK_ARG(npub_aligned(residual, 16) && npub_aligned(x_out, 16));
+    }
+    NPUB_CHECK_ARG(d <= 8 * 256 * 8);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const __half* xh = reinterpret_cast<const __half*>(x);
+    const __half* rh = reinterpret_cast<const __half*>(residual);
+    __half* xoh = reinterpret_cast<__half*>(x_out);
+    const __half* gh = reinterpret_cast<const __half*>(gamma);
+    __half* yh = reinterpret_cast<__half*>(y);
+    const int nch = d / kVec;
+    if (nch <= 128)
+        rmsnorm_kernel<128, 1><<<rows, 128, 0, st>>>(xh, ldx, rh, ldr, xoh, ldxo, gh, yh, ldy, d, eps);
+    else if (nch <= 256)
+        rmsnorm_kernel<256, 1><<<rows, 256, 0, st>>>(xh, ldx, rh, ldr, xoh, ldxo, gh, yh, ldy, d, eps);
+    else if (nch <= 512)
+        rmsnorm_kernel<256, 2><<<rows, 256, 0, st>>>(xh, ldx, rh, ldr, xoh, ldxo, gh, yh, ldy, d, eps);
+    else if (nch <= 1024)
+        rmsnorm_kernel<256, 4><<<rows, 256, 0, st>>>(xh, ldx, rh, ldr, xoh, ldxo, gh, yh, ldy, d, eps);
+    else
+        rmsnorm_kernel<256, 8><<<rows, 256, 0, st>>>(xh, ldx, rh, ldr, xoh, ldxo, gh, yh, ldy, d, eps);
+    return npub_internal_launch_status();
+}
+
+extern "C" int npub_swiglu(const void* g, int64_t ldg, const void* u, int64_t ldu, void* h, int64_t ldh, int rows,
+                           int cols, void* stream) {
+    NPUB_CHECK_ARG(rows >= 0 && cols >= 0);
+    if (rows == 0 || cols == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(g && u && h && ldg >= cols && ldu >= cols && ldh >= cols);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const bool vec = cols % kVec == 0 && ldg % kVec == 0 && ldu % kVec == 0 && ldh % kVec == 0 &&
+                     npub_aligned(g, 16) && npub_aligned(u, 16) && npub_aligned(h, 16);
+    if (vec) {
+        const int64_t work = (int64_t)rows * (cols / kVec);
+        swiglu_vec_kernel<<<grid_for(work, 256), 256, 0, st>>>(
+            reinterpret_cast<const __half*>(g), ldg, reinterpret_cast<const __half*>(u), ldu,
+            reinterpret_cast<__half*>(h), ldh, rows, cols);
+    } else {
+        const int64_t work = (int64_t)rows * cols;
+        swiglu_scalar_kernel<<<grid_for(work, 256), 256, 0, st>>>(
+            reinterpret_cast<const __half*>(g), ldg, reinterpret_cast<const __half*>(u), ldu,
+            reinterpret_cast<__half*>(h), ldh, rows, cols);
+    }
+    return npub_internal_launch_status();
+}
+
+extern "C" int npub_softmax_rows(const void* s, void* p, int64_t ld, int64_t batch_stride, int batch, int rows,
+                                 int cols, float scale, int causal_offset, int zero_full, void* stream) {
+    NPUB_CHECK_ARG(batch >= 0 && rows >= 0 && cols >= 0);
+    if (batch == 0 || rows == 0 || cols == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(s && p && ld >= cols && ld % kVec == 0 && npub_aligned(s, 16) && npub_aligned(p, 16));
+    NPUB_CHECK_ARG(batch == 1 || (batch_stride >= ld * rows && batch_stride % kVec == 0));
+    NPUB_CHECK_ARG(causal_offset >= NPUB_NO_CAUSAL);
+    NPUB_CHECK_ARG((int64_t)batch * rows <= 0x7fffffffLL);
+    NPUB_CHECK_ARG(cols <= 256 * 8 * 32);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int nb = batch * rows;
+    const __half* sh = reinterpret_cast<const __half*>(s);
+    __half* ph = reinterpret_cast<__half*>(p);
+    const int nch = (cols + kVec - 1) / kVec;
+    if (nch <= 128)
+        softmax_kernel<128, 1><<<nb, 128, 0, st>>>(sh, ph, ld, batch_stride, rows, cols, scale, causal_offset, zero_full);
+    else if (nch <= 256)
+        softmax_kernel<256, 1><<<nb, 256, 0, st>>>(sh, ph, ld, batch_stride, rows, cols, scale, causal_offset, zero_full);
+    else if (nch <= 1024)
+        softmax_kernel<256, 4><<<nb, 256, 0, st>>>(sh, ph, ld, batch_stride, rows, cols, scale, causal_offset, zero_full);
+    else if (nch <= 4096)
+        softmax_kernel<256, 16><<<nb, 256, 0, st>>>(sh, ph, ld, batch_stride, rows, cols, scale, causal_offset, zero_full);
+    else
+        softmax_kernel<256, 32><<<nb, 256, 0, st>>>(sh, ph, ld, batch_stride, rows, cols, scale, causal_offset, zero_full);
+    return npub_internal_launch_status();
+}
+
+extern "C" int npub_rope(void* x, int64_t ldx, int tokens, int heads, int head_dim, const int32_t* positions, int pos0,
+                         float theta, void* stream) {
+    NPUB_CHECK_ARG(tokens >= 0 && heads >= 0);
+    if (tokens == 0 || heads == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(x && head_dim > 0 && head_dim % 2 == 0 && ldx >= (int64_t)heads * head_dim && theta > 0.0f);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int64_t work = (int64_t)tokens * heads * (head_dim / 2);
+    rope_kernel<<<grid_for(work, 256), 256, 0, st>>>(reinterpret_cast<__half*>(x), ldx, tokens, heads, head_dim,
+                                                      positions, pos0, log2f(theta));
+    return npub_internal_launch_status();
+}
+
+extern "C" int npub_quantize_w8(const float* W, int64_t ldw, int K, int N, int8_t* Wq, int64_t ldq, void* scale,
+                                void* stream) {
+    NPUB_CHECK_ARG(K >= 0 && N >= 0);
+    if (K == 0 || N == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(W && Wq && scale && ldw >= N && ldq >= K);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    quantize_w8_kernel<<<(N + 31) / 32, 256, 0, st>>>(W, ldw, K, N, Wq, ldq, reinterpret_cast<__half*>(scale));
+    return npub_internal_launch_status();
+}

@@ -1,0 +1,299 @@
+"""Operator surface of the B200 build, named after the reference's
+`b_program_examples/npu.py` (fp16, matmul, run) and the Llama-layer macros of
+`b_program_examples/llama_layer.py:71-152` (rmsnorm, rope, attention, FFN).
+
+Where the reference's functions *emit NPU instructions* that mysim later
+executes (npu.py:41-47 appends an m_mul program; npu.py:62-71 runs it), these
+functions *compute*: they take CUDA tensors, launch the sm_100a kernels of
+libnpub.so on the current stream and return CUDA tensors.  Every op calls the
+C ABI of include/npub.h through ctypes; there is no CPU or PyTorch fallback.
+
+Errors: invalid shapes/dtypes raise ValueError (the reference raises
+CodegenError, d_compiler/npu_compiler/codegen.py:21-22); a failing CUDA call
+raises NpubError (the reference's CalledProcessError from run()).
+"""
+from __future__ import annotations
+
+import math
+import struct
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import NpubError  # noqa: F401  (re-exported)
+
+__all__ = [
+    "fp16", "quantize_w8", "matmul", "rmsnorm", "swiglu", "softmax", "rope", "attention",
+    "attention_decode", "kv_append", "isa_vector", "f32_to_f16_bits", "f16_bits_to_f32", "NpubError",
+]
+
+
+def fp16(x: float) -> float:
+    """Round a python float through FP16 (b_program_examples/npu.py:7-8)."""
+    return struct.unpack('<e', struct.pack('<e', float(x)))[0]
+
+
+# ----------------------------------------------------------------- helpers
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _need(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def _mat(t: torch.Tensor, name: str, dtype: torch.dtype) -> int:
+    """Validate a row-major CUDA matrix and return its leading dimension."""
+    _need(isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor")
+    _need(t.is_cuda, f"{name} must be a CUDA tensor")
+    _need(t.dtype == dtype, f"{name} must be {dtype}, got {t.dtype}")
+    _need(t.dim() == 2, f"{name} must be 2-D, got shape {tuple(t.shape)}")
+    _need(t.stride(1) == 1 or t.shape[1] == 1, f"{name} must have unit stride along its last dim")
+    return max(t.stride(0), t.shape[1]) if t.shape[0] <= 1 else t.stride(0)
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _workspace(nbytes: int, device) -> Tuple[Optional[torch.Tensor], int]:
+    if nbytes <= 0:
+        return None, 0
+    ws = torch.empty(nbytes + 256, dtype=torch.uint8, device=device)
+    off = (-ws.data_ptr()) % 256
+    return ws[off:off + nbytes], nbytes
+
+
+# -------------------------------------------------------------- W8A16 matmul
+
+def quantize_w8(W: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Symmetric per-output-channel int8 quantisation of W [K, N] fp32 (x @ W).
+
+    Returns (Wq int8 [N, K] K-major, scale fp16 [N]) with
+    scale[n] = fp16(max_k |W[k, n]| / 127) and Wq[n, k] = clip(rint(W[k, n] / scale[n]), +-127).
+    """
+    ldw = _mat(W, "W", torch.float32)
+    K, N = W.shape
+    q = torch.empty((N, K), dtype=torch.int8, device=W.device)
+    s = torch.empty((N,), dtype=torch.float16, device=W.device)
+    _lib.call("npub_quantize_w8", W.data_ptr(), ldw, K, N, q.data_ptr(), K, s.data_ptr(), _stream())
+    return q, s
+
+
+def matmul(A: torch.Tensor, W: torch.Tensor, scale: Optional[torch.Tensor] = None, *,
+           out: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
+           alpha: float = 1.0) -> torch.Tensor:
+    """C[M, N] = fp16(alpha * scale[n] * sum_k A[m, k] W[n, k]) (+ residual[m, n]).
+
+    The reference's matmul (npu.py:41-47) computes C = A @ B with B [K, N]; here
+    the weight is packed K-major as W [N, K] -- int8 (W8A16, from quantize_w8)
+    or fp16 (W = B.T.contiguous()).  A is fp16 [M, K]; K must be a multiple of 16.
+    """
+    lda = _mat(A, "A", torch.float16)
+    _need(W.dtype in (torch.int8, torch.float16), "W must be int8 or float16")
+    ldw = _mat(W, "W", W.dtype)
+    M, K = A.shape
+    N, K2 = W.shape
+    _need(K == K2, f"K mismatch: A {tuple(A.shape)} vs W {tuple(W.shape)}")
+    if scale is not None:
+        _need(scale.is_cuda and scale.dtype == torch.float16 and scale.numel() == N and scale.is_contiguous(),
+              "scale must be a contiguous fp16 CUDA tensor of N elements")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float16, device=A.device)
+    ldc = _mat(out, "out", torch.float16)
+    _need(tuple(out.shape) == (M, N), "out must be [M, N]")
+    ldr = 0
+    if residual is not None:
+        ldr = _mat(residual, "residual", torch.float16)
+        _need(tuple(residual.shape) == (M, N), "residual must be [M, N]")
+    int8 = W.dtype == torch.int8
+    wsq = "npub_w8a16_gemm_workspace" if int8 else "npub_f16_gemm_workspace"
+    ws, wsb = _workspace(_lib.query(wsq, M, N, K), A.device)
+    fn = "npub_w8a16_gemm" if int8 else "npub_f16_gemm"
+    _lib.call(fn, A.data_ptr(), lda, W.data_ptr(), ldw, _ptr(scale), out.data_ptr(), ldc, _ptr(residual), ldr,
+              M, N, K, float(alpha), _ptr(ws), wsb, _stream())
+    return out
+
+
+# ---------------------------------------------------------------- vector ops
+
+def rmsnorm(x: torch.Tensor, gamma: torch.Tensor, eps: float = 1e-5, *, residual: Optional[torch.Tensor] = None,
+            residual_out: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None):
+    """y = fp16(x / sqrt(mean(x^2) + eps) * gamma) per row (legalize.py:30-47).
+
+    With `residual`, h = fp16(x + residual) is formed first (llama_layer.py:139),
+    written to `residual_out` (default: a new tensor) and normalised; returns (y, h).
+    """
+    ldx = _mat(x, "x", torch.float16)
+    rows, d = x.shape
+    _need(gamma.is_cuda and gamma.dtype == torch.float16 and gamma.numel() == d and gamma.is_contiguous(),
+          "gamma must be a contiguous fp16 CUDA tensor of d elements")
+    if out is None:
+        out = torch.empty((rows, d), dtype=torch.float16, device=x.device)
+    ldy = _mat(out, "out", torch.float16)
+    ldr = ldxo = 0
+    if residual is not None:
+        ldr = _mat(residual, "residual", torch.float16)
+        _need(tuple(residual.shape) == (rows, d), "residual must match x")
+        if residual_out is None:
+            residual_out = torch.empty((rows, d), dtype=torch.float16, device=x.device)
+        ldxo = _mat(residual_out, "residual_out", torch.float16)
+    _lib.call("npub_rmsnorm", x.data_ptr(), ldx, _ptr(residual), ldr, _ptr(residual_out), ldxo, gamma.data_ptr(),
+              out.data_ptr(), ldy, rows, d, float(eps), _stream())
+    return out if residual is None else (out, residual_out)
+
+
+def swiglu(g: torch.Tensor, u: Optional[torch.Tensor] = None, *, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """h = fp16(g / (1 + exp(-g)) * u) (legalize.py:130-149).  With u=None, g is
+    [rows, 2F] holding the gate in its first F columns and up in the last F."""
+    if u is None:
+        _need(g.dim() == 2 and g.shape[1] % 2 == 0, "g must be [rows, 2F] when u is None")
+        F = g.shape[1] // 2
+        g, u = g[:, :F], g[:, F:]
+    ldg = _mat(g, "g", torch.float16)
+    ldu = _mat(u, "u", torch.float16)
+    _need(g.shape == u.shape, "g and u must have the same shape")
+    rows, cols = g.shape
+    if out is None:
+        out = torch.empty((rows, cols), dtype=torch.float16, device=g.device)
+    ldh = _mat(out, "out", torch.float16)
+    _lib.call("npub_swiglu", g.data_ptr(), ldg, u.data_ptr(), ldu, out.data_ptr(), ldh, rows, cols, _stream())
+    return out
+
+
+def softmax(s: torch.Tensor, *, causal: bool = False, scale: float = 1.0, causal_offset: int = 0,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Row softmax of scale*s over the last dim (legalize.py:97-114); causal rows
+    r see columns c <= r + causal_offset and get exact zeros elsewhere."""
+    _need(s.is_cuda and s.dtype == torch.float16 and s.dim() >= 2 and s.is_contiguous(),
+          "s must be a contiguous fp16 CUDA tensor with >= 2 dims")
+    rows, cols = s.shape[-2], s.shape[-1]
+    batch = s.numel() // max(1, rows * cols)
+    _need(cols % 8 == 0, "the row length must be a multiple of 8")
+    if out is None:
+        out = torch.empty_like(s)
+    _need(out.shape == s.shape and out.is_contiguous() and out.dtype == torch.float16, "bad out")
+    _lib.call("npub_softmax_rows", s.data_ptr(), out.data_ptr(), cols, rows * cols, batch, rows, cols, float(scale),
+              int(causal_offset) if causal else _lib.NPUB_NO_CAUSAL, 1, _stream())
+    return out
+
+
+def rope(x: torch.Tensor, heads: int, head_dim: int, *, pos0: int = 0, positions: Optional[torch.Tensor] = None,
+         theta: float = 10000.0) -> torch.Tensor:
+    """In-place RoPE on the first heads*head_dim columns of x [tokens, >=heads*head_dim]
+    (rotate_half convention, llama_layer.py:33-40,96-112).  Returns x."""
+    ldx = _mat(x, "x", torch.float16)
+    tokens = x.shape[0]
+    _need(x.shape[1] >= heads * head_dim, "x is narrower than heads*head_dim")
+    pos_ptr = None
+    if positions is not None:
+        _need(positions.is_cuda and positions.dtype == torch.int32 and positions.numel() == tokens
+              and positions.is_contiguous(), "positions must be contiguous int32 CUDA [tokens]")
+        pos_ptr = positions.data_ptr()
+    _lib.call("npub_rope", x.data_ptr(), ldx, tokens, heads, head_dim, pos_ptr, int(pos0), float(theta), _stream())
+    return x
+
+
+# ----------------------------------------------------------------- attention
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, kv_heads: Optional[int] = None, *,
+              head_dim: Optional[int] = None, batch: int = 1, causal: bool = True, scale: Optional[float] = None,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Causal (GQA) attention of llama_layer.py:114-137 for `batch` sequences of
+    equal length stacked along rows: q [batch*T, heads*hd], k/v [batch*T, kv_heads*hd]."""
+    kv_heads = kv_heads or heads
+    ldq = _mat(q, "q", torch.float16)
+    ldk = _mat(k, "k", torch.float16)
+    ldv = _mat(v, "v", torch.float16)
+    hd = head_dim or q.shape[1] // heads
+    rows = q.shape[0]
+    _need(rows % batch == 0, "rows must be a multiple of batch")
+    T = rows // batch
+    if scale is None:
+        scale = 1.0 / math.sqrt(hd)
+    if out is None:
+        out = torch.empty((rows, heads * hd), dtype=torch.float16, device=q.device)
+    ldo = _mat(out, "out", torch.float16)
+    ws, wsb = _workspace(_lib.query("npub_attention_workspace", batch, T, heads, hd), q.device)
+    _lib.call("npub_attention_prefill", q.data_ptr(), ldq, k.data_ptr(), ldk, v.data_ptr(), ldv, out.data_ptr(), ldo,
+              batch, T, heads, kv_heads, hd, float(scale), 1 if causal else 0, _ptr(ws), wsb, _stream())
+    return out
+
+
+def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *, heads: int,
+                     kv_heads: Optional[int] = None, lens: Optional[torch.Tensor] = None, ctx_len: int = 0,
+                     scale: Optional[float] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One query token per sequence against fp16 caches [batch, kv_heads, cap, 128]."""
+    kv_heads = kv_heads or heads
+    ldq = _mat(q, "q", torch.float16)
+    batch = q.shape[0]
+    _need(k_cache.dim() == 4 and k_cache.shape == v_cache.shape and k_cache.is_contiguous() and
+          v_cache.is_contiguous() and k_cache.dtype == torch.float16, "caches must be contiguous fp16 [B, KVH, cap, hd]")
+    B, KVH, cap, hd = k_cache.shape
+    _need(B == batch and KVH == kv_heads, "cache shape does not match q / kv_heads")
+    lens_ptr = None
+    if lens is not None:
+        _need(lens.is_cuda and lens.dtype == torch.int32 and lens.numel() == batch and lens.is_contiguous(),
+              "lens must be contiguous int32 CUDA [batch]")
+        lens_ptr = lens.data_ptr()
+        ctx = int(ctx_len) if ctx_len else cap
+    else:
+        ctx = int(ctx_len)
+    if scale is None:
+        scale = 1.0 / math.sqrt(hd)
+    if out is None:
+        out = torch.empty((batch, heads * hd), dtype=torch.float16, device=q.device)
+    ldo = _mat(out, "out", torch.float16)
+    ws, wsb = _workspace(_lib.query("npub_attention_decode_workspace", batch, heads, ctx, hd), q.device)
+    _lib.call("npub_attention_decode", q.data_ptr(), ldq, k_cache.data_ptr(), v_cache.data_ptr(), cap, lens_ptr, ctx,
+              out.data_ptr(), ldo, batch, heads, kv_heads, hd, float(scale), _ptr(ws), wsb, _stream())
+    return out
+
+
+def kv_append(k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *,
+              pos: Optional[torch.Tensor] = None, pos0: int = 0) -> None:
+    """cache[b, h, pos[b], :] = new[b, h*hd:(h+1)*hd] for K and V."""
+    ldk = _mat(k_new, "k_new", torch.float16)
+    ldv = _mat(v_new, "v_new", torch.float16)
+    B, KVH, cap, hd = k_cache.shape
+    pos_ptr = None
+    if pos is not None:
+        _need(pos.is_cuda and pos.dtype == torch.int32 and pos.numel() == B and pos.is_contiguous(),
+              "pos must be contiguous int32 CUDA [batch]")
+        pos_ptr = pos.data_ptr()
+    _lib.call("npub_kv_append", k_new.data_ptr(), ldk, v_new.data_ptr(), ldv, k_cache.data_ptr(), v_cache.data_ptr(),
+              cap, pos_ptr, int(pos0), B, KVH, hd, _stream())
+
+
+# --------------------------------------------------------- NPU ISA semantics
+
+def isa_vector(word: int, in1: torch.Tensor, in2: Optional[torch.Tensor] = None,
+               prev_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Execute one elementwise NPU compute instruction (_poc/mysim.cpp:114-141)
+    over fp32 PE buffers; returns the PE output buffer (fp32)."""
+    for t, nm in ((in1, "in1"), (in2, "in2"), (prev_out, "prev_out")):
+        if t is not None:
+            _need(t.is_cuda and t.dtype == torch.float32 and t.is_contiguous(), f"{nm} must be contiguous fp32 CUDA")
+    n = in1.numel()
+    out = torch.empty(n, dtype=torch.float32, device=in1.device)
+    _lib.call("npub_isa_vector", int(word) & 0xFFFFFFFF, in1.data_ptr(), _ptr(in2), _ptr(prev_out), out.data_ptr(), n,
+              _stream())
+    return out
+
+
+def f32_to_f16_bits(x: torch.Tensor) -> torch.Tensor:
+    """The cmodel's store rounding (mysim.cpp:19-38): fp32 -> fp16 bit patterns (int16)."""
+    _need(x.is_cuda and x.dtype == torch.float32 and x.is_contiguous(), "x must be contiguous fp32 CUDA")
+    y = torch.empty(x.shape, dtype=torch.int16, device=x.device)
+    _lib.call("npub_f32_to_f16", x.data_ptr(), y.data_ptr(), x.numel(), _stream())
+    return y
+
+
+def f16_bits_to_f32(x: torch.Tensor) -> torch.Tensor:
+    _need(x.is_cuda and x.dtype in (torch.int16, torch.float16) and x.is_contiguous(), "x must be 16-bit CUDA")
+    y = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    _lib.call("npub_f16_to_f32", x.data_ptr(), y.data_ptr(), x.numel(), _stream())
+    return y
