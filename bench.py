@@ -1,0 +1,414 @@
+"""Benchmark of the W8A16 / Llama-layer hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload layer|decode|gemm]
+
+Default workload ("layer"): one Llama-7B-shaped decoder layer, prefill of one
+2048-token prompt (d 4096, 32 heads x 128, FFN 11008, RoPE theta 10000,
+causal attention), all seven linears W8A16 (int8 weights ~N(0, 0.02)
+quantised per output channel, fp16 activations ~N(0, 1), seeded).  A step is
+one pass of the layer; the metric is prefill tokens/s.  With --gpus N (under
+torchrun) the layer runs tensor-parallel over N GPUs with NCCL all-reduces
+(total work fixed: strong scaling).
+
+Rank 0 prints one JSON line.  `roofline` covers the dominant kernel, the
+tcgen05 W8A16 GEMM, timed live with CUDA events on its launch stream.
+`cpu_baseline` is the reference cmodel (mysim, built from the reference's
+_poc/mysim.cpp) or its C restatement, run on a bounded sample of the same
+workload's GEMMs on this host's cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+METRIC = "W8A16 GEMM TFLOP/s + Llama-layer tokens/s, % of roofline, 1/2/4/8 B200 vs mysim"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def _peaks():
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), \
+            "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def _traffic(key):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    try:
+        with open(os.path.join(HERE, "profiles", "traffic.json")) as f:
+            return json.load(f).get(key)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 6:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = max(mx, float(parts[1]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[2:6]):
+                if v.lower() in ("active", "1", "0x1"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- CPU baseline
+
+def _cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_reference_rate(seconds_target: float = 12.0, all_cores: bool = False):
+    """FLOP/s of the reference's CPU path on the W8A16 GEMM: the 64-tiled
+    program (d_compiler/npu_compiler/codegen.py:59-108) over dequantised
+    weights, executed by mysim (or the C restatement when mysim is absent).
+    Sample: 64 tokens x 512 output channels x K 4096 of the layer's QKV
+    projection.  With all_cores, one process per core runs concurrently."""
+    import numpy as np
+    sys.path.insert(0, HERE)
+    from oracle import cmodel, emit
+    M, N, K = 64, 512, 4096
+    rng = np.random.default_rng(0)
+    A = rng.standard_normal((M, K)).astype(np.float16)
+    W = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    s = (np.abs(W).max(axis=0) / np.float32(127)).astype(np.float16)
+    q = np.clip(np.rint(W / s.astype(np.float32)), -127, 127)
+    Wd = (q * s.astype(np.float32)).astype(np.float16)
+    words, gimg, c_addr, gn = emit.w8a16_program(A, Wd)
+    flops = 2.0 * M * N * K
+    nproc = _cpu_cores() if all_cores else 1
+    kind = "reference" if cmodel.have_mysim() else "port"
+    if kind == "reference":
+        import tempfile
+        d = tempfile.mkdtemp()
+        with open(os.path.join(d, "program_memory.bin"), "wb") as f:
+            f.write(np.asarray(words, dtype="<u4").tobytes() + b"\n")
+        with open(os.path.join(d, "G_buffer_data.bin"), "wb") as f:
+            f.write(np.asarray(gimg).astype("<f2").tobytes() + b"\n")
+        cmd = [cmodel.MYSIM, "--run", str(len(words) + 1)]
+        t0 = time.time()
+        procs = [subprocess.Popen(cmd, cwd=d, stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+                 for _ in range(nproc)]
+        for p in procs:
+            p.wait()
+        dt = time.time() - t0
+    else:
+        from concurrent.futures import ProcessPoolExecutor
+        import multiprocessing as mp
+        t0 = time.time()
+        with ProcessPoolExecutor(max_workers=nproc, mp_context=mp.get_context("spawn")) as ex:
+            list(ex.map(_run_port, [(words, gimg, gn)] * nproc))
+        dt = time.time() - t0
+    return flops * nproc / dt, nproc, kind, f"W8A16 {M}x{N}x{K} tiled program ({len(words)} instr) x {nproc} process(es)"
+
+
+def _run_port(args):
+    sys.path.insert(0, HERE)
+    from oracle import cmodel
+    words, gimg, gn = args
+    cmodel.run_oracle(words, gimg, gn, maxrun=len(words) + 1)
+    return 0
+
+
+# ---------------------------------------------------------------- our arm
+
+def setup_dist(n_gpus):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    if n_gpus > 1 or "RANK" in os.environ:
+        rank = int(os.environ.get("RANK", 0))
+        world = int(os.environ.get("WORLD_SIZE", 1))
+        local = int(os.environ.get("LOCAL_RANK", rank))
+        torch.cuda.set_device(local)
+        if world > 1:
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        return rank, world, local
+    torch.cuda.set_device(0)
+    return 0, 1, 0
+
+
+def run_ours(args):
+    import torch
+    sys.path.insert(0, HERE)
+    from npu_comp_b200 import llama, npu, _lib
+    rank, world, local = setup_dist(args.gpus)
+    dev = torch.device("cuda", local)
+    import torch.distributed as dist
+    group = dist.group.WORLD if world > 1 else None
+    tp = llama.TP(rank, world, group)
+    cfg = llama.LLAMA_7B
+    hbm, tf_burst, tf_sust, peak_src = _peaks()
+
+    wl = args.workload
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234)
+    if wl == "layer":
+        T = 2048
+        w = llama.make_layer(cfg, seed=0, device=dev, tp=tp)
+        x = torch.randn((T, cfg.d), generator=gen, device=dev).half()
+        sc = llama.Scratch()
+        y = torch.empty_like(x)
+        step = lambda: llama.layer_prefill(x, w, cfg, tp=tp, scratch=sc, out=y)  # noqa: E731
+        units = float(T)
+        unit = "tokens/s"
+        config = {"workload": "llama7b_layer_prefill_w8a16", "tokens": T, "batch": 1, "d": cfg.d,
+                  "heads": cfg.heads, "head_dim": cfg.head_dim, "ffn": cfg.ffn, "theta": cfg.theta,
+                  "parallelism": f"tp{world}", "l2": "inputs larger than L2 (202 MB int8 weights per step)"}
+        h_in, d_out = x, y
+    elif wl == "decode":
+        B, ctx = 64, 4096
+        w = llama.make_layer(cfg, seed=0, device=dev, tp=tp)
+        hk = cfg.kv_heads // world
+        kc = torch.randn((B, hk, ctx + 8, cfg.head_dim), generator=gen, device=dev).half()
+        vc = torch.randn((B, hk, ctx + 8, cfg.head_dim), generator=gen, device=dev).half()
+        x = torch.randn((B, cfg.d), generator=gen, device=dev).half()
+        pos = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+        sc = llama.Scratch()
+        y = torch.empty_like(x)
+        step = lambda: llama.layer_decode(x, w, cfg, kc, vc, pos, ctx_max=ctx + 1, tp=tp, scratch=sc,  # noqa: E731
+                                          out=y)
+        units = float(B)
+        unit = "tokens/s"
+        config = {"workload": "llama7b_layer_decode_w8a16", "batch": B, "kv_len": ctx, "parallelism": f"tp{world}",
+                  "l2": "inputs larger than L2 (4.3 GB KV cache per step)"}
+        h_in, d_out = x, y
+    else:  # gemm: the layer's gate|up projection alone
+        M, N, K = 2048, 2 * cfg.ffn // world, cfg.d
+        Wf = torch.randn((K, N), generator=gen, device=dev) * 0.02
+        q, s = npu.quantize_w8(Wf)
+        del Wf
+        A = torch.randn((M, K), generator=gen, device=dev).half()
+        C = torch.empty((M, N), dtype=torch.float16, device=dev)
+        step = lambda: npu.matmul(A, q, s, out=C)  # noqa: E731
+        units = 2.0 * M * N * K / 1e12
+        unit = "TFLOP/s"
+        config = {"workload": "w8a16_gemm", "M": M, "N": N, "K": K, "parallelism": f"replica{world}",
+                  "l2": "flushed: 256 MB buffer written between steps"}
+        h_in, d_out = A, C
+
+    flush = None
+    if wl == "gemm":
+        flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+        if flush is not None:
+            flush.fill_(1.0)
+    torch.cuda.synchronize()
+    barrier()
+
+    # ---- timed region (device time, CUDA events, max over ranks)
+    npu.gemm_events = []
+    launches0 = _lib.launch_count()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    try:
+        smi_id = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+    except Exception:
+        smi_id = local
+    with ClockSampler(smi_id) as clk:
+        torch.cuda.synchronize()
+        barrier()
+        for i in range(args.steps):
+            if flush is not None:
+                flush.fill_(1.0)
+            ev[i][0].record()
+            step()
+            ev[i][1].record()
+        torch.cuda.synchronize()
+        barrier()
+    launches = _lib.launch_count() - launches0
+    gev = npu.gemm_events
+    npu.gemm_events = None
+    step_ms = sum(a.elapsed_time(b) for a, b in ev)
+    t = torch.tensor([step_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms = float(t.item())
+    ms_per_step = step_ms / args.steps
+    per_rank_units = units  # TP: every rank processes the same tokens (strong scaling)
+    value = per_rank_units / (ms_per_step / 1e3) if wl != "gemm" else units * world / (ms_per_step / 1e3)
+
+    # dominant kernel roofline: W8A16 GEMM launches inside the timed steps
+    g_ms = sum(a.elapsed_time(b) for a, b, _, i8 in gev if i8)
+    g_flops = sum(f for _, _, f, i8 in gev if i8)
+    g_n = sum(1 for *_, i8 in gev if i8)
+    achieved = g_flops / (g_ms / 1e3) / 1e12 if g_ms > 0 else None
+    peak = tf_burst
+    roof = {"kernel": "gemm_tc_kernel<int8> (tcgen05 W8A16)", "bound": "tensor", "achieved": achieved, "peak": peak,
+            "unit": "TFLOP/s", "frac": (achieved / peak) if achieved else None,
+            "peak_source": f"{peak_src} bf16 dense (burst)", "launches": g_n,
+            "flops_per_launch": g_flops / g_n if g_n else None,
+            "avg_launch_us": g_ms * 1e3 / g_n if g_n else None,
+            "traffic": _traffic(wl), "share_of_step": (g_ms / step_ms) if step_ms else None}
+
+    # e2e: same step through the public API with host buffers, copies inside the timed region
+    h_host = torch.empty(h_in.shape, dtype=h_in.dtype, pin_memory=True)
+    h_host.copy_(h_in)
+    o_host = torch.empty(d_out.shape, dtype=d_out.dtype, pin_memory=True)
+    e2e_ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ev[0].record()
+    for i in range(args.steps):
+        if flush is not None:
+            flush.fill_(1.0)
+        h_in.copy_(h_host, non_blocking=True)
+        step()
+        o_host.copy_(d_out, non_blocking=True)
+    e2e_ev[1].record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e2e_ev[0].elapsed_time(e2e_ev[1])
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item()) / args.steps
+    e2e_val = units / (e2e_ms / 1e3) if wl != "gemm" else units * world / (e2e_ms / 1e3)
+
+    out = None
+    if rank == 0:
+        out = {"metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+               "scaling": "strong" if wl != "gemm" else "weak", "vs_baseline": None, "dtype": "int8 x fp16 -> fp32 acc",
+               "data": "synthetic (seeded; random-init weights)", "config": config,
+               "roofline": roof,
+               "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": h_in.numel() * h_in.element_size(),
+                       "d2h_bytes_per_step": d_out.numel() * d_out.element_size()},
+               "gpu_launches": int(launches), "clocks": clk.summary()}
+        if wl == "layer":
+            flops = llama.layer_flops(cfg, 2048, 2048)
+            out["layer_tflops"] = flops / (ms_per_step / 1e3) / 1e12
+            out["layer_tensor_frac"] = out["layer_tflops"] * world / peak
+        if wl == "decode":
+            by = llama.decode_bytes(cfg, 64, 4097)
+            out["hbm_gbs"] = by / world / (ms_per_step / 1e3) / 1e9
+            out["hbm_frac"] = out["hbm_gbs"] / hbm
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
+def _scale_rate(flop_rate, workload):
+    """CPU GEMM FLOP/s -> the workload's unit, through its FLOPs per unit."""
+    sys.path.insert(0, HERE)
+    from npu_comp_b200.llama import LLAMA_7B, layer_flops
+    if workload == "gemm":
+        return flop_rate / 1e12, "TFLOP/s"
+    if workload == "decode":
+        per_tok = layer_flops(LLAMA_7B, 1, 4097, causal=False)
+    else:
+        per_tok = layer_flops(LLAMA_7B, 2048, 2048) / 2048.0
+    return flop_rate / per_tok, "tokens/s"
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["layer", "decode", "gemm"], default="layer")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", args.gpus))
+
+    if args.impl == "reference":
+        # The reference's CPU path (mysim) on this host's cores; rank 0 only.
+        if rank != 0:
+            return 0
+        sys.path.insert(0, HERE)
+        rates = []
+        kind = sample = None
+        cores = 1
+        for i in range(max(1, min(args.steps, 3))):
+            r, cores, kind, sample = cpu_reference_rate(all_cores=True)
+            rates.append(r)
+        rate = statistics.median(rates)
+        value, unit = _scale_rate(rate, args.workload)
+        line = {"impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": world,
+                "steps": len(rates), "warmup": 0, "higher_is_better": True, "vs_baseline": None,
+                "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": kind,
+                                 "sample": sample + " ; GEMM FLOP rate scaled by the layer's FLOPs per token"},
+                "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                "config": {"workload": {"layer": "llama7b_layer_prefill_w8a16", "decode": "llama7b_layer_decode_w8a16",
+                                        "gemm": "w8a16_gemm"}[args.workload]}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    out = run_ours(args)
+    if rank == 0 and out is not None:
+        if not args.no_cpu_baseline and world == 1:
+            rate, cores, kind, sample = cpu_reference_rate(all_cores=False)
+            v, u = _scale_rate(rate, args.workload)
+            out["cpu_baseline"] = {"value": v, "unit": u, "cores": cores, "kind": kind,
+                                   "sample": sample + " ; GEMM FLOP rate scaled by the layer's FLOPs per token"}
+        print(json.dumps(out), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -53,6 +53,8 @@ int npub_version(void);
 const char* npub_strerror(int status);
 /* The cudaError_t of the last NPUB_ERR_CUDA on this thread (0 if none). */
 int npub_last_cuda_error(void);
+/* Number of kernels libnpub has launched in this process (all devices). */
+unsigned long long npub_launch_count(void);
 /* Reads (and with clear != 0 resets) the current device's error word, which
  * kernels set when a bounded wait gives up.  Synchronises the device.
  * Returns 0 when no kernel reported an error. */

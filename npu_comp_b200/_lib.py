@@ -33,6 +33,7 @@ SIGNATURES = {
     "npub_strerror": (ctypes.c_char_p, [_i]),
     "npub_last_cuda_error": (_i, []),
     "npub_device_error": (_i, [_i]),
+    "npub_launch_count": (ctypes.c_ulonglong, []),
     "npub_w8a16_gemm": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _p, _i64, _i, _i, _i, _f, _p, _sz, _p]),
     "npub_w8a16_gemm_workspace": (_sz, [_i, _i, _i]),
     "npub_f16_gemm": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _p, _i64, _i, _i, _i, _f, _p, _sz, _p]),
@@ -94,6 +95,11 @@ def call(name: str, *args) -> None:
         if st == NPUB_ERR_INVALID_ARG:
             raise ValueError(f"{name}: {text}")
         raise NpubError(name, st, text)
+
+
+def launch_count() -> int:
+    """Kernels launched by libnpub so far in this process."""
+    return int(load().npub_launch_count())
 
 
 def query(name: str, *args) -> int:

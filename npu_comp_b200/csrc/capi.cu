@@ -2,14 +2,18 @@
 // the per-device error word that kernels set when a bounded wait gives up.
 #include "common.cuh"
 
+#include <atomic>
+
 // One int per device context (module globals are instantiated per device).
 __device__ int g_npub_device_error;
 
 static thread_local int t_last_cuda_error = 0;
+static std::atomic<unsigned long long> g_launches{0};
 
 void npub_internal_set_cuda_error(cudaError_t e) { t_last_cuda_error = (int)e; }
 
 int npub_internal_launch_status() {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         t_last_cuda_error = (int)e;
@@ -43,6 +47,8 @@ extern "C" const char* npub_strerror(int status) {
 }
 
 extern "C" int npub_last_cuda_error(void) { return t_last_cuda_error; }
+
+extern "C" unsigned long long npub_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 extern "C" int npub_device_error(int clear) {
     cudaError_t e = cudaDeviceSynchronize();

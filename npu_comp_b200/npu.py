@@ -69,6 +69,13 @@ def _workspace(nbytes: int, device) -> Tuple[Optional[torch.Tensor], int]:
 
 # -------------------------------------------------------------- W8A16 matmul
 
+# When a list, every matmul() call appends (start_event, end_event, flops, int8)
+# recorded on the launching stream -- used by bench.py to time the GEMM kernels
+# inside a step.
+gemm_events = None
+
+
+
 def quantize_w8(W: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     """Symmetric per-output-channel int8 quantisation of W [K, N] fp32 (x @ W).
 
@@ -113,8 +120,15 @@ def matmul(A: torch.Tensor, W: torch.Tensor, scale: Optional[torch.Tensor] = Non
     wsq = "npub_w8a16_gemm_workspace" if int8 else "npub_f16_gemm_workspace"
     ws, wsb = _workspace(_lib.query(wsq, M, N, K), A.device)
     fn = "npub_w8a16_gemm" if int8 else "npub_f16_gemm"
+    ev = gemm_events
+    if ev is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
     _lib.call(fn, A.data_ptr(), lda, W.data_ptr(), ldw, _ptr(scale), out.data_ptr(), ldc, _ptr(residual), ldr,
               M, N, K, float(alpha), _ptr(ws), wsb, _stream())
+    if ev is not None:
+        e1.record()
+        ev.append((e0, e1, 2.0 * M * N * K, int8))
     return out
 
 
