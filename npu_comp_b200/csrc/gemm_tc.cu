@@ -22,6 +22,7 @@
 //               epilogue (warp 4+i reads TMEM lanes 32i..32i+31)
 #include "common.cuh"
 #include "gemm_tc.h"
+#include "gemm_w8a16_pair.h"
 
 #include <cudaTypedefs.h>
 
@@ -412,13 +413,55 @@ int run_gemm(GemmParams& p, bool a_int8, int bt, int grid_x, int grid_y, int bat
 
 // Shared host path of npub_w8a16_gemm / npub_f16_gemm:
 // Aop = weights [N, K] (128-row side), Bop = activations [M, K] (token side).
-static size_t linear_workspace(int M, int N, int K) {
+static size_t linear_workspace(int M, int N, int K, bool w_int8) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
+    if (w_int8) return w8a16_pair_workspace(M, N, K);
     const int bt = pick_bt(M);
     const int tiles = ((N + BM - 1) / BM) * ((M + bt - 1) / bt);
     const int k_tiles = (K + BK - 1) / BK;
     const int s = pick_splits(tiles, k_tiles);
     return s > 1 ? (size_t)s * M * N * sizeof(float) : 0;
+}
+
+// W8A16 on 2-CTA pairs: weights are the 256-row MMA side, tokens the BT side.
+static int linear_w8a16_pair(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C,
+                             int64_t ldc, const void* R, int64_t ldr, int M, int N, int K, float alpha, void* ws,
+                             size_t ws_bytes, cudaStream_t st) {
+    PairParams p;
+    memset(&p, 0, sizeof(p));
+    const int bt = pair_bt(M);
+    int rc = make_tmap_3d(&p.tmW, true, W, (uint64_t)K, (uint64_t)N, 1, (uint64_t)ldw, (uint64_t)ldw * N, 128, 1,
+                          false);
+    if (rc) return rc;
+    rc = make_tmap_3d(&p.tmX, false, A, (uint64_t)K, (uint64_t)M, 1, (uint64_t)lda, (uint64_t)lda * M,
+                      (uint32_t)(bt / 2), 1, true);
+    if (rc) return rc;
+    const int splits = w8a16_pair_splits(M, N, K);
+    p.alpha = alpha;
+    if (splits > 1) {
+        const size_t need = (size_t)splits * M * N * sizeof(float);
+        if (!ws || ws_bytes < need) return NPUB_ERR_WORKSPACE;
+        if (!npub_aligned(ws, 16)) return NPUB_ERR_INVALID_ARG;
+        p.out_f32 = 1;
+        p.part = reinterpret_cast<float*>(ws);
+    } else {
+        p.C = reinterpret_cast<__half*>(C);
+        p.ldc = ldc;
+        p.R = reinterpret_cast<const __half*>(R);
+        p.ldr = ldr;
+        p.scale = reinterpret_cast<const __half*>(scale);
+    }
+    rc = w8a16_pair_run(p, M, N, K, st);
+    if (rc || p.splits == 1) return rc;
+    const int64_t total = (int64_t)M * N;
+    int blocks = (int)((total + 255) / 256);
+    const int cap = num_sms() * 8;
+    if (blocks > cap) blocks = cap;
+    splitk_reduce_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<const float*>(ws), p.splits, M, N,
+                                                 reinterpret_cast<const __half*>(scale), alpha,
+                                                 reinterpret_cast<const __half*>(R), ldr, reinterpret_cast<__half*>(C),
+                                                 ldc);
+    return npub_internal_launch_status();
 }
 
 static int linear(bool w_int8, const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C,
@@ -434,6 +477,7 @@ static int linear(bool w_int8, const void* A, int64_t lda, const void* W, int64_
     NPUB_CHECK_ARG(ldc >= N);
     NPUB_CHECK_ARG(!R || ldr >= N);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (w_int8) return linear_w8a16_pair(A, lda, W, ldw, scale, C, ldc, R, ldr, M, N, K, alpha, ws, ws_bytes, st);
 
     GemmParams p;
     memset(&p, 0, sizeof(p));
@@ -496,7 +540,7 @@ extern "C" int npub_w8a16_gemm(const void* A, int64_t lda, const int8_t* Wq, int
                         stream);
 }
 
-extern "C" size_t npub_w8a16_gemm_workspace(int M, int N, int K) { return npub::linear_workspace(M, N, K); }
+extern "C" size_t npub_w8a16_gemm_workspace(int M, int N, int K) { return npub::linear_workspace(M, N, K, true); }
 
 extern "C" int npub_f16_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C,
                              int64_t ldc, const void* R, int64_t ldr, int M, int N, int K, float alpha, void* workspace,
@@ -505,4 +549,4 @@ extern "C" int npub_f16_gemm(const void* A, int64_t lda, const void* W, int64_t 
                         stream);
 }
 
-extern "C" size_t npub_f16_gemm_workspace(int M, int N, int K) { return npub::linear_workspace(M, N, K); }
+extern "C" size_t npub_f16_gemm_workspace(int M, int N, int K) { return npub::linear_workspace(M, N, K, false); }

@@ -1,0 +1,204 @@
+"""Regenerate the golden fixtures of tests/golden/ from the reference tree.
+
+Run in a container where the reference (KwanyoungCho/NPU_COMP) is mounted:
+
+    python tests/golden/make_goldens.py [--ref /root/reference]
+
+It never copies reference sources into this repository.  It compiles and runs
+the reference's own generators and simulator (outputs under oracle/_ref/ and a
+temporary directory) and records only their outputs:
+
+  isa_goldens.json   for each of the 55 ISA example programs under
+                     b_program/inst_*/: the program words produced by its
+                     w_support_program_mem_gen.cpp, the line count and sha256
+                     of the golden trace _poc/goldens/<name>.txt (captured from
+                     the original cmodel binary on the ramp G-buffer made by
+                     c_hex_data/w_support_binary_data_gen.cpp).  The script
+                     also asserts that our C restatement (oracle/isa_oracle.c)
+                     and the reference simulator reproduce every trace.
+  examples.npz       inputs and outputs of the reference's example scripts
+                     b_program_examples/test_{matmul,rmsnorm,swiglu,attention}.py
+                     and llama_layer.py, run as-is (on a copy, with mysim
+                     built from _poc/mysim.cpp): the G-buffer results of the
+                     NPU programs and the scripts' own python references.
+  w8a16_config1.npz  the single W8A16 matmul configuration (A [64,512] ~N(0,1),
+                     W [512,512] ~N(0,0.02), numpy default_rng(0)) run through
+                     the compiler-style 64-tiled program on the reference
+                     simulator: C as fp16, with sha256 of the inputs.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import os
+import runpy
+import shutil
+import subprocess
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+from oracle import cmodel, emit, ref  # noqa: E402
+
+
+def _gxx(src, out):
+    os.makedirs(os.path.dirname(out), exist_ok=True)
+    if not os.path.exists(out) or os.path.getmtime(src) > os.path.getmtime(out):
+        subprocess.run(["g++", "-O2", "-std=c++17", src, "-o", out], check=True)
+    return out
+
+
+def ramp_gbuffer(refdir):
+    exe = _gxx(os.path.join(refdir, "c_hex_data", "w_support_binary_data_gen.cpp"),
+               os.path.join(ROOT, "oracle", "_ref", "gen", "gbuf_ramp"))
+    with tempfile.TemporaryDirectory() as d:
+        subprocess.run([exe], cwd=d, check=True, stdout=subprocess.DEVNULL)
+        raw = open(os.path.join(d, "G_buffer_data.bin"), "rb").read()
+    return raw
+
+
+def isa_goldens(refdir):
+    gbuf_raw = ramp_gbuffer(refdir)
+    gbuf = np.frombuffer(gbuf_raw[: (len(gbuf_raw) // 2) * 2], dtype="<f2")
+    assert len(gbuf_raw) == 16385 and np.array_equal(gbuf.astype(np.float32), np.arange(8192, dtype=np.float16)
+                                                     .astype(np.float32)), "ramp G-buffer mismatch"
+    out = []
+    gold_dir = os.path.join(refdir, "_poc", "goldens")
+    for fn in sorted(os.listdir(gold_dir)):
+        name = fn[:-4]
+        src = os.path.join(refdir, "b_program", name, "w_support_program_mem_gen.cpp")
+        exe = _gxx(src, os.path.join(ROOT, "oracle", "_ref", "gen", name))
+        with tempfile.TemporaryDirectory() as d:
+            subprocess.run([exe], cwd=d, check=True, stdout=subprocess.DEVNULL)
+            praw = open(os.path.join(d, "program_memory.bin"), "rb").read()
+        assert len(praw) == 1025, (name, len(praw))
+        words = np.frombuffer(praw[:1024], dtype="<u4")
+        text = open(os.path.join(gold_dir, fn)).read()
+        # our restatement; like _poc/verify_all.sh, the trace of the default
+        # 30-instruction run is compared with the same number of golden lines
+        m = cmodel.Machine(gbuf.astype(np.float16), gcap=1 << 16)
+        _, trace = m.execute(words, 30, trace=True, gbytes=16385, pbytes=1025)
+        mine = trace
+        lines = text.splitlines(keepends=True)[: len(trace.splitlines())]
+        golden = "".join(lines)
+        assert mine == golden, f"C restatement differs from golden {name}"
+        # the reference simulator rebuilt from source
+        if cmodel.have_mysim():
+            with tempfile.TemporaryDirectory() as d:
+                open(os.path.join(d, "program_memory.bin"), "wb").write(praw)
+                open(os.path.join(d, "G_buffer_data.bin"), "wb").write(gbuf_raw)
+                r = subprocess.run([cmodel.MYSIM], cwd=d, capture_output=True, text=True, check=True)
+            sim = r.stdout
+            assert sim == golden, f"mysim differs from golden {name}"
+        nz = int(np.max(np.nonzero(words)[0])) + 1 if words.any() else 0
+        out.append({"name": name, "words": [int(w) for w in words[:nz]], "nwords": int(words.size),
+                    "lines": len(lines), "sha256": hashlib.sha256(golden.encode()).hexdigest()})
+    return out
+
+
+def run_script(refdir, script, workdir):
+    """Run a reference example script as-is in a copy of its directory; return its globals."""
+    sdir = os.path.join(refdir, "b_program_examples")
+    for f in ("npu.py", script):
+        shutil.copy(os.path.join(sdir, f), workdir)
+    shutil.copy(cmodel.MYSIM, os.path.join(workdir, "mysim"))
+    cwd = os.getcwd()
+    sys.path.insert(0, workdir)
+    try:
+        os.chdir(workdir)
+        for mod in ("npu",):
+            sys.modules.pop(mod, None)
+        import io
+        import contextlib
+        buf = io.StringIO()
+        with contextlib.redirect_stdout(buf):
+            g = runpy.run_path(os.path.join(workdir, script), run_name="__main__")
+        g["__stdout__"] = buf.getvalue()
+        return g
+    finally:
+        os.chdir(cwd)
+        sys.path.remove(workdir)
+
+
+def examples(refdir):
+    res = {}
+    with tempfile.TemporaryDirectory() as d:
+        g = run_script(refdir, "test_matmul.py", d)
+        res["matmul_A"] = np.array(g["A"], np.float32)
+        res["matmul_B"] = np.array(g["B"], np.float32)
+        res["matmul_npu"] = np.array(g["got"], np.float32).reshape(g["M"], g["N"])
+        res["matmul_ref"] = np.array(g["exp"], np.float32).reshape(g["M"], g["N"])
+    with tempfile.TemporaryDirectory() as d:
+        g = run_script(refdir, "test_rmsnorm.py", d)
+        res["rmsnorm_X"] = np.array(g["X"], np.float32)
+        res["rmsnorm_W"] = np.array(g["W"], np.float32)
+        res["rmsnorm_npu"] = np.array(g["got"], np.float32)
+        res["rmsnorm_ref"] = np.array(g["exp"], np.float32)
+    with tempfile.TemporaryDirectory() as d:
+        g = run_script(refdir, "test_swiglu.py", d)
+        for k in ("X", "Wg", "Wu", "Wd"):
+            res[f"swiglu_{k}"] = np.array(g[k], np.float32)
+        res["swiglu_npu"] = np.array(g["got"], np.float32).reshape(g["SEQ"], g["D"])
+        res["swiglu_ref"] = np.array(g["Outr"], np.float32).reshape(g["SEQ"], g["D"])
+    with tempfile.TemporaryDirectory() as d:
+        g = run_script(refdir, "test_attention.py", d)
+        for k in ("X", "Wq", "Wk", "Wv", "Wo"):
+            res[f"attention_{k}"] = np.array(g[k], np.float32)
+        res["attention_npu"] = np.array(g["got"], np.float32).reshape(g["SEQ"], g["D"])
+        res["attention_ref"] = np.array(g["Outr"], np.float32).reshape(g["SEQ"], g["D"])
+    with tempfile.TemporaryDirectory() as d:
+        g = run_script(refdir, "llama_layer.py", d)
+        H, KV = g["H"], g["KV"]
+        res["layer_X"] = np.array(g["X"], np.float32)
+        res["layer_Wn1"] = np.array(g["Wn1"], np.float32)
+        res["layer_Wn2"] = np.array(g["Wn2"], np.float32)
+        res["layer_Wq"] = np.array(g["Wq"], np.float32)      # [H, D, HD]
+        res["layer_Wk"] = np.array(g["Wk"], np.float32)      # [KV, D, HD]
+        res["layer_Wv"] = np.array(g["Wv"], np.float32)
+        res["layer_Wo"] = np.array(g["Wo"], np.float32)      # [H, HD, D]
+        res["layer_Wg"] = np.array(g["Wg"], np.float32)
+        res["layer_Wu"] = np.array(g["Wu"], np.float32)
+        res["layer_Wd"] = np.array(g["Wd"], np.float32)
+        res["layer_cos"] = np.array(g["COS"], np.float32)
+        res["layer_sin"] = np.array(g["SIN"], np.float32)
+        res["layer_npu"] = np.array(g["got"], np.float32).reshape(g["SEQ"], g["D"])
+        res["layer_ref"] = np.array(g["exp"], np.float32).reshape(g["SEQ"], g["D"])
+        res["layer_dims"] = np.array([g["SEQ"], g["D"], H, KV, g["HD"], g["F"]], np.int64)
+    return res
+
+
+def config1():
+    rng = np.random.default_rng(0)
+    A = rng.standard_normal((64, 512)).astype(np.float16)
+    W = (rng.standard_normal((512, 512)) * 0.02).astype(np.float32)
+    q, s = ref.quantize_w8(W)
+    words, gimg, ca, gn = emit.w8a16_program(A, ref.dequant_f16(q, s))
+    C = cmodel.run_mysim(words, gimg, gn, maxrun=len(words) + 1)[ca: ca + 64 * 512].reshape(64, 512)
+    return {"C_mysim": C.astype(np.float16), "instructions": np.int64(len(words)),
+            "sha_A": hashlib.sha256(A.tobytes()).hexdigest(), "sha_W": hashlib.sha256(W.tobytes()).hexdigest()}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    a = ap.parse_args()
+    subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={a.ref}"], check=True)
+    gold = isa_goldens(a.ref)
+    with open(os.path.join(HERE, "isa_goldens.json"), "w") as f:
+        json.dump({"gbuf": "ramp G[i] = fp16(i), i < 8192 (c_hex_data/w_support_binary_data_gen.cpp)",
+                   "maxrun": 30, "gbytes": 16385, "pbytes": 1025, "programs": gold}, f, indent=0)
+    np.savez_compressed(os.path.join(HERE, "examples.npz"), **examples(a.ref))
+    c1 = config1()
+    np.savez_compressed(os.path.join(HERE, "w8a16_config1.npz"), C_mysim=c1["C_mysim"],
+                        instructions=c1["instructions"], sha_A=np.array(c1["sha_A"]), sha_W=np.array(c1["sha_W"]))
+    print(f"wrote {len(gold)} ISA goldens, examples.npz, w8a16_config1.npz")
+
+
+if __name__ == "__main__":
+    main()
