@@ -100,46 +100,51 @@ def _shard_rows(q: torch.Tensor, s: torch.Tensor, blocks: List[range]) -> (torch
     return q.index_select(0, idx).contiguous(), s.index_select(0, idx).contiguous()
 
 
+def tp_ranges(cfg: LlamaConfig, rank: int, size: int) -> Dict[str, List[range]]:
+    """This rank's slices of the layer's linears under tensor parallelism.
+
+    qkv / gu: output-channel (row) ranges of the fused column-parallel weights
+    [q heads | k heads | v heads] and [gate | up]; o / d: input (K) ranges of
+    the row-parallel O and down projections."""
+    if cfg.heads % size or cfg.kv_heads % size or cfg.ffn % size:
+        raise ValueError(f"tp={size} must divide heads {cfg.heads}, kv_heads {cfg.kv_heads} and ffn {cfg.ffn}")
+    hq, hk, f, hd = cfg.heads // size, cfg.kv_heads // size, cfg.ffn // size, cfg.head_dim
+    qd, kd = cfg.q_dim, cfg.kv_dim
+    r = rank
+    return {
+        "qkv": [range(r * hq * hd, (r + 1) * hq * hd), range(qd + r * hk * hd, qd + (r + 1) * hk * hd),
+                range(qd + kd + r * hk * hd, qd + kd + (r + 1) * hk * hd)],
+        "o": [range(r * hq * hd, (r + 1) * hq * hd)],
+        "gu": [range(r * f, (r + 1) * f), range(cfg.ffn + r * f, cfg.ffn + (r + 1) * f)],
+        "d": [range(r * f, (r + 1) * f)],
+    }
+
+
 def quantize_linear(W: torch.Tensor):
     """fp32 [K, N] -> (int8 [N, K], fp16 [N]) with the libnpub quantiser."""
     return npu.quantize_w8(W.contiguous())
 
 
-def make_layer(cfg: LlamaConfig, seed: int, device, tp: TP = TP(), std: float = 0.02,
-               keep_fp32: bool = False) -> LayerWeights:
+def make_layer(cfg: LlamaConfig, seed: int, device, tp: TP = TP(), std: float = 0.02) -> LayerWeights:
     """Random-init layer (weights ~N(0, std), RMSNorm gains 1), quantised per
     output channel over the full matrix, then sliced to this rank's shard."""
-    r, n = tp.rank, tp.size
-    assert cfg.heads % n == 0 and cfg.kv_heads % n == 0 and cfg.ffn % n == 0, "tp must divide heads and ffn"
-    hq, hk, f = cfg.heads // n, cfg.kv_heads // n, cfg.ffn // n
-    hd, d = cfg.head_dim, cfg.d
+    rg = tp_ranges(cfg, tp.rank, tp.size)
+    hq, hk, f = cfg.heads // tp.size, cfg.kv_heads // tp.size, cfg.ffn // tp.size
+    d = cfg.d
     gen = torch.Generator(device=device)
     gen.manual_seed(int(seed))
 
     def rnd(k, m):
         return torch.randn((k, m), generator=gen, device=device, dtype=torch.float32) * std
 
-    # QKV (column parallel)
-    Wqkv = rnd(d, cfg.q_dim + 2 * cfg.kv_dim)
-    q, s = quantize_linear(Wqkv)
-    qd, kd = cfg.q_dim, cfg.kv_dim
-    wqkv, sqkv = _shard_rows(q, s, [range(r * hq * hd, (r + 1) * hq * hd),
-                                    range(qd + r * hk * hd, qd + (r + 1) * hk * hd),
-                                    range(qd + kd + r * hk * hd, qd + kd + (r + 1) * hk * hd)])
-    del Wqkv, q, s
-    # O (row parallel): K slice of [d, q_dim]
-    q, s = quantize_linear(rnd(cfg.q_dim, d))
-    wo = q[:, r * hq * hd:(r + 1) * hq * hd].contiguous()
-    so = s
-    del q
-    # gate | up (column parallel)
-    q, s = quantize_linear(rnd(d, 2 * cfg.ffn))
-    wgu, sgu = _shard_rows(q, s, [range(r * f, (r + 1) * f), range(cfg.ffn + r * f, cfg.ffn + (r + 1) * f)])
-    del q, s
-    # down (row parallel)
-    q, s = quantize_linear(rnd(cfg.ffn, d))
-    wd = q[:, r * f:(r + 1) * f].contiguous()
-    sd = s
+    q, s = quantize_linear(rnd(d, cfg.q_dim + 2 * cfg.kv_dim))          # QKV, column parallel
+    wqkv, sqkv = _shard_rows(q, s, rg["qkv"])
+    q, so = quantize_linear(rnd(cfg.q_dim, d))                           # O, row parallel
+    wo = q[:, rg["o"][0].start:rg["o"][0].stop].contiguous()
+    q, s = quantize_linear(rnd(d, 2 * cfg.ffn))                          # gate | up, column parallel
+    wgu, sgu = _shard_rows(q, s, rg["gu"])
+    q, sd = quantize_linear(rnd(cfg.ffn, d))                             # down, row parallel
+    wd = q[:, rg["d"][0].start:rg["d"][0].stop].contiguous()
     del q
     ones = torch.ones(d, dtype=torch.float16, device=device)
     return LayerWeights(wqkv, sqkv, wo, so, wgu, sgu, wd, sd, ones, ones.clone(), hq, hk, f)

@@ -54,6 +54,7 @@ def lib() -> ctypes.CDLL:
         L.ora_gsize.argtypes = [P]
         L.ora_gread.argtypes = [P, P, I64]
         L.ora_f32_to_f16_array.argtypes = [P, P, I64]
+        L.ora_vector.argtypes = [ctypes.c_uint32, P, P, P, P, I64]
         _lib = L
     return _lib
 
@@ -64,6 +65,17 @@ def f32_to_f16_bits(x) -> np.ndarray:
     y = np.empty(x.shape, dtype=np.uint16)
     lib().ora_f32_to_f16_array(x.ctypes.data, y.ctypes.data, x.size)
     return y
+
+
+def vector_op(word: int, in1, in2=None, prev=None) -> np.ndarray:
+    """fp32 result of one elementwise compute instruction (mysim.cpp:114-141)."""
+    a = np.ascontiguousarray(np.asarray(in1, dtype=np.float32))
+    b = None if in2 is None else np.ascontiguousarray(np.asarray(in2, dtype=np.float32))
+    p = None if prev is None else np.ascontiguousarray(np.asarray(prev, dtype=np.float32))
+    out = np.empty_like(a)
+    lib().ora_vector(int(word) & 0xFFFFFFFF, a.ctypes.data, None if b is None else b.ctypes.data,
+                     None if p is None else p.ctypes.data, out.ctypes.data, a.size)
+    return out
 
 
 def fp16_round(x) -> np.ndarray:

@@ -187,6 +187,65 @@ static float operand_b(ora_state* st, int mode, int cst, long i) {
     return (float)cst;
 }
 
+/* Whether an opcode reads its second operand (sqrt, exp and convert do not). */
+static int reads_b(uint32_t op) { return !(op == 0x0Eu || op == 0x0Fu || op == 0x13u); }
+
+/* One element of a compute instruction (mysim.cpp:117-140): a from PE input
+ * 1, b the second operand (PE input 2 in vector mode, else the immediate),
+ * prev the previous PE output (read by mul-add). */
+static float elem_op(uint32_t w, float a, float b, float prev) {
+    uint32_t op = w & 0xFFu;
+    int mode = (int)((w >> 30) & 3u), actf = (int)((w >> 29) & 1u);
+    int matrix = op >= 0x40u && op <= 0x43u;
+    int cst = (int)((w >> 8) & 0xFFFFu);
+    float r = a;
+    switch (op) {
+        case 0x01: case 0x40: r = a + b; break;
+        case 0x02: case 0x41: r = a - b; break;
+        case 0x0A: case 0x42: r = a * b; break;
+        case 0x0B: r = a / b; break;
+        case 0x0C: { float p = a * b; r = prev + p; } break;
+        case 0x0D: case 0x43: r = b; break;
+        case 0x0E: r = sqrtf(a); break;
+        case 0x0F: r = expf(a); break;
+        case 0x11: r = (a == b) ? 1.0f : 0.0f; break;
+        case 0x12: r = ((w >> 28) & 1u) ? (a > b ? a : b) : (a < b ? a : b); break;
+        case 0x13: r = (float)to_i64(a); break;
+        case 0x09: {
+            int16_t s = (int16_t)cst;
+            if (mode == 2) s = (int16_t)to_i32(b);
+            r = a * ldexpf(1.0f, (int)s);
+        } break;
+        case 0x08: {
+            int64_t ia = to_i64(a), ib = to_i64(b);
+            switch ((w >> 27) & 7u) {
+                case 0: r = (float)(ia & ib); break;
+                case 1: r = (float)(ia | ib); break;
+                case 2: r = (float)(~ia); break;
+                case 3: r = (float)(ia ^ ib); break;
+                case 4: r = (float)(~(ia & ib)); break;
+                case 5: r = (float)(~(ia | ib)); break;
+                default: break;
+            }
+        } break;
+        default: break;
+    }
+    if (actf && matrix) r = hw_act(r);
+    return r;
+}
+
+/* Elementwise semantics of one compute instruction over fp32 PE buffers
+ * (in2 is read in vector mode only, prev by mul-add); the checker for the
+ * GPU's npub_isa_vector. */
+void ora_vector(uint32_t w, const float* in1, const float* in2, const float* prev, float* out, long n) {
+    int mode = (int)((w >> 30) & 3u);
+    int cst = (int)((w >> 8) & 0xFFFFu);
+    for (long i = 0; i < n; i++) {
+        float b = mode == 2 ? in2[i] : (float)cst;
+        out[i] = elem_op(w, in1[i], b, prev ? prev[i] : 0.0f);
+    }
+}
+
 /*
  * Execute up to `maxrun` instructions of `prog` (nprog words).  When `trace`
  * is non-zero the reference's stdout trace is reproduced; `gbytes`/`pbytes`
@@ -261,44 +320,10 @@ long ora_exec(void* h, const uint32_t* prog, long nprog, long maxrun, int trace,
                     memset(st->out.v, 0, (size_t)n * sizeof(float));
                 }
                 if (st->in1.n < n) { st->error = 1; return -1; }
+                const int rb = reads_b(op);
                 for (long i = 0; i < n; i++) {
-                    float a = st->in1.v[i], r = a, b;
-                    switch (op) {
-                        case 0x01: case 0x40: r = a + operand_b(st, mode, cst, i); break;
-                        case 0x02: case 0x41: r = a - operand_b(st, mode, cst, i); break;
-                        case 0x0A: case 0x42: r = a * operand_b(st, mode, cst, i); break;
-                        case 0x0B: r = a / operand_b(st, mode, cst, i); break;
-                        case 0x0C: { float p = a * operand_b(st, mode, cst, i); r = st->out.v[i] + p; } break;
-                        case 0x0D: case 0x43: r = operand_b(st, mode, cst, i); break;
-                        case 0x0E: r = sqrtf(a); break;
-                        case 0x0F: r = expf(a); break;
-                        case 0x11: r = (a == operand_b(st, mode, cst, i)) ? 1.0f : 0.0f; break;
-                        case 0x12:
-                            b = operand_b(st, mode, cst, i);
-                            r = ((w >> 28) & 1u) ? (a > b ? a : b) : (a < b ? a : b);
-                            break;
-                        case 0x13: r = (float)to_i64(a); break;
-                        case 0x09: {
-                            int16_t s = (int16_t)cst;
-                            if (mode == 2) s = (int16_t)to_i32(operand_b(st, mode, cst, i));
-                            r = a * ldexpf(1.0f, (int)s);
-                        } break;
-                        case 0x08: {
-                            int64_t ia = to_i64(a), ib = to_i64(operand_b(st, mode, cst, i));
-                            switch ((w >> 27) & 7u) {
-                                case 0: r = (float)(ia & ib); break;
-                                case 1: r = (float)(ia | ib); break;
-                                case 2: r = (float)(~ia); break;
-                                case 3: r = (float)(ia ^ ib); break;
-                                case 4: r = (float)(~(ia & ib)); break;
-                                case 5: r = (float)(~(ia | ib)); break;
-                                default: break;
-                            }
-                        } break;
-                        default: break;
-                    }
-                    if (actf && matrix) r = hw_act(r);
-                    st->out.v[i] = r;
+                    float b = rb ? operand_b(st, mode, cst, i) : 0.0f;
+                    st->out.v[i] = elem_op(w, st->in1.v[i], b, st->out.v[i]);
                 }
                 if (st->error) return -1;
             }

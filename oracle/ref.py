@@ -22,8 +22,13 @@ import numpy as np
 
 
 def f16(x) -> np.ndarray:
-    """Round through fp16 (RNE) and back to float32 -- the cmodel's save."""
-    return np.asarray(x, dtype=np.float32).astype(np.float16).astype(np.float32)
+    """Round through fp16 (RNE) and back to float32 -- the cmodel's save, or
+    npu.fp16() of a python double (float64 input is rounded directly, with no
+    intermediate float32 rounding)."""
+    x = np.asarray(x)
+    if x.dtype != np.float64:
+        x = x.astype(np.float32)
+    return x.astype(np.float16).astype(np.float32)
 
 
 # ------------------------------------------------------------------ W8A16
@@ -57,8 +62,14 @@ def w8a16_ref(A: np.ndarray, q: np.ndarray, s: np.ndarray, residual: Optional[np
 
 
 def matmul_f16_ref(A: np.ndarray, B: np.ndarray) -> np.ndarray:
-    """One-shot NPU matmul: fp16(sum_k f32 A * f32 B) (test_matmul.py:22, mysim.cpp:109-113)."""
+    """One-shot NPU matmul: fp16(sum_k f32 A * f32 B) (mysim.cpp:109-113)."""
     return f16(A.astype(np.float32) @ B.astype(np.float32))
+
+
+def matmul_f16_pyref(A: np.ndarray, B: np.ndarray) -> np.ndarray:
+    """The example scripts' reference matmul: fp16 of a double-precision sum
+    (test_matmul.py:22, test_swiglu.py:40, test_attention.py:58)."""
+    return f16(A.astype(np.float64) @ B.astype(np.float64))
 
 
 def tiled_fp16_ref(A: np.ndarray, B: np.ndarray, T: int = 64) -> np.ndarray:
@@ -110,11 +121,12 @@ def silu_mul_ref(g: np.ndarray, u: np.ndarray) -> np.ndarray:
 
 
 def swiglu_npu_ref(G: np.ndarray, U: np.ndarray) -> np.ndarray:
-    """Per-save fp16 SiLU*up of test_swiglu.py:43-46."""
-    G = G.astype(np.float32)
+    """Per-save fp16 SiLU*up of test_swiglu.py:43-46 (python doubles between saves)."""
+    G = G.astype(np.float64)
     with np.errstate(over="ignore"):
-        sig = f16(1.0 / f16(1.0 + f16(np.exp(-G.astype(np.float64)))))
-    return f16(f16(G * sig) * U.astype(np.float32))
+        sig = f16(1.0 / f16(1.0 + f16(np.exp(-G))).astype(np.float64)).astype(np.float64)
+    silu = f16(G * sig).astype(np.float64)
+    return f16(silu * U.astype(np.float64))
 
 
 def softmax_ref(s: np.ndarray, scale: float = 1.0, causal: bool = False, offset: int = 0) -> np.ndarray:

@@ -1,0 +1,67 @@
+"""The C ABI library (CPU): it loads, exports every entry point declared in
+include/npub.h, and rejects invalid arguments with NPUB_ERR_INVALID_ARG before
+touching a device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from npu_comp_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared():
+    src = open(os.path.join(ROOT, "include", "npub.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(npub_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_the_bound_entry_points():
+    names = declared()
+    assert len(names) >= 20
+    assert set(names) == set(_lib.SIGNATURES), set(names) ^ set(_lib.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol(libnpub_path):
+    lib = ctypes.CDLL(libnpub_path)
+    missing = [n for n in declared() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_status_strings_and_version(libnpub_path):
+    lib = _lib.load()
+    assert lib.npub_version() >= 10000
+    for st in (0, -1, -2, -3, -4, -5, -6):
+        assert lib.npub_strerror(st)
+    assert lib.npub_strerror(-1).decode().startswith("invalid argument")
+
+
+def test_invalid_arguments_rejected_before_any_device_work(libnpub_path):
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    # K not a multiple of 16
+    assert lib.npub_w8a16_gemm(p, 24, p, 32, None, p, 8, None, 0, 4, 8, 24, 1.0, None, 0, None) == -1
+    # lda < K
+    assert lib.npub_w8a16_gemm(p, 8, p, 32, None, p, 8, None, 0, 4, 8, 16, 1.0, None, 0, None) == -1
+    # misaligned activation pointer
+    assert lib.npub_f16_gemm(ctypes.c_void_p(18), 16, p, 16, None, p, 8, None, 0, 4, 8, 16, 1.0, None, 0,
+                             None) == -1
+    # d not a multiple of 8
+    assert lib.npub_rmsnorm(p, 12, None, 0, None, 0, p, p, 12, 2, 12, 1e-5, None) == -1
+    # heads not divisible by kv_heads
+    assert lib.npub_attention_prefill(p, 384, p, 256, p, 256, p, 384, 1, 8, 3, 2, 128, 0.1, 1, p, 1 << 30,
+                                      None) == -1
+    # unsupported head_dim for decode
+    assert lib.npub_attention_decode(p, 64, p, p, 16, None, 8, p, 64, 1, 1, 1, 64, 0.1, None, 0, None) == -2
+    # matrix multiply is not an elementwise instruction
+    assert lib.npub_isa_vector((2 << 30) | 0x42, p, p, None, p, 4, None) == -2
+    # zero-sized work is a no-op
+    assert lib.npub_swiglu(None, 0, None, 0, None, 0, 0, 0, None) == 0
+
+
+def test_python_wrappers_fail_loudly_without_the_library(monkeypatch, tmp_path):
+    monkeypatch.setattr(_lib, "_lib", None)
+    with pytest.raises(ImportError):
+        _lib.load(str(tmp_path / "missing.so"))

@@ -1,0 +1,91 @@
+"""Attention on the GPU against the oracle: causal GQA prefill (tcgen05 GEMMs +
+softmax), decode over a KV cache, and the KV-cache append.
+Tolerance: normwise relative error <= 1e-2 (TOL)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import npu_comp_b200 as nb
+from oracle import ref
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+
+
+def dev(a, d):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(d)
+
+
+@pytest.mark.parametrize("B,T,H,KV,hd,causal", [(1, 256, 2, 2, 128, True), (2, 200, 4, 2, 64, True),
+                                                 (1, 8, 4, 2, 16, True), (1, 130, 2, 1, 128, False),
+                                                 (3, 77, 2, 2, 32, True)])
+def test_prefill_attention(cuda_device, rng, B, T, H, KV, hd, causal):
+    q = rng.standard_normal((B * T, H * hd)).astype(np.float16)
+    k = rng.standard_normal((B * T, KV * hd)).astype(np.float16)
+    v = rng.standard_normal((B * T, KV * hd)).astype(np.float16)
+    o = nb.attention(dev(q, cuda_device), dev(k, cuda_device), dev(v, cuda_device), H, KV, head_dim=hd,
+                     batch=B, causal=causal).float().cpu().numpy()
+    for b in range(B):
+        sl = slice(b * T, (b + 1) * T)
+        exp = ref.attention_ref(q[sl], k[sl], v[sl], H, KV, hd, causal)
+        assert ref.rel_err(o[sl], exp) <= TOL
+
+
+def test_prefill_attention_full_size(cuda_device):
+    """32 heads x 2048 tokens x 128: sampled heads against the float64 oracle."""
+    g = torch.Generator(device=cuda_device).manual_seed(11)
+    T, H, hd = 2048, 32, 128
+    qkv = torch.randn((T, 3 * H * hd), generator=g, device=cuda_device).half()
+    q, k, v = qkv[:, :H * hd], qkv[:, H * hd:2 * H * hd], qkv[:, 2 * H * hd:]
+    o = nb.attention(q, k, v, H, H).float().cpu().numpy()
+    qn, kn, vn = (t.cpu().numpy() for t in (q, k, v))
+    for h in (0, 17, 31):
+        sl = slice(h * hd, (h + 1) * hd)
+        exp = ref.attention_ref(qn[:, sl], kn[:, sl], vn[:, sl], 1, 1, hd, True)
+        assert ref.rel_err(o[:, sl], exp) <= TOL
+
+
+def test_attention_reference_example(cuda_device, examples):
+    """The reference's single-head causal attention example (test_attention.py)."""
+    X, Wq, Wk, Wv, Wo = (examples[f"attention_{k}"].astype(np.float16) for k in ("X", "Wq", "Wk", "Wv", "Wo"))
+    x = dev(X, cuda_device)
+    q = nb.matmul(x, dev(Wq.T, cuda_device))
+    k = nb.matmul(x, dev(Wk.T, cuda_device))
+    v = nb.matmul(x, dev(Wv.T, cuda_device))
+    ctx = nb.attention(q, k, v, 1, 1, head_dim=Wq.shape[1])
+    out = nb.matmul(ctx, dev(Wo.T, cuda_device)).float().cpu().numpy()
+    assert np.abs(out - examples["attention_npu"]).max() < 2e-2  # test_attention.py:75
+    assert ref.rel_err(out, examples["attention_ref"]) <= TOL
+
+
+@pytest.mark.parametrize("B,H,KV,ctx,cap", [(4, 8, 4, 300, 320), (2, 4, 4, 4096, 4100), (3, 2, 1, 1, 8)])
+def test_decode_attention(cuda_device, rng, B, H, KV, ctx, cap):
+    hd = 128
+    q = rng.standard_normal((B, H * hd)).astype(np.float16)
+    kc = rng.standard_normal((B, KV, cap, hd)).astype(np.float16)
+    vc = rng.standard_normal((B, KV, cap, hd)).astype(np.float16)
+    lens = rng.integers(1, ctx + 1, B).astype(np.int32)
+    o = nb.attention_decode(dev(q, cuda_device), dev(kc, cuda_device), dev(vc, cuda_device), heads=H, kv_heads=KV,
+                            lens=dev(lens, cuda_device), ctx_len=ctx).float().cpu().numpy()
+    assert ref.rel_err(o, ref.decode_attention_ref(q, kc, vc, lens, H, KV, hd)) <= TOL
+
+
+def test_decode_matches_last_prefill_row(cuda_device, rng):
+    """Decode of token T over a cache of T keys == row T of causal prefill over T+1 tokens."""
+    T, H, hd = 97, 4, 128
+    q = rng.standard_normal((T + 1, H * hd)).astype(np.float16)
+    k = rng.standard_normal((T + 1, H * hd)).astype(np.float16)
+    v = rng.standard_normal((T + 1, H * hd)).astype(np.float16)
+    full = nb.attention(dev(q, cuda_device), dev(k, cuda_device), dev(v, cuda_device), H, H).float()
+    kc = torch.zeros((1, H, 128, hd), dtype=torch.float16, device=cuda_device)
+    vc = torch.zeros_like(kc)
+    for t in range(T + 1):
+        nb.kv_append(dev(k[t:t + 1], cuda_device), dev(v[t:t + 1], cuda_device), kc, vc, pos0=t)
+    kv_ref = k.reshape(T + 1, H, hd).transpose(1, 0, 2)
+    assert np.array_equal(kc[0, :, :T + 1].cpu().numpy(), kv_ref)
+    lens = torch.tensor([T + 1], dtype=torch.int32, device=cuda_device)
+    o = nb.attention_decode(dev(q[T:T + 1], cuda_device), kc, vc, heads=H, lens=lens, ctx_len=T + 1).float()
+    e = ((o[0] - full[T]).abs().max() / full[T].abs().max()).item()
+    assert e <= TOL

@@ -1,0 +1,103 @@
+"""RMSNorm, SwiGLU, softmax and RoPE kernels against the oracle (GPU).
+Tolerance: normwise relative error <= 1e-2 (TOL) unless stated."""
+import numpy as np
+import pytest
+import torch
+
+import npu_comp_b200 as nb
+from oracle import ref
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+
+
+def dev(a, d):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(d)
+
+
+@pytest.mark.parametrize("rows,d", [(2048, 4096), (7, 64), (1, 8), (33, 11008)])
+def test_rmsnorm(cuda_device, rng, rows, d):
+    x = rng.standard_normal((rows, d)).astype(np.float16)
+    g = (1 + 0.02 * rng.standard_normal(d)).astype(np.float16)
+    y = nb.rmsnorm(dev(x, cuda_device), dev(g, cuda_device), 1e-5).float().cpu().numpy()
+    assert ref.rel_err(y, ref.rmsnorm_ref(x, g, 1e-5)) <= TOL
+
+
+def test_rmsnorm_fused_residual(cuda_device, rng):
+    x = rng.standard_normal((64, 256)).astype(np.float16)
+    r = rng.standard_normal((64, 256)).astype(np.float16)
+    g = np.ones(256, np.float16)
+    y, h = nb.rmsnorm(dev(x, cuda_device), dev(g, cuda_device), 1e-5, residual=dev(r, cuda_device))
+    hs = (x.astype(np.float32) + r.astype(np.float32)).astype(np.float16)
+    assert np.array_equal(h.cpu().numpy(), hs)  # fp16 round of an exact fp32 sum
+    assert ref.rel_err(y.float().cpu().numpy(), ref.rmsnorm_ref(hs, g, 1e-5)) <= TOL
+
+
+def test_rmsnorm_reference_example(cuda_device, examples):
+    """The reference's RMSNorm example (test_rmsnorm.py, eps 0) within its own tolerance."""
+    X, W = examples["rmsnorm_X"], examples["rmsnorm_W"]
+    y = nb.rmsnorm(dev(X.astype(np.float16), cuda_device), dev(W.astype(np.float16), cuda_device), 0.0)
+    got = y.float().cpu().numpy()
+    assert np.abs(got - examples["rmsnorm_npu"]).max() < 1e-2  # test_rmsnorm.py:57
+    assert np.abs(got - examples["rmsnorm_ref"]).max() < 1e-2
+
+
+@pytest.mark.parametrize("rows,cols", [(2048, 11008), (3, 13), (8, 128)])
+def test_swiglu(cuda_device, rng, rows, cols):
+    gu = rng.standard_normal((rows, 2 * cols)).astype(np.float16)
+    h = nb.swiglu(dev(gu, cuda_device)).float().cpu().numpy()
+    assert ref.rel_err(h, ref.silu_mul_ref(gu[:, :cols], gu[:, cols:])) <= TOL
+
+
+def test_swiglu_ffn_reference_example(cuda_device, examples):
+    """The reference's SwiGLU FFN example (test_swiglu.py) built from our fp16 matmul and swiglu."""
+    X, Wg, Wu, Wd = (examples[f"swiglu_{k}"].astype(np.float16) for k in ("X", "Wg", "Wu", "Wd"))
+    x = dev(X, cuda_device)
+    g = nb.matmul(x, dev(Wg.T, cuda_device))
+    u = nb.matmul(x, dev(Wu.T, cuda_device))
+    h = nb.swiglu(g, u)
+    out = nb.matmul(h, dev(Wd.T, cuda_device)).float().cpu().numpy()
+    assert ref.rel_err(out, examples["swiglu_npu"]) <= TOL
+    assert ref.rel_err(out, examples["swiglu_ref"]) <= TOL
+
+
+@pytest.mark.parametrize("causal,offset", [(False, 0), (True, 0), (True, 5)])
+def test_softmax(cuda_device, rng, causal, offset):
+    s = rng.standard_normal((3, 136, 256)).astype(np.float16)
+    p = nb.softmax(dev(s, cuda_device), causal=causal, scale=0.7, causal_offset=offset).float().cpu().numpy()
+    exp = ref.softmax_ref(s, 0.7, causal, offset)
+    assert ref.rel_err(p, exp) <= TOL
+    if causal:
+        mask = np.arange(256)[None, :] > np.arange(136)[:, None] + offset
+        assert np.all(p[:, mask] == 0.0)  # masked entries are exact zeros (exp(-30000) in the reference)
+
+
+def test_softmax_prefill_shape(cuda_device):
+    g = torch.Generator(device=cuda_device).manual_seed(3)
+    s = torch.randn((32, 2048, 2048), generator=g, device=cuda_device).half()
+    p = nb.softmax(s, causal=True)
+    sub = s[5, 1000:1010].float().cpu().numpy()
+    ref_rows = ref.softmax_ref(sub, 1.0, True, offset=1000)
+    assert ref.rel_err(p[5, 1000:1010].float().cpu().numpy(), ref_rows) <= TOL
+    rows = p.float().sum(-1)
+    assert torch.allclose(rows, torch.ones_like(rows), atol=2e-2)
+
+
+@pytest.mark.parametrize("T,H,hd,pos0", [(64, 4, 128, 0), (8, 4, 16, 3), (5, 2, 64, 4096)])
+def test_rope(cuda_device, rng, T, H, hd, pos0):
+    x = rng.standard_normal((T, H * hd + 16)).astype(np.float16)
+    xt = dev(x, cuda_device)
+    nb.rope(xt, H, hd, pos0=pos0)
+    got = xt.float().cpu().numpy()
+    exp = ref.rope_ref(x[:, :H * hd], H, hd, np.arange(T) + pos0)
+    assert ref.rel_err(got[:, :H * hd], exp) <= TOL
+    assert np.array_equal(got[:, H * hd:], x[:, H * hd:].astype(np.float32))  # columns past the heads untouched
+
+
+def test_rope_positions_tensor(cuda_device, rng):
+    T, H, hd = 6, 2, 32
+    pos = np.array([0, 7, 3, 4095, 1, 2], np.int32)
+    x = rng.standard_normal((T, H * hd)).astype(np.float16)
+    xt = dev(x, cuda_device)
+    nb.rope(xt, H, hd, positions=dev(pos, cuda_device))
+    assert ref.rel_err(xt.float().cpu().numpy(), ref.rope_ref(x, H, hd, pos)) <= TOL

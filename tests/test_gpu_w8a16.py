@@ -1,0 +1,136 @@
+"""W8A16 matmul on the GPU (tcgen05 2-CTA pairs) against the oracle.
+
+Tolerance (floating point, fp16 output): normwise relative error
+max|got - ref| / max|ref| <= 1e-2 (TOL); integer quantisation is bit-exact.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import npu_comp_b200 as nb
+from oracle import ref
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def to_dev(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def test_config1_against_reference_simulator(cuda_device):
+    """The single W8A16 matmul configuration vs the reference's CPU path (mysim
+    running the compiler's 64-tiled program on dequantised weights)."""
+    rng = np.random.default_rng(0)
+    A = rng.standard_normal((64, 512)).astype(np.float16)
+    W = (rng.standard_normal((512, 512)) * 0.02).astype(np.float32)
+    q, s = ref.quantize_w8(W)
+    qd, sd = nb.quantize_w8(to_dev(W, cuda_device))
+    assert np.array_equal(qd.cpu().numpy(), q) and np.array_equal(sd.cpu().numpy(), s)
+    C = nb.matmul(to_dev(A, cuda_device), qd, sd).float().cpu().numpy()
+    C_mysim = np.load(os.path.join(GOLDEN, "w8a16_config1.npz"))["C_mysim"].astype(np.float32)
+    exact = ref.w8a16_ref(A, q, s)
+    assert ref.rel_err(C, C_mysim) <= TOL
+    assert ref.rel_err(C, exact) <= TOL
+    # the GPU keeps fp32 accumulation to the end: closer to exact than the fp16 tiled program
+    assert ref.rel_err(C, exact) <= ref.rel_err(C_mysim, exact)
+    assert np.abs(C - exact).mean() < 2e-3
+
+
+@pytest.mark.parametrize("K,N", [(512, 512), (4096, 300), (1, 33), (64, 7)])
+def test_quantizer_bit_exact(cuda_device, rng, K, N):
+    W = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    W[:, 0] = 0.0  # a zero column
+    q, s = ref.quantize_w8(W)
+    qd, sd = nb.quantize_w8(to_dev(W, cuda_device))
+    assert np.array_equal(qd.cpu().numpy(), q)
+    assert np.array_equal(sd.cpu().numpy().view(np.uint16), s.view(np.uint16))
+
+
+SHAPES = [(64, 512, 512), (1, 1000, 256), (8, 64, 64), (128, 128, 64), (200, 300, 160), (129, 257, 96),
+          (333, 777, 1024), (64, 12288, 4096), (64, 4096, 1376), (512, 256, 11008), (2048, 4096, 4096)]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_w8a16_shapes(cuda_device, rng, M, N, K):
+    A = rng.standard_normal((M, K)).astype(np.float16)
+    W = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    q, s = ref.quantize_w8(W)
+    C = nb.matmul(to_dev(A, cuda_device), to_dev(q, cuda_device), to_dev(s, cuda_device)).float().cpu().numpy()
+    assert C.shape == (M, N)
+    assert ref.rel_err(C, ref.w8a16_ref(A, q, s)) <= TOL
+
+
+def test_w8a16_residual_alpha_and_strided_output(cuda_device, rng):
+    M, N, K = 300, 500, 128
+    A = rng.standard_normal((M, K)).astype(np.float16)
+    q = rng.integers(-127, 128, (N, K)).astype(np.int8)
+    s = (rng.uniform(0.5, 2, N) * 1e-3).astype(np.float16)
+    R = rng.standard_normal((M, N)).astype(np.float16)
+    out = torch.zeros((M, N + 24), dtype=torch.float16, device=cuda_device)[:, 8:8 + N]
+    nb.matmul(to_dev(A, cuda_device), to_dev(q, cuda_device), to_dev(s, cuda_device), out=out,
+              residual=to_dev(R, cuda_device), alpha=0.5)
+    got = out.float().cpu().numpy()
+    assert ref.rel_err(got, ref.w8a16_ref(A, q, s, residual=R, alpha=0.5)) <= TOL
+
+
+def test_w8a16_exact_known_answer(cuda_device, rng):
+    """Small integers and power-of-two scales: every intermediate is exact, so the
+    fp16 result must equal the exact value bit for bit."""
+    M, N, K = 96, 384, 256
+    A = rng.integers(-3, 4, (M, K)).astype(np.float16)
+    q = rng.integers(-4, 5, (N, K)).astype(np.int8)
+    q[0, :] = 127
+    q[1, :] = -127
+    s = (2.0 ** rng.integers(-10, -4, N)).astype(np.float16)
+    C = nb.matmul(to_dev(A, cuda_device), to_dev(q, cuda_device), to_dev(s, cuda_device)).cpu().numpy()
+    exact = ref.w8a16_ref(A, q, s)
+    assert np.array_equal(C, exact.astype(np.float16))
+
+
+def test_w8a16_split_k_deterministic(cuda_device, rng):
+    M, N, K = 64, 4096, 4096  # decode shape: split-K partials + reduction
+    A = to_dev(rng.standard_normal((M, K)).astype(np.float16), cuda_device)
+    q = to_dev(rng.integers(-127, 128, (N, K)).astype(np.int8), cuda_device)
+    s = to_dev((np.ones(N) * 1e-3).astype(np.float16), cuda_device)
+    c1 = nb.matmul(A, q, s)
+    c2 = nb.matmul(A, q, s)
+    assert torch.equal(c1, c2)
+
+
+def test_w8a16_full_size_against_torch_fp32(cuda_device):
+    """Gate|up projection of the Llama-7B layer at prefill size vs a torch fp32
+    reference of the same op on the dequantised weights."""
+    g = torch.Generator(device=cuda_device).manual_seed(7)
+    M, N, K = 2048, 22016, 4096
+    W = torch.randn((K, N), generator=g, device=cuda_device) * 0.02
+    q, s = nb.quantize_w8(W)
+    del W
+    A = torch.randn((M, K), generator=g, device=cuda_device).half()
+    C = nb.matmul(A, q, s).float()
+    ref32 = (A.float() @ q.float().t()) * s.float()[None, :]
+    e = ((C - ref32).abs().max() / ref32.abs().max()).item()
+    assert e <= TOL
+    assert torch.isfinite(C).all()
+
+
+def test_f16_matmul_against_npu_matmul(cuda_device, examples):
+    """fp16 weights: the reference's own matmul example (test_matmul.py, 8x64 @ 64x64)."""
+    A, B = examples["matmul_A"], examples["matmul_B"]
+    C = nb.matmul(to_dev(A.astype(np.float16), cuda_device), to_dev(B.T.astype(np.float16), cuda_device))
+    got = C.float().cpu().numpy()
+    assert ref.rel_err(got, examples["matmul_npu"]) <= TOL
+    # fp16 store of an fp32 accumulation: nearly every element is byte-identical
+    assert np.mean(got == examples["matmul_npu"]) > 0.95
+
+
+def test_invalid_shapes_raise(cuda_device):
+    A = torch.zeros((4, 24), dtype=torch.float16, device=cuda_device)
+    q = torch.zeros((8, 24), dtype=torch.int8, device=cuda_device)
+    with pytest.raises(ValueError):
+        nb.matmul(A, q)  # K = 24 is not a multiple of 16
+    with pytest.raises(ValueError):
+        nb.matmul(A, torch.zeros((8, 16), dtype=torch.int8, device=cuda_device))  # K mismatch
