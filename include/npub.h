@@ -46,6 +46,7 @@ extern "C" {
 #define NPUB_ERR_WORKSPACE (-4)      /* workspace missing or smaller than *_workspace() */
 #define NPUB_ERR_DEVICE_TIMEOUT (-5) /* a bounded device-side wait gave up (npub_device_error) */
 #define NPUB_ERR_NO_DEVICE (-6)      /* no sm_100 device current */
+#define NPUB_ERR_SCRATCH_LIMIT (-7)  /* request needs more than the static scratch of npub_w8a16_gemm_noalloc */
 
 /* Library version (major*10000 + minor*100 + patch). */
 int npub_version(void);
@@ -78,6 +79,22 @@ int npub_w8a16_gemm(const void* A, int64_t lda, const int8_t* Wq, int64_t ldw, c
                     int64_t ldc, const void* R, int64_t ldr, int M, int N, int K, float alpha, void* workspace,
                     size_t workspace_bytes, void* stream);
 size_t npub_w8a16_gemm_workspace(int M, int N, int K);
+
+/* Allocation-free W8A16 matmul (no counterpart in the reference, which has no
+ * device memory at all).  Same contract and result as npub_w8a16_gemm, for
+ * callers that cannot allocate device memory -- a plugin whose host runtime
+ * owns all device memory, a plain C/ctypes caller with no device allocator,
+ * or a fixed-budget decode loop where cudaMalloc is not allowed -- and so
+ * cannot pass a workspace.  The split-K scratch comes from a static device
+ * array of NPUB_NOALLOC_SCRATCH_BYTES that every device loading the library
+ * holds until exit.  Requests whose npub_w8a16_gemm_workspace(M, N, K)
+ * exceeds that return NPUB_ERR_SCRATCH_LIMIT.  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) with that
+ * device current; make that first call before any stream capture.  All calls
+ * share the array: calls that overlap on the GPU race.  Nothing is allocated. */
+#define NPUB_NOALLOC_SCRATCH_BYTES (16u << 20)
+int npub_w8a16_gemm_noalloc(const void* A, int64_t lda, const int8_t* Wq, int64_t ldw, const void* scale, void* C,
+                            int64_t ldc, const void* R, int64_t ldr, int M, int N, int K, float alpha, void* stream);
 
 /* Same contract with fp16 weights W [N, K] (ldw % 8 == 0): the plain fp16
  * matmul of npu.py:41-47 / mysim.cpp:109-113 on tensor cores (used for the

@@ -18,6 +18,7 @@ NPUB_ERR_CUDA = -3
 NPUB_ERR_WORKSPACE = -4
 NPUB_ERR_DEVICE_TIMEOUT = -5
 NPUB_ERR_NO_DEVICE = -6
+NPUB_ERR_SCRATCH_LIMIT = -7
 NPUB_NO_CAUSAL = -1
 
 _p = ctypes.c_void_p
@@ -36,6 +37,7 @@ SIGNATURES = {
     "npub_launch_count": (ctypes.c_ulonglong, []),
     "npub_w8a16_gemm": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _p, _i64, _i, _i, _i, _f, _p, _sz, _p]),
     "npub_w8a16_gemm_workspace": (_sz, [_i, _i, _i]),
+    "npub_w8a16_gemm_noalloc": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _p, _i64, _i, _i, _i, _f, _p]),
     "npub_f16_gemm": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _p, _i64, _i, _i, _i, _f, _p, _sz, _p]),
     "npub_f16_gemm_workspace": (_sz, [_i, _i, _i]),
     "npub_quantize_w8": (_i, [_p, _i64, _i, _i, _p, _i64, _p, _p]),

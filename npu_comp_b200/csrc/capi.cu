@@ -42,6 +42,9 @@ extern "C" const char* npub_strerror(int status) {
         case NPUB_ERR_WORKSPACE: return "workspace missing or too small";
         case NPUB_ERR_DEVICE_TIMEOUT: return "a device-side wait timed out";
         case NPUB_ERR_NO_DEVICE: return "no sm_100 device";
+        case NPUB_ERR_SCRATCH_LIMIT:
+            return "request needs more split-K scratch than the allocation-free entry point holds "
+                   "(NPUB_NOALLOC_SCRATCH_BYTES); use npub_w8a16_gemm with a workspace";
         default: return "unknown status";
     }
 }
