@@ -65,8 +65,9 @@ class ClockSampler:
 
     def __enter__(self):
         try:
+            self.t0 = time.time()
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -77,6 +78,13 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+
+    def wait_first_sample(self, timeout=3.0):
+        """Block until nvidia-smi has produced a sample (its start-up takes ~0.5 s)."""
+        t0 = time.time()
+        while self.proc is not None and not self.lines and time.time() - t0 < timeout:
+            time.sleep(0.02)
+        self.lines.clear()
 
     def __exit__(self, *a):
         if self.proc is not None:
@@ -267,6 +275,7 @@ def run_ours(args):
     except Exception:
         smi_id = local
     with ClockSampler(smi_id) as clk:
+        clk.wait_first_sample()
         torch.cuda.synchronize()
         barrier()
         for i in range(args.steps):
@@ -366,7 +375,7 @@ def _scale_rate(flop_rate, workload):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["layer", "decode", "gemm"], default="layer")

@@ -340,13 +340,13 @@ int num_sms() {
 }
 
 int make_tmap_3d(CUtensorMap* m, bool int8, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
-                 uint64_t s2, uint32_t box1, uint32_t box2, bool swizzle128) {
+                 uint64_t s2, uint32_t box1, uint32_t box2, bool swizzle128, uint32_t box0) {
     auto enc = encode_fn();
     if (!enc) return NPUB_ERR_CUDA;
     const int es = int8 ? 1 : 2;
     cuuint64_t gdim[3] = {d0, d1, d2};
     cuuint64_t gstride[2] = {s1 * es, s2 * es};
-    cuuint32_t box[3] = {(cuuint32_t)BK, box1, box2};
+    cuuint32_t box[3] = {(cuuint32_t)box0, box1, box2};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(m, int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
                      const_cast<void*>(base), gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -431,7 +431,7 @@ static int linear_w8a16_pair(const void* A, int64_t lda, const void* W, int64_t 
     memset(&p, 0, sizeof(p));
     const int bt = pair_bt(M);
     int rc = make_tmap_3d(&p.tmW, true, W, (uint64_t)K, (uint64_t)N, 1, (uint64_t)ldw, (uint64_t)ldw * N, 128, 1,
-                          false);
+                          false, kPairBK);
     if (rc) return rc;
     rc = make_tmap_3d(&p.tmX, false, A, (uint64_t)K, (uint64_t)M, 1, (uint64_t)lda, (uint64_t)lda * M,
                       (uint32_t)(bt / 2), 1, true);

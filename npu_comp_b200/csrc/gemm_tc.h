@@ -40,8 +40,10 @@ struct GemmParams {
 
 int num_sms();
 int pick_bt(int b_rows);
+// box0: elements of the innermost box dimension (64 = one 128-byte fp16 row;
+// up to 256 for the unswizzled int8 weight tiles).
 int make_tmap_3d(CUtensorMap* m, bool int8, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
-                 uint64_t s2, uint32_t box1, uint32_t box2, bool swizzle128);
+                 uint64_t s2, uint32_t box1, uint32_t box2, bool swizzle128, uint32_t box0 = 64);
 int run_gemm(GemmParams& p, bool a_int8, int bt, int grid_x, int grid_y, int batch, cudaStream_t st);
 // A plain (unbatched) mapping: zl = z, no row offsets.
 inline void zmap_plain(GemmParams& p) {

@@ -10,12 +10,12 @@
 // BT = 256 for 2*256*256*64 FLOP per pair -- which is what lets a deep TMA ring
 // cover L2 latency.
 //
-// Roles per CTA (512 threads):
+// Roles per CTA (256 + 128 x converter groups threads):
 //   warp 0      TMA producer: int8 weight tile -> own barrier full_a[s];
 //               token half-tile -> the even CTA's barrier full_b[s]
 //   warp 1      TMEM allocator (both CTAs); MMA issuer (even CTA only)
 //   warps 4-7   epilogue: TMEM -> registers -> scale/residual -> global
-//   warps 8-15  converters in two groups of four that take alternate K steps:
+//   warps 8+    converters in groups of four warps that take K steps in turn:
 //               int8 stage -> fp16 128-byte-swizzled stage, then an arrive on
 //               the even CTA's conv[c]
 // The accumulator is double-buffered in TMEM (2 x BT columns), so the epilogue
@@ -36,15 +36,18 @@ namespace npub {
 
 namespace pair {
 
-constexpr int kThreads = 512;
-constexpr int BK = 64;
+constexpr int kThreads = 256 + 128 * kPairConvGroups;
+constexpr int BK = kPairBK;       // K per stage
+constexpr int KCH = kPairKch;     // 64-wide swizzled chunks per stage
 constexpr int UMMA_K = 16;
 constexpr int kRowsPerCta = 128;  // weight rows per CTA (MMA M = 256 per pair)
 
 template <int BT, int STAGES, int CSTAGES>
 struct Smem {
-    static constexpr int kBh = (BT / 2) * BK * 2;  // fp16 token half-tile per stage
-    static constexpr int kA16 = kRowsPerCta * BK * 2;
+    static constexpr int kBhChunk = (BT / 2) * 64 * 2;  // one 64-wide chunk of the token half-tile
+    static constexpr int kBh = KCH * kBhChunk;          // fp16 token half-tile per stage
+    static constexpr int kA16Chunk = kRowsPerCta * 64 * 2;
+    static constexpr int kA16 = KCH * kA16Chunk;
     static constexpr int kA8 = kRowsPerCta * BK;
     static constexpr int kBars = 8 * (3 * STAGES + 2 * CSTAGES + 4) + 16;
     static constexpr int kTotal = STAGES * (kBh + kA8) + CSTAGES * kA16 + kBars + 1024;
@@ -92,7 +95,8 @@ template <int BT, int STAGES, int CSTAGES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     w8a16_pair_kernel(const __grid_constant__ PairParams p) {
     using L = Smem<BT, STAGES, CSTAGES>;
-    static_assert(STAGES % 2 == 0 && CSTAGES >= 2, "see kPairStages*: converter groups alternate K steps");
+    static_assert(STAGES % kPairConvGroups == 0 && CSTAGES >= kPairConvGroups && CSTAGES >= 2,
+                  "see kPairStages*: converter groups take turns");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sB = smem;                            // STAGES x kBh   (1024-aligned)
@@ -168,7 +172,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     mbar_arrive_expect_tx(&full_a[s], (uint32_t)L::kA8);
                     if (leader) mbar_arrive_expect_tx(&full_b[s], (uint32_t)(2 * L::kBh));
                     tma_load_3d(sA8 + s * L::kA8, &p.tmW, &full_a[s], k, arow, 0);
-                    tma_load_3d_pair(sB + s * L::kBh, &p.tmX, full_b0 + (uint32_t)s * 8u, k, brow, 0);
+#pragma unroll
+                    for (int ch = 0; ch < KCH; ++ch)
+                        tma_load_3d_pair(sB + s * L::kBh + ch * L::kBhChunk, &p.tmX, full_b0 + (uint32_t)s * 8u,
+                                         k + 64 * ch, brow, 0);
                     ++issued;
                 }
             }
@@ -210,12 +217,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t abase = smem_u32(sA16 + c * L::kA16);
-                    const uint32_t bbase = smem_u32(sB + s * L::kBh);
 #pragma unroll
-                    for (int kk = 0; kk < BK / UMMA_K; ++kk)
-                        tc_mma_f16_pair(dcol, umma_desc_sw128(abase + kk * UMMA_K * 2),
-                                        umma_desc_sw128(bbase + kk * UMMA_K * 2), idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                    for (int ch = 0; ch < KCH; ++ch) {
+                        const uint32_t abase = smem_u32(sA16 + c * L::kA16 + ch * L::kA16Chunk);
+                        const uint32_t bbase = smem_u32(sB + s * L::kBh + ch * L::kBhChunk);
+#pragma unroll
+                        for (int kk = 0; kk < 64 / UMMA_K; ++kk)
+                            tc_mma_f16_pair(dcol, umma_desc_sw128(abase + kk * UMMA_K * 2),
+                                            umma_desc_sw128(bbase + kk * UMMA_K * 2), idesc,
+                                            (i > 0 || ch > 0 || kk > 0) ? 1u : 0u);
+                    }
                     tc_commit_pair(smem_u32(&empty[s]));
                     tc_commit_pair(mapa_shared(smem_u32(&empty[s]), peer));
                     tc_commit_pair(smem_u32(&c_empty[c]));
@@ -229,7 +240,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 8) {
         // ------------------------------------------------------------ converters
-        const int grp = (warp - 8) >> 2;             // converter group 0 / 1
+        const int grp = (warp - 8) >> 2;             // converter group
         const int t = (threadIdx.x - 256) & 127;     // 0..127 within the group
         const uint32_t conv0 = mapa_shared(smem_u32(&conv[0]), 0);
         uint32_t g = 0;
@@ -237,7 +248,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int tile = cid; tile < p.n_tiles && ok; tile += ncl) {
             const TileCoord tc = tile_coord(p, tile, BT);
             for (int i = 0; i < tc.nk; ++i, ++g) {
-                if ((int)(g & 1u) != grp) continue;
+                if ((int)(g % kPairConvGroups) != grp) continue;
                 const int s = (int)(g % STAGES);
                 const uint32_t ph = (g / STAGES) & 1u;
                 const int c = (int)(g % CSTAGES);
@@ -252,15 +263,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const uint8_t* a8 = sA8 + s * L::kA8;
                 uint8_t* a16 = sA16 + c * L::kA16;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
+                for (int j = 0; j < 4 * KCH; ++j) {  // 16 int8 per task, 4*KCH tasks per row
                     const int task = t + 128 * j;
-                    const int row = task >> 2, q = task & 3;
+                    const int row = task / (4 * KCH), q = task % (4 * KCH);
                     const uint4 raw = *reinterpret_cast<const uint4*>(a8 + row * BK + q * 16);
                     uint4 lo, hi;
                     cvt16(raw, lo, hi);
-                    const int sw = row & 7;
-                    *reinterpret_cast<uint4*>(a16 + row * 128 + (((2 * q) ^ sw) << 4)) = lo;
-                    *reinterpret_cast<uint4*>(a16 + row * 128 + (((2 * q + 1) ^ sw) << 4)) = hi;
+                    const int sw = row & 7, qq = q & 3;
+                    uint8_t* dst = a16 + (q >> 2) * L::kA16Chunk + row * 128;
+                    *reinterpret_cast<uint4*>(dst + (((2 * qq) ^ sw) << 4)) = lo;
+                    *reinterpret_cast<uint4*>(dst + (((2 * qq + 1) ^ sw) << 4)) = hi;
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -414,7 +426,7 @@ size_t w8a16_pair_workspace(int M, int N, int K) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
     const int bt = pair_bt(M);
     const int tiles = ((N + 255) / 256) * ((M + bt - 1) / bt);
-    const int k_tiles = (K + 63) / 64;
+    const int k_tiles = (K + kPairBK - 1) / kPairBK;
     const int s = pair_splits(tiles, k_tiles, clusters_for_bt(bt));
     return s > 1 ? (size_t)s * M * N * sizeof(float) : 0;
 }
@@ -425,7 +437,7 @@ int w8a16_pair_run(PairParams& p, int M, int N, int K, cudaStream_t st) {
     const int bt = pair_bt(M);
     p.M = M;
     p.N = N;
-    p.k_tiles = (K + 63) / 64;
+    p.k_tiles = (K + kPairBK - 1) / kPairBK;
     p.n_apairs = (N + 255) / 256;
     p.n_btiles = (M + bt - 1) / bt;
     const int clusters = clusters_for_bt(bt);
@@ -444,7 +456,7 @@ int w8a16_pair_run(PairParams& p, int M, int N, int K, cudaStream_t st) {
 int w8a16_pair_splits(int M, int N, int K) {
     const int bt = pair_bt(M);
     const int tiles = ((N + 255) / 256) * ((M + bt - 1) / bt);
-    return pair_splits(tiles, (K + 63) / 64, clusters_for_bt(bt));
+    return pair_splits(tiles, (K + kPairBK - 1) / kPairBK, clusters_for_bt(bt));
 }
 
 }  // namespace npub

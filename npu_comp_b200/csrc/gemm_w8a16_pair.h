@@ -8,15 +8,40 @@
 
 namespace npub {
 
-// TMA ring depths per token-tile width (shared memory: 24/16/12 KB per stage)
-// and the depth of the converted fp16 weight ring (16 KB per stage).  The TMA
+// TMA ring depths per token-tile width and the depth of the converted fp16
+// weight ring; one stage carries kPairBK = 128 of K (48/32/24 KB of TMA data
+// at BT = 256/128/64, 32 KB of converted weights).  Measured on B200: the
+// per-stage synchronisation cost is fixed, so two 64-wide K chunks per stage
+// beat deeper rings of single chunks (1113 vs 915 TFLOP/s at 2048x22016x4096).  The TMA
 // depth must be even: the two converter groups take alternate K steps, and a
 // group waiting for step g relies on having itself consumed step g - STAGES
 // (so the barrier phase it waits on cannot alias an older one).
-constexpr int kPairStages256 = 6;
-constexpr int kPairStages128 = 10;
-constexpr int kPairStages64 = 12;
-constexpr int kPairCStages = 4;
+#ifndef NPUB_PAIR_STAGES256
+#define NPUB_PAIR_STAGES256 3
+#endif
+#ifndef NPUB_PAIR_STAGES128
+#define NPUB_PAIR_STAGES128 5
+#endif
+#ifndef NPUB_PAIR_STAGES64
+#define NPUB_PAIR_STAGES64 6
+#endif
+#ifndef NPUB_PAIR_CSTAGES
+#define NPUB_PAIR_CSTAGES 2
+#endif
+#ifndef NPUB_PAIR_CONV_GROUPS
+#define NPUB_PAIR_CONV_GROUPS 1
+#endif
+constexpr int kPairStages256 = NPUB_PAIR_STAGES256;
+constexpr int kPairStages128 = NPUB_PAIR_STAGES128;
+constexpr int kPairStages64 = NPUB_PAIR_STAGES64;
+constexpr int kPairCStages = NPUB_PAIR_CSTAGES;
+constexpr int kPairConvGroups = NPUB_PAIR_CONV_GROUPS;  // converter groups of 4 warps (alternate K steps)
+#ifndef NPUB_PAIR_KCH
+#define NPUB_PAIR_KCH 2
+#endif
+// 64-wide K chunks per pipeline stage (one 128-byte swizzled row of fp16 each).
+constexpr int kPairKch = NPUB_PAIR_KCH;
+constexpr int kPairBK = 64 * kPairKch;
 
 struct PairParams {
     CUtensorMap tmW;  // int8 weights [N, K]: box {64, 128, 1}, no swizzle

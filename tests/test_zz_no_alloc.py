@@ -80,12 +80,9 @@ def test_noalloc_scratch_is_exercised_and_reused(cuda_device):
 def test_noalloc_rejects_requests_beyond_its_scratch(cuda_device):
     lib = _lib.load()
     shape = None
-    for M in (128, 192, 256):
-        for N in (12288, 22016, 32000):
-            if lib.npub_w8a16_gemm_workspace(M, N, 4096) > SCRATCH:
-                shape = (M, N, 4096)
-                break
-        if shape:
+    for M, N, K in ((256, 8192, 16384), (256, 4096, 32768), (256, 8192, 32768), (128, 8192, 65536)):
+        if lib.npub_w8a16_gemm_workspace(M, N, K) > SCRATCH:
+            shape = (M, N, K)
             break
     if shape is None:
         pytest.skip("no split-K shape exceeds the scratch on this device")
