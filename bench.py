@@ -213,7 +213,7 @@ def run_ours(args):
         x = torch.randn((T, cfg.d), generator=gen, device=dev).half()
         sc = llama.Scratch()
         y = torch.empty_like(x)
-        step = lambda: llama.layer_prefill(x, w, cfg, tp=tp, scratch=sc, out=y)  # noqa: E731
+        step = lambda ev=None: llama.layer_prefill(x, w, cfg, tp=tp, scratch=sc, out=y, events=ev)  # noqa: E731
         units = float(T)
         unit = "tokens/s"
         config = {"workload": "llama7b_layer_prefill_w8a16", "tokens": T, "batch": 1, "d": cfg.d,
@@ -266,9 +266,30 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
 
+    # The step is replayed from a CUDA graph: one launch per step instead of
+    # ~15 host-side op calls (the kernels and their arguments are identical).
+    eager_step = step
+    graph = None
+    if not args.eager and world == 1:
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                eager_step()
+            torch.cuda.synchronize()
+            step = graph.replay
+            for _ in range(2):
+                step()
+            torch.cuda.synchronize()
+        except Exception as e:  # keep the eager step (the line says which)
+            print(f"graph capture failed, timing eager launches: {e}", file=sys.stderr)
+            graph = None
+            step = eager_step
+
     # ---- timed region (device time, CUDA events, max over ranks)
-    npu.gemm_events = []
-    launches0 = _lib.launch_count()
+    c0 = _lib.launch_count()
+    eager_step()
+    torch.cuda.synchronize()
+    launches_per_step = _lib.launch_count() - c0  # kernels of one step (a graph replay bypasses the counter)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     try:
         smi_id = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
@@ -286,9 +307,7 @@ def run_ours(args):
             ev[i][1].record()
         torch.cuda.synchronize()
         barrier()
-    launches = _lib.launch_count() - launches0
-    gev = npu.gemm_events
-    npu.gemm_events = None
+    launches = launches_per_step * args.steps
     step_ms = sum(a.elapsed_time(b) for a, b in ev)
     t = torch.tensor([step_ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -298,18 +317,38 @@ def run_ours(args):
     per_rank_units = units  # TP: every rank processes the same tokens (strong scaling)
     value = per_rank_units / (ms_per_step / 1e3) if wl != "gemm" else units * world / (ms_per_step / 1e3)
 
-    # dominant kernel roofline: W8A16 GEMM launches inside the timed steps
-    g_ms = sum(a.elapsed_time(b) for a, b, _, i8 in gev if i8)
-    g_flops = sum(f for _, _, f, i8 in gev if i8)
-    g_n = sum(1 for *_, i8 in gev if i8)
+    # Dominant kernel roofline and per-op breakdown: eager steps with CUDA events
+    # around each op on its stream, each enqueued behind a graph replay so that the
+    # host is ahead of the device and the events bracket device time only.
+    reps = max(1, min(args.steps, 10))
+    npu.gemm_events = []
+    evs = [] if wl == "layer" else None
+    for _ in range(reps):
+        if flush is not None:
+            flush.fill_(1.0)
+        if graph is not None:
+            graph.replay()
+        eager_step(evs) if wl == "layer" else eager_step()
+    torch.cuda.synchronize()
+    gev = npu.gemm_events
+    npu.gemm_events = None
+    breakdown = None
+    if evs is not None:
+        breakdown = {}
+        for name, a_, b_ in evs:
+            breakdown[name] = breakdown.get(name, 0.0) + a_.elapsed_time(b_) * 1e3 / reps
+        breakdown = {k_: round(v_, 1) for k_, v_ in breakdown.items()}
+    g_ms = sum(a.elapsed_time(b) for a, b, _, i8 in gev if i8) / reps
+    g_flops = sum(f for _, _, f, i8 in gev if i8) / reps
+    g_n = sum(1 for *_, i8 in gev if i8) // reps
     achieved = g_flops / (g_ms / 1e3) / 1e12 if g_ms > 0 else None
     peak = tf_burst
-    roof = {"kernel": "gemm_tc_kernel<int8> (tcgen05 W8A16)", "bound": "tensor", "achieved": achieved, "peak": peak,
-            "unit": "TFLOP/s", "frac": (achieved / peak) if achieved else None,
-            "peak_source": f"{peak_src} bf16 dense (burst)", "launches": g_n,
+    roof = {"kernel": "w8a16_pair_kernel (tcgen05 cta_group::2 W8A16)", "bound": "tensor", "achieved": achieved,
+            "peak": peak, "unit": "TFLOP/s", "frac": (achieved / peak) if achieved else None,
+            "peak_source": f"{peak_src} bf16 dense (burst)", "launches_per_step": g_n,
             "flops_per_launch": g_flops / g_n if g_n else None,
             "avg_launch_us": g_ms * 1e3 / g_n if g_n else None,
-            "traffic": _traffic(wl), "share_of_step": (g_ms / step_ms) if step_ms else None}
+            "traffic": _traffic(wl), "share_of_step": (g_ms / ms_per_step) if ms_per_step else None}
 
     # e2e: same step through the public API with host buffers, copies inside the timed region
     h_host = torch.empty(h_in.shape, dtype=h_in.dtype, pin_memory=True)
@@ -344,8 +383,10 @@ def run_ours(args):
                "roofline": roof,
                "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": h_in.numel() * h_in.element_size(),
                        "d2h_bytes_per_step": d_out.numel() * d_out.element_size()},
-               "gpu_launches": int(launches), "clocks": clk.summary()}
+               "gpu_launches": int(launches), "clocks": clk.summary(),
+               "launch": "cuda_graph" if graph is not None else "eager"}
         if wl == "layer":
+            out["breakdown_us"] = breakdown
             flops = llama.layer_flops(cfg, 2048, 2048)
             out["layer_tflops"] = flops / (ms_per_step / 1e3) / 1e12
             out["layer_tensor_frac"] = out["layer_tflops"] * world / peak
@@ -380,6 +421,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["layer", "decode", "gemm"], default="layer")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="launch every op from the host instead of a CUDA graph")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank = int(os.environ.get("RANK", 0))

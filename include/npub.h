@@ -120,6 +120,11 @@ int npub_quantize_w8(const float* W, int64_t ldw, int K, int N, int8_t* Wq, int6
 int npub_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr, void* x_out, int64_t ldxo,
                  const void* gamma, void* y, int64_t ldy, int rows, int d, float eps, void* stream);
 
+/* Residual add, the v_add of b_program_examples/llama_layer.py:139,152:
+ *   out = fp16(a + b)  (fp32 add), a, b, out fp16 [rows, cols] (out may alias a or b). */
+int npub_add(const void* a, int64_t lda, const void* b, int64_t ldb, void* out, int64_t ldo, int rows, int cols,
+             void* stream);
+
 /* SwiGLU, legalize.py:130-149, llama_layer.py:143-151:
  *   h = fp16( g / (1 + exp(-g)) * u )   (fp32 math), g, u, h fp16 [rows, cols]. */
 int npub_swiglu(const void* g, int64_t ldg, const void* u, int64_t ldu, void* h, int64_t ldh, int rows, int cols,
@@ -150,8 +155,9 @@ int npub_rope(void* x, int64_t ldx, int tokens, int heads, int head_dim, const i
  * rows [b*tokens, (b+1)*tokens)), row strides ldq/ldk/ldv; head h reads
  * columns [h*head_dim, (h+1)*head_dim) of q and kv head h / (heads/kv_heads)
  * of k and v (grouped-query heads).  out fp16 [batch*tokens, heads*head_dim] (ldo).
- * head_dim % 16 == 0, head_dim <= 256; batch*heads <= 65535.
- * Scratch: npub_attention_workspace() bytes, 256-byte aligned. */
+ * head_dim % 16 == 0, head_dim <= 256; batch*heads <= 65535.  head_dim 128 runs a
+ * fused flash-attention kernel and needs no scratch; other sizes materialise
+ * S/P: npub_attention_workspace() bytes, 256-byte aligned. */
 int npub_attention_prefill(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
                            void* out, int64_t ldo, int batch, int tokens, int heads, int kv_heads, int head_dim,
                            float scale, int causal, void* workspace, size_t workspace_bytes, void* stream);

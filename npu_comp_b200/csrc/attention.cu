@@ -1,6 +1,7 @@
 // Attention for sm_100a.
 //
-// Prefill (llama_layer.py:114-137, legalize.py:117-127): per head
+// Prefill (llama_layer.py:114-137, legalize.py:117-127): head_dim 128 runs the
+// fused flash-attention kernel of fmha.cu; other head sizes run per head
 //   S = Q K^T * scale (tcgen05 GEMM, tiles above the causal diagonal skipped)
 //   P = softmax(S) in place (vector_ops.cu)
 //   O = P V (tcgen05 GEMM, K loop cut at the diagonal), V transposed once so
@@ -12,6 +13,10 @@
 #include "gemm_tc.h"
 
 namespace npub {
+
+int fmha_prefill(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* out,
+                 int64_t ldo, int batch, int tokens, int heads, int kv_heads, float scale, int causal,
+                 cudaStream_t st);
 
 // V rows of `batch` sequences [batch*T, ldv] (kv head h at columns h*hd) ->
 // Vt [batch*kvh, hd, tp] (tokens contiguous, zero past T).
@@ -235,6 +240,7 @@ static size_t attn_s_bytes(int batch, int tokens, int heads) {
 
 extern "C" size_t npub_attention_workspace(int batch, int tokens, int heads, int head_dim) {
     if (batch <= 0 || tokens <= 0 || heads <= 0 || head_dim <= 0) return 0;
+    if (head_dim == 128) return 0;  // fused flash-attention kernel (fmha.cu): no scratch
     const int64_t tp = pad8(tokens);
     // S/P [batch*heads, tokens, tp] + Vt [batch*heads, head_dim, tp] (kv_heads <= heads)
     const size_t v_bytes = ((size_t)batch * heads * head_dim * tp * 2 + 255) / 256 * 256;
@@ -254,6 +260,9 @@ extern "C" int npub_attention_prefill(const void* q, int64_t ldq, const void* k,
                    ldv >= (int64_t)kv_heads * head_dim && ldo >= (int64_t)heads * head_dim);
     NPUB_CHECK_ARG(npub_aligned(q, 16) && npub_aligned(k, 16) && npub_aligned(v, 16));
     NPUB_CHECK_ARG((int64_t)batch * heads <= 65535 && (int64_t)batch * tokens <= 0x7fffffffLL);
+    cudaStream_t st0 = reinterpret_cast<cudaStream_t>(stream);
+    if (head_dim == 128)
+        return fmha_prefill(q, ldq, k, ldk, v, ldv, out, ldo, batch, tokens, heads, kv_heads, scale, causal, st0);
     const size_t need = npub_attention_workspace(batch, tokens, heads, head_dim);
     if (!workspace || workspace_bytes < need) return NPUB_ERR_WORKSPACE;
     NPUB_CHECK_ARG(npub_aligned(workspace, 256));

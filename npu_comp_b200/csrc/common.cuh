@@ -7,7 +7,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/npub.h"
+#include "npub.h"
 
 #define NPUB_CHECK_ARG(cond) \
     do {                     \
@@ -267,4 +267,50 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster_addr) {
                  : "memory");
 }
 
+}  // namespace npub
+
+namespace npub {
+// Shared-memory descriptor for an MN-major operand in 128-byte swizzled rows:
+// each row holds 64 fp16 of the MN dimension for one K index; 8-row groups
+// (K) are `sbo` bytes apart and 64-wide MN blocks `lbo` bytes apart.
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1u << 46;
+    d |= (uint64_t)2u << 61;
+    return d;
+}
+// Instruction descriptor, kind::f16, fp16 inputs, fp32 accumulator, A K-major,
+// B MN-major.
+__host__ __device__ constexpr uint32_t umma_idesc_f16_bmn(int m, int n) {
+    return umma_idesc_f16(m, n) | (1u << 16);
+}
+}  // namespace npub
+
+namespace npub {
+// 32 lanes x 32 bit x 32 columns into r[0..31], without waiting.
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Named barrier over `nthreads` threads (multiple of 32).
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+// Hardware base-2 exponential (MUFU ex2, approximate, flush-to-zero).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 }  // namespace npub

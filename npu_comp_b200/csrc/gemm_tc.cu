@@ -273,14 +273,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                 dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
             } else {
+                float rv[16];  // residual loads first: stores may alias them as far as the compiler knows
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    if (bb + j < p.b_rows) {
-                        float x = v[j] * sc;
-                        if (p.res) x += __half2float(p.res[rbase + (int64_t)(bb + j) * p.r_sb]);
-                        o[(int64_t)(bb + j) * p.o_sb] = __float2half_rn(x);
-                    }
-                }
+                for (int j = 0; j < 16; ++j)
+                    rv[j] = (p.res && bb + j < p.b_rows) ? __half2float(__ldg(p.res + rbase + (int64_t)(bb + j) * p.r_sb))
+                                                         : 0.0f;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (bb + j < p.b_rows) o[(int64_t)(bb + j) * p.o_sb] = __float2half_rn(v[j] * sc + rv[j]);
             }
         }
     }

@@ -314,14 +314,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         if (tb + j < p.M) o[(int64_t)(tb + j) * p.N] = v[j];
                 } else {
                     __half* o = p.C + obase;
+                    // all residual loads are issued before the first store (the two may
+                    // alias as far as the compiler knows, which would serialise them)
+                    float rv[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        if (tb + j < p.M) {
-                            float x = v[j] * sc;
-                            if (p.R) x += __half2float(p.R[(int64_t)(tb + j) * p.ldr + a]);
-                            o[(int64_t)(tb + j) * p.ldc] = __float2half_rn(x);
-                        }
-                    }
+                    for (int j = 0; j < 16; ++j)
+                        rv[j] = (p.R && tb + j < p.M) ? __half2float(__ldg(p.R + (int64_t)(tb + j) * p.ldr + a)) : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (tb + j < p.M) o[(int64_t)(tb + j) * p.ldc] = __float2half_rn(v[j] * sc + rv[j]);
                 }
             }
             tc_fence_before();

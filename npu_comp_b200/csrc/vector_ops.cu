@@ -127,6 +127,32 @@ __global__ void swiglu_scalar_kernel(const __half* __restrict__ g, int64_t ldg, 
     }
 }
 
+// ------------------------------------------------------------ residual add
+__global__ void add_vec_kernel(const __half* __restrict__ a, int64_t lda, const __half* __restrict__ b, int64_t ldb,
+                               __half* __restrict__ o, int64_t ldo, int rows, int cols) {
+    const int cpr = cols / kVec;
+    const int64_t total = (int64_t)rows * cpr;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int rr = (int)(i / cpr), c = (int)(i - (int64_t)rr * cpr) * kVec;
+        float av[8], bv[8], ov[8];
+        unpack8(*reinterpret_cast<const uint4*>(a + (int64_t)rr * lda + c), av);
+        unpack8(*reinterpret_cast<const uint4*>(b + (int64_t)rr * ldb + c), bv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ov[k] = av[k] + bv[k];
+        *reinterpret_cast<uint4*>(o + (int64_t)rr * ldo + c) = pack8(ov);
+    }
+}
+
+__global__ void add_scalar_kernel(const __half* __restrict__ a, int64_t lda, const __half* __restrict__ b, int64_t ldb,
+                                  __half* __restrict__ o, int64_t ldo, int rows, int cols) {
+    const int64_t total = (int64_t)rows * cols;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int rr = (int)(i / cols), c = (int)(i - (int64_t)rr * cols);
+        o[(int64_t)rr * ldo + c] =
+            __float2half_rn(__half2float(a[(int64_t)rr * lda + c]) + __half2float(b[(int64_t)rr * ldb + c]));
+    }
+}
+
 // ------------------------------------------------------------ softmax
 // One CTA per row.  Valid columns: [0, min(cols, r + off + 1)) when causal.
 // Masked columns are written as zero up to zend.
@@ -210,6 +236,42 @@ __global__ void rope_kernel(__half* x, int64_t ldx, int tokens, int heads, int h
         const float x1 = __half2float(row[k]), x2 = __half2float(row[k + half]);
         row[k] = __float2half_rn(x1 * cs - x2 * sn);
         row[k + half] = __float2half_rn(x2 * cs + x1 * sn);
+    }
+}
+
+// Vectorised RoPE: one CTA per token; the token's cos/sin for the hd/2
+// frequencies are computed once into shared memory, then every head's pairs
+// (x[i], x[i + hd/2]) are rotated 8 at a time with 128-bit accesses.
+__global__ void rope_vec_kernel(__half* x, int64_t ldx, int heads, int hd, const int32_t* __restrict__ pos, int pos0,
+                                float log2_theta) {
+    __shared__ float cs[256], sn[256];
+    const int t = blockIdx.x;
+    const int half = hd / 2;
+    const int p = pos ? pos[t] : pos0 + t;
+    for (int k = threadIdx.x; k < half; k += blockDim.x) {
+        const float inv_freq = exp2f(-(2.0f * (float)k / (float)hd) * log2_theta);
+        float sv, cv;
+        sincosf((float)p * inv_freq, &sv, &cv);
+        cs[k] = cv;
+        sn[k] = sv;
+    }
+    __syncthreads();
+    __half* row = x + (int64_t)t * ldx;
+    const int per_head = half / 8;
+    for (int i = threadIdx.x; i < heads * per_head; i += blockDim.x) {
+        const int hh = i / per_head, k0 = (i - hh * per_head) * 8;
+        __half* a = row + (int64_t)hh * hd + k0;
+        float x1[8], x2[8], y1[8], y2[8];
+        unpack8(*reinterpret_cast<const uint4*>(a), x1);
+        unpack8(*reinterpret_cast<const uint4*>(a + half), x2);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float c = cs[k0 + e], sv = sn[k0 + e];
+            y1[e] = x1[e] * c - x2[e] * sv;
+            y2[e] = x2[e] * c + x1[e] * sv;
+        }
+        *reinterpret_cast<uint4*>(a) = pack8(y1);
+        *reinterpret_cast<uint4*>(a + half) = pack8(y2);
     }
 }
 
@@ -361,6 +423,11 @@ extern "C" int npub_rope(void* x, int64_t ldx, int tokens, int heads, int head_d
     if (tokens == 0 || heads == 0) return NPUB_OK;
     NPUB_CHECK_ARG(x && head_dim > 0 && head_dim % 2 == 0 && ldx >= (int64_t)heads * head_dim && theta > 0.0f);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (head_dim % 16 == 0 && head_dim <= 512 && ldx % 8 == 0 && npub_aligned(x, 16)) {
+        rope_vec_kernel<<<tokens, 128, 0, st>>>(reinterpret_cast<__half*>(x), ldx, heads, head_dim, positions, pos0,
+                                                log2f(theta));
+        return npub_internal_launch_status();
+    }
     const int64_t work = (int64_t)tokens * heads * (head_dim / 2);
     rope_kernel<<<grid_for(work, 256), 256, 0, st>>>(reinterpret_cast<__half*>(x), ldx, tokens, heads, head_dim,
                                                       positions, pos0, log2f(theta));
@@ -374,5 +441,24 @@ extern "C" int npub_quantize_w8(const float* W, int64_t ldw, int K, int N, int8_
     NPUB_CHECK_ARG(W && Wq && scale && ldw >= N && ldq >= K);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     quantize_w8_kernel<<<(N + 31) / 32, 256, 0, st>>>(W, ldw, K, N, Wq, ldq, reinterpret_cast<__half*>(scale));
+    return npub_internal_launch_status();
+}
+
+extern "C" int npub_add(const void* a, int64_t lda, const void* b, int64_t ldb, void* out, int64_t ldo, int rows,
+                        int cols, void* stream) {
+    NPUB_CHECK_ARG(rows >= 0 && cols >= 0);
+    if (rows == 0 || cols == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(a && b && out && lda >= cols && ldb >= cols && ldo >= cols);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const bool vec = cols % kVec == 0 && lda % kVec == 0 && ldb % kVec == 0 && ldo % kVec == 0 && npub_aligned(a, 16) &&
+                     npub_aligned(b, 16) && npub_aligned(out, 16);
+    const __half* ah = reinterpret_cast<const __half*>(a);
+    const __half* bh = reinterpret_cast<const __half*>(b);
+    __half* oh = reinterpret_cast<__half*>(out);
+    if (vec)
+        add_vec_kernel<<<grid_for((int64_t)rows * (cols / kVec), 256), 256, 0, st>>>(ah, lda, bh, ldb, oh, ldo, rows,
+                                                                                    cols);
+    else
+        add_scalar_kernel<<<grid_for((int64_t)rows * cols, 256), 256, 0, st>>>(ah, lda, bh, ldb, oh, ldo, rows, cols);
     return npub_internal_launch_status();
 }

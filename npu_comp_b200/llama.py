@@ -12,9 +12,9 @@ stored quantised and K-major: Wq [N, K] int8 + scale [N] fp16.
 Tensor parallelism (Megatron style, one process per GPU): QKV and gate/up are
 column-parallel (each rank owns heads / FFN columns), O and down are
 row-parallel (each rank owns the matching K slice) followed by one all-reduce
-(sum) per block through torch.distributed (NCCL over NVLink).  Rank 0 folds
-the residual into its row-parallel epilogue, so the reduced sum is already
-x + attn (resp. h + ffn).
+(sum) per block through torch.distributed (NCCL over NVLink).  The residual
+adds run after the reductions: h = x + attn inside the second RMSNorm kernel,
+y = h + ffn in a vector add.
 """
 from __future__ import annotations
 
@@ -180,9 +180,30 @@ class Scratch:
         return t
 
 
+class _Marks:
+    """Optional per-op CUDA events: (name, start, end) appended to `events`."""
+
+    def __init__(self, events):
+        self.events = events
+        self.cur = None
+
+    def __call__(self, name):
+        if self.events is None:
+            return
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        if self.cur is not None:
+            self.events.append((self.cur[0], self.cur[1], e))
+        self.cur = (name, e)
+
+    def end(self):
+        self("")
+
+
 def layer_prefill(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, *, batch: int = 1, tp: TP = TP(),
                   positions: Optional[torch.Tensor] = None, kv_out: Optional[tuple] = None,
-                  scratch: Optional[Scratch] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                  scratch: Optional[Scratch] = None, out: Optional[torch.Tensor] = None,
+                  events: Optional[list] = None) -> torch.Tensor:
     """One decoder layer over `batch` prompts of equal length stacked in x [batch*T, d].
 
     kv_out: optional (k_cache, v_cache) [batch, kv_heads_local, cap, hd] that
@@ -197,28 +218,42 @@ def layer_prefill(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, *, batch: 
     qkv_n = (hq + 2 * hk) * hd
     if positions is None:
         positions = torch.arange(T, device=dev, dtype=torch.int32).repeat(batch)
+    mk = _Marks(events)
     # attention block
+    mk("rmsnorm")
     xn = npu.rmsnorm(x, w.g1, cfg.eps, out=sc.get("xn", (BT, d), device=dev))
+    mk("qkv_gemm")
     qkv = npu.matmul(xn, w.wqkv, w.sqkv, out=sc.get("qkv", (BT, qkv_n), device=dev))
     q = qkv[:, : hq * hd]
     k = qkv[:, hq * hd:(hq + hk) * hd]
     v = qkv[:, (hq + hk) * hd:]
-    npu.rope(q, hq, hd, positions=positions, theta=cfg.theta)
-    npu.rope(k, hk, hd, positions=positions, theta=cfg.theta)
+    mk("rope")
+    npu.rope(qkv, hq + hk, hd, positions=positions, theta=cfg.theta)  # q and k heads are adjacent columns
     if kv_out is not None:
         _store_prompt_kv(k, v, kv_out, batch, T, hk, hd)
+    mk("attention")
     ctx = npu.attention(q, k, v, hq, hk, head_dim=hd, batch=batch, causal=True,
                         out=sc.get("ctx", (BT, hq * hd), device=dev))
+    mk("o_gemm")
+    attn = npu.matmul(ctx, w.wo, w.so, out=sc.get("attn", (BT, d), device=dev))
+    mk("all_reduce")
+    tp.all_reduce(attn)
+    # FFN block: h = x + attn is formed inside the RMSNorm kernel (llama_layer.py:139)
+    mk("rmsnorm")
     h = sc.get("h", (BT, d), device=dev)
-    npu.matmul(ctx, w.wo, w.so, out=h, residual=x if tp.rank == 0 else None)
-    tp.all_reduce(h)
-    # FFN block
-    hn = npu.rmsnorm(h, w.g2, cfg.eps, out=sc.get("hn", (BT, d), device=dev))
+    hn, _ = npu.rmsnorm(attn, w.g2, cfg.eps, residual=x, residual_out=h, out=sc.get("hn", (BT, d), device=dev))
+    mk("gate_up_gemm")
     gu = npu.matmul(hn, w.wgu, w.sgu, out=sc.get("gu", (BT, 2 * w.ffn), device=dev))
+    mk("swiglu")
     a = npu.swiglu(gu, out=sc.get("act", (BT, w.ffn), device=dev))
+    mk("down_gemm")
+    ffn = npu.matmul(a, w.wd, w.sd, out=sc.get("ffn", (BT, d), device=dev))
+    mk("all_reduce")
+    tp.all_reduce(ffn)
+    mk("residual")
     y = out if out is not None else torch.empty((BT, d), dtype=torch.float16, device=dev)
-    npu.matmul(a, w.wd, w.sd, out=y, residual=h if tp.rank == 0 else None)
-    tp.all_reduce(y)
+    npu.add(ffn, h, out=y)
+    mk.end()
     return y
 
 
@@ -245,22 +280,22 @@ def layer_decode(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, k_cache: to
     q = qkv[:, : hq * hd]
     k = qkv[:, hq * hd:(hq + hk) * hd]
     v = qkv[:, (hq + hk) * hd:]
-    npu.rope(q, hq, hd, positions=pos, theta=cfg.theta)
-    npu.rope(k, hk, hd, positions=pos, theta=cfg.theta)
+    npu.rope(qkv, hq + hk, hd, positions=pos, theta=cfg.theta)  # q and k heads are adjacent columns
     npu.kv_append(k, v, k_cache, v_cache, pos=pos)
     lens = sc.get("dlens", (B,), dtype=torch.int32, device=dev)
     torch.add(pos, 1, out=lens)
     ctx = npu.attention_decode(q, k_cache, v_cache, heads=hq, kv_heads=hk, lens=lens, ctx_len=ctx_max,
                                out=sc.get("dctx", (B, hq * hd), device=dev))
+    attn = npu.matmul(ctx, w.wo, w.so, out=sc.get("dattn", (B, d), device=dev))
+    tp.all_reduce(attn)
     h = sc.get("dh", (B, d), device=dev)
-    npu.matmul(ctx, w.wo, w.so, out=h, residual=x if tp.rank == 0 else None)
-    tp.all_reduce(h)
-    hn = npu.rmsnorm(h, w.g2, cfg.eps, out=sc.get("dhn", (B, d), device=dev))
+    hn, _ = npu.rmsnorm(attn, w.g2, cfg.eps, residual=x, residual_out=h, out=sc.get("dhn", (B, d), device=dev))
     gu = npu.matmul(hn, w.wgu, w.sgu, out=sc.get("dgu", (B, 2 * w.ffn), device=dev))
     a = npu.swiglu(gu, out=sc.get("dact", (B, w.ffn), device=dev))
+    ffn = npu.matmul(a, w.wd, w.sd, out=sc.get("dffn", (B, d), device=dev))
+    tp.all_reduce(ffn)
     y = out if out is not None else torch.empty((B, d), dtype=torch.float16, device=dev)
-    npu.matmul(a, w.wd, w.sd, out=y, residual=h if tp.rank == 0 else None)
-    tp.all_reduce(y)
+    npu.add(ffn, h, out=y)
     return y
 
 

@@ -24,7 +24,7 @@ from . import _lib
 from ._lib import NpubError  # noqa: F401  (re-exported)
 
 __all__ = [
-    "fp16", "quantize_w8", "matmul", "rmsnorm", "swiglu", "softmax", "rope", "attention",
+    "fp16", "quantize_w8", "matmul", "rmsnorm", "add", "swiglu", "softmax", "rope", "attention",
     "attention_decode", "kv_append", "isa_vector", "f32_to_f16_bits", "f16_bits_to_f32", "NpubError",
 ]
 
@@ -158,6 +158,19 @@ def rmsnorm(x: torch.Tensor, gamma: torch.Tensor, eps: float = 1e-5, *, residual
     _lib.call("npub_rmsnorm", x.data_ptr(), ldx, _ptr(residual), ldr, _ptr(residual_out), ldxo, gamma.data_ptr(),
               out.data_ptr(), ldy, rows, d, float(eps), _stream())
     return out if residual is None else (out, residual_out)
+
+
+def add(a: torch.Tensor, b: torch.Tensor, *, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out = fp16(a + b), the residual add of llama_layer.py:139,152 (fp16 [rows, cols])."""
+    lda = _mat(a, "a", torch.float16)
+    ldb = _mat(b, "b", torch.float16)
+    _need(a.shape == b.shape, "a and b must have the same shape")
+    rows, cols = a.shape
+    if out is None:
+        out = torch.empty((rows, cols), dtype=torch.float16, device=a.device)
+    ldo = _mat(out, "out", torch.float16)
+    _lib.call("npub_add", a.data_ptr(), lda, b.data_ptr(), ldb, out.data_ptr(), ldo, rows, cols, _stream())
+    return out
 
 
 def swiglu(g: torch.Tensor, u: Optional[torch.Tensor] = None, *, out: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -101,3 +101,11 @@ def test_rope_positions_tensor(cuda_device, rng):
     xt = dev(x, cuda_device)
     nb.rope(xt, H, hd, positions=dev(pos, cuda_device))
     assert ref.rel_err(xt.float().cpu().numpy(), ref.rope_ref(x, H, hd, pos)) <= TOL
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 4096), (33, 1000)])
+def test_residual_add(cuda_device, rng, rows, cols):
+    a = rng.standard_normal((rows, cols)).astype(np.float16)
+    b = rng.standard_normal((rows, cols)).astype(np.float16)
+    got = nb.add(dev(a, cuda_device), dev(b, cuda_device)).cpu().numpy()
+    assert np.array_equal(got, (a.astype(np.float32) + b.astype(np.float32)).astype(np.float16))  # exact

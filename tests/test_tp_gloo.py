@@ -57,19 +57,16 @@ def partial_layer(x, W, rank, size, tp):
         ctx[:, h * hd:(h + 1) * hd] = P @ v[:, kv * hd:(kv + 1) * hd]
     o = rg["o"][0]
     h_part = ctx @ W["o"][o.start:o.stop]
-    if rank == 0:
-        h_part = h_part + x            # rank 0 folds the residual in (as the GPU layer does)
     tp.all_reduce(h_part)
+    h_part = h_part + x                # residual after the reduction (as the GPU layer does)
     cols = torch.cat([torch.arange(r.start, r.stop) for r in rg["gu"]])
     gu = rms(h_part, W["g2"]) @ W["gu"][:, cols]
     f = c.ffn // size
     a = gu[:, :f] / (1 + torch.exp(-gu[:, :f])) * gu[:, f:]
     dr = rg["d"][0]
     y = a @ W["d"][dr.start:dr.stop]
-    if rank == 0:
-        y = y + h_part
     tp.all_reduce(y)
-    return y
+    return y + h_part
 
 
 def _worker(rank, size, port, q):
