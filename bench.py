@@ -1,20 +1,26 @@
 """Benchmark of the W8A16 / Llama-layer hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload layer|decode|gemm]
+                    [--workload stack|layer|decode|gemm]
 
-Default workload ("layer"): one Llama-7B-shaped decoder layer, prefill of one
-2048-token prompt (d 4096, 32 heads x 128, FFN 11008, RoPE theta 10000,
-causal attention), all seven linears W8A16 (int8 weights ~N(0, 0.02)
-quantised per output channel, fp16 activations ~N(0, 1), seeded).  A step is
-one pass of the layer; the metric is prefill tokens/s.  With --gpus N (under
-torchrun) the layer runs tensor-parallel over N GPUs with NCCL all-reduces
-(total work fixed: strong scaling).
+Default workload ("stack"): the 32-layer Llama-7B-shaped decoder (d 4096,
+32 heads x 128, FFN 11008, vocab 32000 fp16 lm_head, RoPE theta 10000), all
+seven linears of every layer W8A16 (int8 weights ~N(0, 0.02) quantised per
+output channel), random-init weights, 32 seeded prompts x 1024 tokens of
+prefill followed by 128 greedy decode steps.  A step is one prefill plus the
+128 decode steps; the metric is (prompt + generated) tokens per second.  With
+--gpus N under torchrun the stack runs tensor-parallel over N GPUs (NCCL
+all-reduces after the row-parallel projections; total work fixed: strong
+scaling).
+
+Other workloads: "layer" (one layer, prefill of a 2048-token prompt),
+"decode" (one layer, 64 sequences x 1 token over a 4096-token KV cache),
+"gemm" (the layer's gate|up W8A16 GEMM, 2048 x 22016 x 4096).
 
 Rank 0 prints one JSON line.  `roofline` covers the dominant kernel, the
-tcgen05 W8A16 GEMM, timed live with CUDA events on its launch stream.
+tcgen05 W8A16 GEMM, timed with CUDA events on its launch stream.
 `cpu_baseline` is the reference cmodel (mysim, built from the reference's
-_poc/mysim.cpp) or its C restatement, run on a bounded sample of the same
+_poc/mysim.cpp) or its C restatement, run on a bounded sample of the
 workload's GEMMs on this host's cores.
 """
 from __future__ import annotations
@@ -230,8 +236,8 @@ def run_ours(args):
         pos = torch.full((B,), ctx, dtype=torch.int32, device=dev)
         sc = llama.Scratch()
         y = torch.empty_like(x)
-        step = lambda: llama.layer_decode(x, w, cfg, kc, vc, pos, ctx_max=ctx + 1, tp=tp, scratch=sc,  # noqa: E731
-                                          out=y)
+        step = lambda ev=None: llama.layer_decode(x, w, cfg, kc, vc, pos, ctx_max=ctx + 1, tp=tp,  # noqa: E731
+                                                  scratch=sc, out=y, events=ev)
         units = float(B)
         unit = "tokens/s"
         config = {"workload": "llama7b_layer_decode_w8a16", "batch": B, "kv_len": ctx, "parallelism": f"tp{world}",
@@ -322,13 +328,13 @@ def run_ours(args):
     # host is ahead of the device and the events bracket device time only.
     reps = max(1, min(args.steps, 10))
     npu.gemm_events = []
-    evs = [] if wl == "layer" else None
+    evs = [] if wl in ("layer", "decode") else None
     for _ in range(reps):
         if flush is not None:
             flush.fill_(1.0)
         if graph is not None:
             graph.replay()
-        eager_step(evs) if wl == "layer" else eager_step()
+        eager_step(evs) if evs is not None else eager_step()
     torch.cuda.synchronize()
     gev = npu.gemm_events
     npu.gemm_events = None
@@ -391,9 +397,142 @@ def run_ours(args):
             out["layer_tflops"] = flops / (ms_per_step / 1e3) / 1e12
             out["layer_tensor_frac"] = out["layer_tflops"] * world / peak
         if wl == "decode":
+            out["breakdown_us"] = breakdown
             by = llama.decode_bytes(cfg, 64, 4097)
             out["hbm_gbs"] = by / world / (ms_per_step / 1e3) / 1e9
             out["hbm_frac"] = out["hbm_gbs"] / hbm
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
+def run_stack(args):
+    """The 32-layer Llama-7B-shaped W8A16 stack: 32 prompts x 1024 tokens of
+    prefill, then 128 greedy decode steps (one CUDA-graph replay each), tensor
+    parallel over the ranks.  A step is prefill + decode; the metric counts
+    prompt and generated tokens."""
+    import torch
+    sys.path.insert(0, HERE)
+    from npu_comp_b200 import llama, npu, _lib
+    rank, world, local = setup_dist(args.gpus)
+    dev = torch.device("cuda", local)
+    import torch.distributed as dist
+    tp = llama.TP(rank, world, dist.group.WORLD if world > 1 else None)
+    cfg = llama.LLAMA_7B
+    B, T, S = 32, 1024, 128
+    hbm, tf_burst, tf_sust, peak_src = _peaks()
+    w = llama.make_stack(cfg, seed=0, device=dev, tp=tp)
+    st = llama.LlamaStack(cfg, w, B, T, S, dev, tp)
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321)
+    prompts = torch.randint(0, cfg.vocab, (B, T), generator=g, device=dev, dtype=torch.int32)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        st.prefill(prompts)
+        st.decode(S)
+    torch.cuda.synchronize()
+    barrier()
+    c0 = _lib.launch_count()
+    st.prefill(prompts)
+    prefill_launches = _lib.launch_count() - c0
+    c0 = _lib.launch_count()
+    st._decode_step()
+    decode_launches = _lib.launch_count() - c0
+    torch.cuda.synchronize()
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    try:
+        smi_id = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+    except Exception:
+        smi_id = local
+    with ClockSampler(smi_id) as clk:
+        clk.wait_first_sample()
+        torch.cuda.synchronize()
+        barrier()
+        for i in range(args.steps):
+            ev[i][0].record()
+            st.prefill(prompts)
+            ev[i][1].record()
+            st.decode(S)
+            ev[i][2].record()
+        torch.cuda.synchronize()
+        barrier()
+    pre_ms = sum(e[0].elapsed_time(e[1]) for e in ev)
+    dec_ms = sum(e[1].elapsed_time(e[2]) for e in ev)
+    t = torch.tensor([pre_ms, dec_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    pre_ms, dec_ms = (float(v) / args.steps for v in t.tolist())
+    ms_per_step = pre_ms + dec_ms
+    tokens = B * (T + S)
+    value = tokens / (ms_per_step / 1e3)
+
+    # W8A16 GEMM roofline: the prefill's GEMM launches timed with CUDA events on their stream
+    npu.gemm_events = []
+    st.prefill(prompts)
+    torch.cuda.synchronize()
+    gev, npu.gemm_events = npu.gemm_events, None
+    g_ms = sum(a.elapsed_time(b) for a, b, _, i8 in gev if i8)
+    g_flops = sum(f for _, _, f, i8 in gev if i8)
+    g_n = sum(1 for *_, i8 in gev if i8)
+    achieved = g_flops / (g_ms / 1e3) / 1e12 if g_ms > 0 else None
+    roof = {"kernel": "w8a16_pair_kernel (tcgen05 cta_group::2 W8A16)", "bound": "tensor", "achieved": achieved,
+            "peak": tf_burst, "unit": "TFLOP/s", "frac": achieved / tf_burst if achieved else None,
+            "peak_source": f"{peak_src} bf16 dense (burst)", "launches_per_prefill": g_n,
+            "avg_launch_us": g_ms * 1e3 / g_n if g_n else None, "traffic": _traffic("stack"),
+            "share_of_prefill": g_ms / pre_ms if pre_ms else None}
+
+    # e2e: prompts from pinned host memory in, generated tokens back to the host
+    h_prompts = torch.empty((B, T), dtype=torch.int32, pin_memory=True)
+    h_prompts.copy_(prompts)
+    h_tokens = torch.empty((S + 1, B), dtype=torch.int32, pin_memory=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier()
+    e0.record()
+    for _ in range(args.steps):
+        prompts.copy_(h_prompts, non_blocking=True)
+        st.prefill(prompts)
+        st.decode(S, record=True)
+        h_tokens.copy_(torch.stack(st.tokens[-(S + 1):]), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+
+    out = None
+    if rank == 0:
+        flops = llama.stack_flops(cfg, B, T, S)
+        kv_read = sum(2 * B * cfg.kv_heads * (T + s + 1) * cfg.head_dim * 2 for s in range(S)) * cfg.layers
+        w_read = S * (cfg.layers * (cfg.d * (cfg.q_dim + 2 * cfg.kv_dim) + cfg.q_dim * cfg.d + 3 * cfg.d * cfg.ffn)
+                      + 2 * cfg.vocab * cfg.d)
+        out = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+               "vs_baseline": None, "dtype": "int8 x fp16 -> fp32 acc",
+               "data": "synthetic (seeded prompts; random-init weights)",
+               "config": {"workload": "llama7b_stack_w8a16", "layers": cfg.layers, "d": cfg.d, "heads": cfg.heads,
+                          "head_dim": cfg.head_dim, "ffn": cfg.ffn, "vocab": cfg.vocab, "batch": B,
+                          "prompt_len": T, "new_tokens": S, "parallelism": f"tp{world}",
+                          "l2": "inputs larger than L2 (6.5 GB int8 weights, 19 GB KV cache per step)"},
+               "prefill_ms": pre_ms, "decode_ms": dec_ms,
+               "prefill_tokens_per_s": B * T / (pre_ms / 1e3), "decode_tokens_per_s": B * S / (dec_ms / 1e3),
+               "stack_tflops": flops / (ms_per_step / 1e3) / 1e12,
+               "decode_hbm_gbs": (kv_read + w_read) / world / (dec_ms / 1e3) / 1e9,
+               "roofline": roof,
+               "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": B * T * 4,
+                       "d2h_bytes_per_step": (S + 1) * B * 4},
+               "gpu_launches": int((prefill_launches + S * decode_launches) * args.steps),
+               "clocks": clk.summary(), "launch": "decode steps replayed from a CUDA graph"
+               if st.graph is not None else "eager"}
+    st.release()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -406,7 +545,10 @@ def _scale_rate(flop_rate, workload):
     from npu_comp_b200.llama import LLAMA_7B, layer_flops
     if workload == "gemm":
         return flop_rate / 1e12, "TFLOP/s"
-    if workload == "decode":
+    if workload == "stack":
+        from npu_comp_b200.llama import stack_flops
+        per_tok = stack_flops(LLAMA_7B, 32, 1024, 128) / (32 * (1024 + 128))
+    elif workload == "decode":
         per_tok = layer_flops(LLAMA_7B, 1, 4097, causal=False)
     else:
         per_tok = layer_flops(LLAMA_7B, 2048, 2048) / 2048.0
@@ -416,14 +558,16 @@ def _scale_rate(flop_rate, workload):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default: 5 for the stack, 300 otherwise)")
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["layer", "decode", "gemm"], default="layer")
+    ap.add_argument("--workload", choices=["stack", "layer", "decode", "gemm"], default="stack")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch every op from the host instead of a CUDA graph")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.steps is None:
+        args.steps = 5 if args.workload == "stack" else 300
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", args.gpus))
 
@@ -446,11 +590,11 @@ def main():
                                  "sample": sample + " ; GEMM FLOP rate scaled by the layer's FLOPs per token"},
                 "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
                 "config": {"workload": {"layer": "llama7b_layer_prefill_w8a16", "decode": "llama7b_layer_decode_w8a16",
-                                        "gemm": "w8a16_gemm"}[args.workload]}}
+                                        "gemm": "w8a16_gemm", "stack": "llama7b_stack_w8a16"}[args.workload]}}
         print(json.dumps(line), flush=True)
         return 0
 
-    out = run_ours(args)
+    out = run_stack(args) if args.workload == "stack" else run_ours(args)
     if rank == 0 and out is not None:
         if not args.no_cpu_baseline and world == 1:
             rate, cores, kind, sample = cpu_reference_rate(all_cores=False)

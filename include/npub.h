@@ -148,6 +148,15 @@ int npub_softmax_rows(const void* s, void* p, int64_t ld, int64_t batch_stride, 
 int npub_rope(void* x, int64_t ldx, int tokens, int heads, int head_dim, const int32_t* positions, int pos0,
               float theta, void* stream);
 
+/* Token embedding and greedy selection around the layer stack (no counterpart
+ * in the reference, whose programs start from hidden states):
+ * npub_embed: out[r, :] = table[ids[r], :] (fp16, d % 8 == 0); ids outside
+ * [0, vocab) give zeros.  npub_argmax_rows: per row the largest logit
+ * (val, may be NULL) and its smallest index (idx). */
+int npub_embed(const int32_t* ids, int n, const void* table, int64_t ldt, int vocab, int d, void* out, int64_t ldo,
+               void* stream);
+int npub_argmax_rows(const void* x, int64_t ldx, int rows, int cols, int32_t* idx, float* val, void* stream);
+
 /* -------------------------------------------------------- attention ----
  * Causal prefill attention, llama_layer.py:114-137, legalize.py:117-127 for
  * every sequence b and head h: S = Q K^T * scale + mask; P = softmax(S); O = P V.

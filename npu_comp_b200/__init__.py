@@ -4,7 +4,7 @@ Llama-layer ops, behind an operator surface named after
 b_program_examples/npu.py.  Kernels live in libnpub.so (C ABI: include/npub.h).
 """
 from .npu import (  # noqa: F401
-    NpubError, add, attention, attention_decode, f16_bits_to_f32, f32_to_f16_bits, fp16, isa_vector, kv_append, matmul,
+    NpubError, add, argmax, attention, attention_decode, embed, f16_bits_to_f32, f32_to_f16_bits, fp16, isa_vector, kv_append, matmul,
     quantize_w8, rmsnorm, rope, softmax, swiglu,
 )
 

@@ -36,7 +36,8 @@ namespace npub {
 
 namespace pair {
 
-constexpr int kThreads = 256 + 128 * kPairConvGroups;
+template <int G>
+constexpr int threads_for() { return 256 + 128 * G; }
 constexpr int BK = kPairBK;       // K per stage
 constexpr int KCH = kPairKch;     // 64-wide swizzled chunks per stage
 constexpr int UMMA_K = 16;
@@ -91,12 +92,11 @@ __device__ __forceinline__ TileCoord tile_coord(const PairParams& p, int tile, i
     return c;
 }
 
-template <int BT, int STAGES, int CSTAGES>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+template <int BT, int STAGES, int CSTAGES, int G>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<G>(), 1)
     w8a16_pair_kernel(const __grid_constant__ PairParams p) {
     using L = Smem<BT, STAGES, CSTAGES>;
-    static_assert(STAGES % kPairConvGroups == 0 && CSTAGES >= kPairConvGroups && CSTAGES >= 2,
-                  "see kPairStages*: converter groups take turns");
+    static_assert(STAGES % G == 0 && CSTAGES >= G && CSTAGES >= 2, "see kPairStages*: converter groups take turns");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sB = smem;                            // STAGES x kBh   (1024-aligned)
@@ -248,7 +248,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int tile = cid; tile < p.n_tiles && ok; tile += ncl) {
             const TileCoord tc = tile_coord(p, tile, BT);
             for (int i = 0; i < tc.nk; ++i, ++g) {
-                if ((int)(g % kPairConvGroups) != grp) continue;
+                if ((int)(g % G) != grp) continue;
                 const int s = (int)(g % STAGES);
                 const uint32_t ph = (g / STAGES) & 1u;
                 const int c = (int)(g % CSTAGES);
@@ -342,11 +342,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------- host side
 
-template <int BT, int STAGES, int CSTAGES>
+template <int BT, int STAGES, int CSTAGES, int G>
 static int launch(const PairParams& p, int max_clusters, cudaStream_t st) {
     using L = Smem<BT, STAGES, CSTAGES>;
     static_assert(L::kTotal <= 232448, "shared memory budget");
-    auto kern = w8a16_pair_kernel<BT, STAGES, CSTAGES>;
+    auto kern = w8a16_pair_kernel<BT, STAGES, CSTAGES, G>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) {
         npub_internal_set_cuda_error(e);
@@ -354,23 +354,23 @@ static int launch(const PairParams& p, int max_clusters, cudaStream_t st) {
     }
     int clusters = p.n_tiles < max_clusters ? p.n_tiles : max_clusters;
     if (clusters < 1) clusters = 1;
-    kern<<<dim3(2 * clusters, 1, 1), kThreads, L::kTotal, st>>>(p);
+    kern<<<dim3(2 * clusters, 1, 1), threads_for<G>(), L::kTotal, st>>>(p);
     return npub_internal_launch_status();
 }
 
 static std::mutex g_mu;
 static int g_max_clusters[64][3];
 
-template <int BT, int STAGES, int CSTAGES>
+template <int BT, int STAGES, int CSTAGES, int G>
 static int max_clusters_for(int dev, int slot) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (g_max_clusters[dev][slot] > 0) return g_max_clusters[dev][slot];
     using L = Smem<BT, STAGES, CSTAGES>;
-    auto kern = w8a16_pair_kernel<BT, STAGES, CSTAGES>;
+    auto kern = w8a16_pair_kernel<BT, STAGES, CSTAGES, G>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * 256, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(threads_for<G>(), 1, 1);
     cfg.dynamicSmemBytes = L::kTotal;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
@@ -399,7 +399,7 @@ int pair_splits(int tiles, int k_tiles, int clusters) {
     double best_t = 1e30;
     for (int s = 1; s <= 16 && k_tiles / s >= 4; ++s) {
         const int waves = (tiles * s + clusters - 1) / clusters;
-        const double t = waves * ((double)k_tiles / s + 8.0) + (s > 1 ? 2.0 + 0.5 * s : 0.0);
+        const double t = waves * ((double)k_tiles / s + 3.0) + (s > 1 ? 1.0 + 0.25 * s : 0.0);
         if (t < best_t - 1e-9) {
             best_t = t;
             best = s;
@@ -417,9 +417,9 @@ static int cur_device() {
 static int clusters_for_bt(int bt) {
     const int dev = cur_device();
     switch (bt) {
-        case 64: return pair::max_clusters_for<64, kPairStages64, kPairCStages>(dev, 0);
-        case 128: return pair::max_clusters_for<128, kPairStages128, kPairCStages>(dev, 1);
-        default: return pair::max_clusters_for<256, kPairStages256, kPairCStages>(dev, 2);
+        case 64: return pair::max_clusters_for<64, kPairStages64, kPairCStages64, kPairGroups64>(dev, 0);
+        case 128: return pair::max_clusters_for<128, kPairStages128, kPairCStages, kPairConvGroups>(dev, 1);
+        default: return pair::max_clusters_for<256, kPairStages256, kPairCStages, kPairConvGroups>(dev, 2);
     }
 }
 
@@ -448,9 +448,9 @@ int w8a16_pair_run(PairParams& p, int M, int N, int K, cudaStream_t st) {
     p.n_tiles = p.n_apairs * p.n_btiles * p.splits;
     p.err = npub_internal_device_error_word();
     switch (bt) {
-        case 64: return pair::launch<64, kPairStages64, kPairCStages>(p, clusters, st);
-        case 128: return pair::launch<128, kPairStages128, kPairCStages>(p, clusters, st);
-        default: return pair::launch<256, kPairStages256, kPairCStages>(p, clusters, st);
+        case 64: return pair::launch<64, kPairStages64, kPairCStages64, kPairGroups64>(p, clusters, st);
+        case 128: return pair::launch<128, kPairStages128, kPairCStages, kPairConvGroups>(p, clusters, st);
+        default: return pair::launch<256, kPairStages256, kPairCStages, kPairConvGroups>(p, clusters, st);
     }
 }
 

@@ -23,7 +23,13 @@ namespace npub {
 #define NPUB_PAIR_STAGES128 5
 #endif
 #ifndef NPUB_PAIR_STAGES64
-#define NPUB_PAIR_STAGES64 6
+#define NPUB_PAIR_STAGES64 4
+#endif
+#ifndef NPUB_PAIR_CSTAGES64
+#define NPUB_PAIR_CSTAGES64 4
+#endif
+#ifndef NPUB_PAIR_GROUPS64
+#define NPUB_PAIR_GROUPS64 2
 #endif
 #ifndef NPUB_PAIR_CSTAGES
 #define NPUB_PAIR_CSTAGES 2
@@ -36,6 +42,11 @@ constexpr int kPairStages128 = NPUB_PAIR_STAGES128;
 constexpr int kPairStages64 = NPUB_PAIR_STAGES64;
 constexpr int kPairCStages = NPUB_PAIR_CSTAGES;
 constexpr int kPairConvGroups = NPUB_PAIR_CONV_GROUPS;  // converter groups of 4 warps (alternate K steps)
+// Skinny (decode) tiles: the tensor core finishes a stage quickly, so the
+// int8 -> fp16 conversion hand-off is the critical path; more converted stages
+// and two converter groups keep it off.
+constexpr int kPairCStages64 = NPUB_PAIR_CSTAGES64;
+constexpr int kPairGroups64 = NPUB_PAIR_GROUPS64;
 #ifndef NPUB_PAIR_KCH
 #define NPUB_PAIR_KCH 2
 #endif

@@ -275,6 +275,59 @@ __global__ void rope_vec_kernel(__half* x, int64_t ldx, int heads, int hd, const
     }
 }
 
+// ------------------------------------------------------------ embedding / argmax
+// out[r, :] = table[ids[r], :]; ids outside [0, vocab) give a zero row.
+__global__ void embed_kernel(const int32_t* __restrict__ ids, const __half* __restrict__ table, int64_t ldt,
+                             int vocab, int d, __half* __restrict__ out, int64_t ldo) {
+    const int r = blockIdx.x;
+    const int id = ids[r];
+    const bool ok = id >= 0 && id < vocab;
+    const uint4* src = reinterpret_cast<const uint4*>(table + (int64_t)(ok ? id : 0) * ldt);
+    uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)r * ldo);
+    for (int c = threadIdx.x; c < d / kVec; c += blockDim.x) dst[c] = ok ? src[c] : make_uint4(0, 0, 0, 0);
+}
+
+// Row argmax over fp16 logits: the largest value and its smallest index.
+__global__ void argmax_kernel(const __half* __restrict__ x, int64_t ldx, int cols, int32_t* __restrict__ idx,
+                              float* __restrict__ val) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const __half* row = x + (int64_t)blockIdx.x * ldx;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+        const float v = __half2float(row[c]);
+        if (v > best || (v == best && c < bi)) {
+            best = v;
+            bi = c;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) {
+            best = ov;
+            bi = oi;
+        }
+    }
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) {
+        sv[w] = best;
+        si[w] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int i = 1; i < (int)(blockDim.x >> 5); ++i)
+            if (sv[i] > best || (sv[i] == best && si[i] < bi)) {
+                best = sv[i];
+                bi = si[i];
+            }
+        idx[blockIdx.x] = bi;
+        if (val) val[blockIdx.x] = best;
+    }
+}
+
 // ------------------------------------------------------------ quantiser
 // W [K, N] fp32 -> Wq [N, K] int8 + s [N] fp16.  One CTA per 32 columns:
 // pass 1 column absmax (coalesced over n), pass 2 writes K-major rows via smem.
@@ -460,5 +513,26 @@ extern "C" int npub_add(const void* a, int64_t lda, const void* b, int64_t ldb, 
                                                                                     cols);
     else
         add_scalar_kernel<<<grid_for((int64_t)rows * cols, 256), 256, 0, st>>>(ah, lda, bh, ldb, oh, ldo, rows, cols);
+    return npub_internal_launch_status();
+}
+
+extern "C" int npub_embed(const int32_t* ids, int n, const void* table, int64_t ldt, int vocab, int d, void* out,
+                          int64_t ldo, void* stream) {
+    NPUB_CHECK_ARG(n >= 0);
+    if (n == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(ids && table && out && vocab > 0 && d > 0 && d % kVec == 0 && ldt >= d && ldo >= d);
+    NPUB_CHECK_ARG(ldt % kVec == 0 && ldo % kVec == 0 && npub_aligned(table, 16) && npub_aligned(out, 16));
+    embed_kernel<<<n, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        ids, reinterpret_cast<const __half*>(table), ldt, vocab, d, reinterpret_cast<__half*>(out), ldo);
+    return npub_internal_launch_status();
+}
+
+extern "C" int npub_argmax_rows(const void* x, int64_t ldx, int rows, int cols, int32_t* idx, float* val,
+                                void* stream) {
+    NPUB_CHECK_ARG(rows >= 0);
+    if (rows == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(x && idx && cols > 0 && ldx >= cols);
+    argmax_kernel<<<rows, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(reinterpret_cast<const __half*>(x), ldx,
+                                                                           cols, idx, val);
     return npub_internal_launch_status();
 }

@@ -266,7 +266,7 @@ def _store_prompt_kv(k, v, kv_out, batch, T, hk, hd):
 
 def layer_decode(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, k_cache: torch.Tensor, v_cache: torch.Tensor,
                  pos: torch.Tensor, *, ctx_max: int, tp: TP = TP(), scratch: Optional[Scratch] = None,
-                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                 out: Optional[torch.Tensor] = None, events: Optional[list] = None) -> torch.Tensor:
     """One decode step: x [B, d] holds one new token per sequence at positions
     pos [B] (int32); its K/V are appended to the caches, attention covers
     positions 0..pos[b]."""
@@ -275,27 +275,41 @@ def layer_decode(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, k_cache: to
     B, d = x.shape
     hd = cfg.head_dim
     hq, hk = w.heads, w.kv_heads
+    mk = _Marks(events)
+    mk("rmsnorm")
     xn = npu.rmsnorm(x, w.g1, cfg.eps, out=sc.get("dxn", (B, d), device=dev))
+    mk("qkv_gemm")
     qkv = npu.matmul(xn, w.wqkv, w.sqkv, out=sc.get("dqkv", (B, (hq + 2 * hk) * hd), device=dev))
     q = qkv[:, : hq * hd]
     k = qkv[:, hq * hd:(hq + hk) * hd]
     v = qkv[:, (hq + hk) * hd:]
+    mk("rope_kv_append")
     npu.rope(qkv, hq + hk, hd, positions=pos, theta=cfg.theta)  # q and k heads are adjacent columns
     npu.kv_append(k, v, k_cache, v_cache, pos=pos)
     lens = sc.get("dlens", (B,), dtype=torch.int32, device=dev)
     torch.add(pos, 1, out=lens)
+    mk("attention")
     ctx = npu.attention_decode(q, k_cache, v_cache, heads=hq, kv_heads=hk, lens=lens, ctx_len=ctx_max,
                                out=sc.get("dctx", (B, hq * hd), device=dev))
+    mk("o_gemm")
     attn = npu.matmul(ctx, w.wo, w.so, out=sc.get("dattn", (B, d), device=dev))
+    mk("all_reduce")
     tp.all_reduce(attn)
+    mk("rmsnorm")
     h = sc.get("dh", (B, d), device=dev)
     hn, _ = npu.rmsnorm(attn, w.g2, cfg.eps, residual=x, residual_out=h, out=sc.get("dhn", (B, d), device=dev))
+    mk("gate_up_gemm")
     gu = npu.matmul(hn, w.wgu, w.sgu, out=sc.get("dgu", (B, 2 * w.ffn), device=dev))
+    mk("swiglu")
     a = npu.swiglu(gu, out=sc.get("dact", (B, w.ffn), device=dev))
+    mk("down_gemm")
     ffn = npu.matmul(a, w.wd, w.sd, out=sc.get("dffn", (B, d), device=dev))
+    mk("all_reduce")
     tp.all_reduce(ffn)
+    mk("residual")
     y = out if out is not None else torch.empty((B, d), dtype=torch.float16, device=dev)
     npu.add(ffn, h, out=y)
+    mk.end()
     return y
 
 
@@ -320,3 +334,153 @@ def decode_bytes(cfg: LlamaConfig, batch: int, ctx: int) -> float:
 
 def softmax_scale(cfg: LlamaConfig) -> float:
     return 1.0 / math.sqrt(cfg.head_dim)
+
+
+# ---------------------------------------------------------------------------
+# The full decoder stack: embedding -> L layers -> final RMSNorm -> lm_head ->
+# greedy argmax.  Prefill runs all prompts of a batch at once and fills the
+# per-layer KV caches; decode appends one token per sequence per step.
+
+
+@dataclass
+class StackWeights:
+    layers: List[LayerWeights]
+    embed: torch.Tensor      # fp16 [vocab, d], replicated on every rank
+    norm: torch.Tensor       # fp16 [d]
+    lm_head: torch.Tensor    # fp16 [vocab / tp, d]: this rank's vocabulary rows (K-major for the GEMM)
+    vocab_off: int
+
+
+def make_stack(cfg: LlamaConfig, seed: int, device, tp: TP = TP(), layers: Optional[int] = None) -> StackWeights:
+    """Random-init Llama-shaped stack: W8A16 layers (make_layer), an fp16 embedding
+    table ~N(0, 1) and an fp16 lm_head ~N(0, 0.02) split over the vocabulary."""
+    n_layers = cfg.layers if layers is None else layers
+    if cfg.vocab % tp.size:
+        raise ValueError(f"tp={tp.size} must divide the vocabulary {cfg.vocab}")
+    lw = [make_layer(cfg, seed + 1000 * (i + 1), device, tp) for i in range(n_layers)]
+    gen = torch.Generator(device=device)
+    gen.manual_seed(int(seed) + 7)
+    embed = torch.randn((cfg.vocab, cfg.d), generator=gen, device=device).half()
+    lm = torch.randn((cfg.vocab, cfg.d), generator=gen, device=device) * 0.02
+    vs = cfg.vocab // tp.size
+    lm_shard = lm[tp.rank * vs:(tp.rank + 1) * vs].half().contiguous()
+    del lm
+    return StackWeights(lw, embed, torch.ones(cfg.d, dtype=torch.float16, device=device), lm_shard, tp.rank * vs)
+
+
+class LlamaStack:
+    """A batch of `batch` sequences through the stack on this rank.
+
+    prefill(prompts [B, T] int32) fills the KV caches and returns the first
+    generated token of every sequence; decode(steps) generates `steps` more,
+    replaying one CUDA graph per step (token ids and positions stay on the
+    device, so the host only launches the graph)."""
+
+    def __init__(self, cfg: LlamaConfig, w: StackWeights, batch: int, prompt_len: int, max_new: int, device,
+                 tp: TP = TP(), use_graph: bool = True):
+        self.cfg, self.w, self.tp, self.dev = cfg, w, tp, device
+        self.B, self.T = batch, prompt_len
+        self.cap = prompt_len + max_new + 1
+        hk = cfg.kv_heads // tp.size
+        kv_shape = (batch, hk, self.cap, cfg.head_dim)
+        self.kc = [torch.zeros(kv_shape, dtype=torch.float16, device=device) for _ in w.layers]
+        self.vc = [torch.zeros(kv_shape, dtype=torch.float16, device=device) for _ in w.layers]
+        self.sc = Scratch()
+        self.ids = torch.zeros((batch,), dtype=torch.int32, device=device)
+        self.pos = torch.zeros((batch,), dtype=torch.int32, device=device)
+        self.tokens: List[torch.Tensor] = []
+        self.use_graph = use_graph
+        self.graph = None
+        self.positions = torch.arange(prompt_len, device=device, dtype=torch.int32).repeat(batch)
+
+    # -- greedy selection over the (possibly vocab-sharded) lm_head
+    def _next_ids(self, xl: torch.Tensor) -> None:
+        cfg, w, tp, sc = self.cfg, self.w, self.tp, self.sc
+        B = xl.shape[0]
+        hn = npu.rmsnorm(xl, w.norm, cfg.eps, out=sc.get("fn", (B, cfg.d), device=self.dev))
+        logits = npu.matmul(hn, w.lm_head, out=sc.get("logits", (B, w.lm_head.shape[0]), device=self.dev))
+        idx, val = npu.argmax(logits, idx=sc.get("amax_i", (B,), torch.int32, self.dev),
+                              val=sc.get("amax_v", (B,), torch.float32, self.dev))
+        if tp.size == 1:
+            self.ids.copy_(idx)
+            return
+        import torch.distributed as dist
+        gidx = sc.get("amax_g", (B,), torch.int32, self.dev)
+        torch.add(idx, w.vocab_off, out=gidx)
+        all_v = sc.get("all_v", (tp.size * B,), torch.float32, self.dev)
+        all_i = sc.get("all_i", (tp.size * B,), torch.int32, self.dev)
+        dist.all_gather_into_tensor(all_v, val, group=tp.group)
+        dist.all_gather_into_tensor(all_i, gidx, group=tp.group)
+        # shards hold ascending vocabulary ranges: the first maximal rank has the smallest index
+        best = torch.argmax(all_v.view(tp.size, B), dim=0)
+        self.ids.copy_(torch.gather(all_i.view(tp.size, B), 0, best.view(1, B)).view(B))
+
+    def prefill(self, prompts: torch.Tensor) -> torch.Tensor:
+        cfg, B, T = self.cfg, self.B, self.T
+        x = npu.embed(prompts.reshape(-1), self.w.embed, out=self.sc.get("px0", (B * T, cfg.d), device=self.dev))
+        bufs = (x, self.sc.get("px1", (B * T, cfg.d), device=self.dev))
+        for i, lw in enumerate(self.w.layers):
+            y = bufs[(i + 1) % 2]
+            layer_prefill(bufs[i % 2], lw, cfg, batch=B, tp=self.tp, positions=self.positions,
+                          kv_out=(self.kc[i], self.vc[i]), scratch=self.sc, out=y)
+        last = bufs[len(self.w.layers) % 2].view(B, T, cfg.d)[:, T - 1]
+        xl = self.sc.get("xlast", (B, cfg.d), device=self.dev)
+        xl.copy_(last)
+        self._next_ids(xl)
+        self.pos.fill_(T)
+        self.tokens = [self.ids.clone()]
+        return self.ids
+
+    def _decode_step(self) -> None:
+        cfg, B = self.cfg, self.B
+        x = npu.embed(self.ids, self.w.embed, out=self.sc.get("dx0", (B, cfg.d), device=self.dev))
+        bufs = (x, self.sc.get("dx1", (B, cfg.d), device=self.dev))
+        for i, lw in enumerate(self.w.layers):
+            layer_decode(bufs[i % 2], lw, cfg, self.kc[i], self.vc[i], self.pos, ctx_max=self.cap, tp=self.tp,
+                         scratch=self.sc, out=bufs[(i + 1) % 2])
+        self._next_ids(bufs[len(self.w.layers) % 2])
+        self.pos.add_(1)
+
+    def _capture(self) -> None:
+        ids0, pos0 = self.ids.clone(), self.pos.clone()
+        side = torch.cuda.Stream(device=self.dev)
+        side.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(side):  # warm-up outside capture (allocations, first-launch set-up)
+            self._decode_step()
+        torch.cuda.current_stream(self.dev).wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._decode_step()
+        self.ids.copy_(ids0)
+        self.pos.copy_(pos0)
+        self.graph = g
+
+    def decode(self, steps: int, record: bool = False) -> None:
+        if self.use_graph and self.graph is None:
+            try:
+                self._capture()
+            except Exception:
+                self.graph = None
+                self.use_graph = False
+        for _ in range(steps):
+            if self.graph is not None:
+                self.graph.replay()
+            else:
+                self._decode_step()
+            if record:
+                self.tokens.append(self.ids.clone())
+
+    def release(self) -> None:
+        """Drop the CUDA graph (it may hold collectives) before the process group ends."""
+        self.graph = None
+
+
+def stack_flops(cfg: LlamaConfig, batch: int, prompt_len: int, new_tokens: int, layers: Optional[int] = None) -> float:
+    """Algorithmic FLOPs of prefill + greedy decode of the stack (layers and lm_head)."""
+    L = cfg.layers if layers is None else layers
+    pre = L * batch * layer_flops(cfg, prompt_len, prompt_len) + 2.0 * batch * cfg.d * cfg.vocab
+    dec = 0.0
+    for s in range(new_tokens):
+        ctx = prompt_len + s + 1
+        dec += L * batch * layer_flops(cfg, 1, ctx, causal=False) + 2.0 * batch * cfg.d * cfg.vocab
+    return pre + dec

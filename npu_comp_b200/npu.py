@@ -25,7 +25,7 @@ from ._lib import NpubError  # noqa: F401  (re-exported)
 
 __all__ = [
     "fp16", "quantize_w8", "matmul", "rmsnorm", "add", "swiglu", "softmax", "rope", "attention",
-    "attention_decode", "kv_append", "isa_vector", "f32_to_f16_bits", "f16_bits_to_f32", "NpubError",
+    "attention_decode", "kv_append", "embed", "argmax", "isa_vector", "f32_to_f16_bits", "f16_bits_to_f32", "NpubError",
 ]
 
 
@@ -222,6 +222,33 @@ def rope(x: torch.Tensor, heads: int, head_dim: int, *, pos0: int = 0, positions
         pos_ptr = positions.data_ptr()
     _lib.call("npub_rope", x.data_ptr(), ldx, tokens, heads, head_dim, pos_ptr, int(pos0), float(theta), _stream())
     return x
+
+
+# ------------------------------------------------------- embedding / argmax
+
+def embed(ids: torch.Tensor, table: torch.Tensor, *, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Rows of the fp16 embedding table [vocab, d] for int32 token ids [n]."""
+    _need(ids.is_cuda and ids.dtype == torch.int32 and ids.is_contiguous(), "ids must be contiguous int32 CUDA")
+    ldt = _mat(table, "table", torch.float16)
+    vocab, d = table.shape
+    n = ids.numel()
+    if out is None:
+        out = torch.empty((n, d), dtype=torch.float16, device=table.device)
+    ldo = _mat(out, "out", torch.float16)
+    _lib.call("npub_embed", ids.data_ptr(), n, table.data_ptr(), ldt, vocab, d, out.data_ptr(), ldo, _stream())
+    return out
+
+
+def argmax(x: torch.Tensor, *, idx: Optional[torch.Tensor] = None, val: Optional[torch.Tensor] = None):
+    """Per-row (index, value) of the largest fp16 logit (smallest index on ties)."""
+    ldx = _mat(x, "x", torch.float16)
+    rows, cols = x.shape
+    if idx is None:
+        idx = torch.empty((rows,), dtype=torch.int32, device=x.device)
+    if val is None:
+        val = torch.empty((rows,), dtype=torch.float32, device=x.device)
+    _lib.call("npub_argmax_rows", x.data_ptr(), ldx, rows, cols, idx.data_ptr(), val.data_ptr(), _stream())
+    return idx, val
 
 
 # ----------------------------------------------------------------- attention

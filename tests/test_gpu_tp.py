@@ -1,0 +1,77 @@
+"""Tensor-parallel Llama layer on 2 GPUs (NCCL) against the 1-GPU layer.
+
+Each rank builds its shard of the same seeded layer (llama.make_layer with
+TP(rank, 2)), runs prefill and a decode step, and rank 0 compares with the
+unsharded layer run on its GPU.  Skipped when fewer than 2 GPUs are visible.
+Tolerance: normwise relative error <= 1e-2 (the all-reduce sums fp16 partials
+in a different order than the single-GPU accumulation)."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    import datetime
+    import torch.distributed as dist
+    from npu_comp_b200 import llama
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        cfg = llama.LlamaConfig(d=1024, heads=8, kv_heads=4, head_dim=128, ffn=2752, eps=1e-5)
+        tp = llama.TP(rank, world, dist.group.WORLD)
+        w = llama.make_layer(cfg, seed=11, device=dev, tp=tp)
+        g = torch.Generator(device=dev).manual_seed(3)
+        B, T = 2, 192
+        x = torch.randn((B * T, cfg.d), generator=g, device=dev).half()
+        hk = cfg.kv_heads // world
+        kc = torch.zeros((B, hk, 256, cfg.head_dim), dtype=torch.float16, device=dev)
+        vc = torch.zeros_like(kc)
+        y = llama.layer_prefill(x, w, cfg, batch=B, tp=tp, kv_out=(kc, vc))
+        xd = torch.randn((B, cfg.d), generator=g, device=dev).half()
+        pos = torch.full((B,), T, dtype=torch.int32, device=dev)
+        yd = llama.layer_decode(xd, w, cfg, kc, vc, pos, ctx_max=T + 1, tp=tp)
+        torch.cuda.synchronize()
+        if rank == 0:
+            w1 = llama.make_layer(cfg, seed=11, device=dev)
+            kc1 = torch.zeros((B, cfg.kv_heads, 256, cfg.head_dim), dtype=torch.float16, device=dev)
+            vc1 = torch.zeros_like(kc1)
+            y1 = llama.layer_prefill(x, w1, cfg, batch=B, kv_out=(kc1, vc1))
+            yd1 = llama.layer_decode(xd, w1, cfg, kc1, vc1, pos, ctx_max=T + 1)
+            e = ((y.float() - y1.float()).abs().max() / y1.float().abs().max()).item()
+            ed = ((yd.float() - yd1.float()).abs().max() / yd1.float().abs().max()).item()
+            q.put((e, ed))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_layer_matches_single_gpu():
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    e, ed = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert e <= TOL, e
+    assert ed <= TOL, ed
