@@ -233,14 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 if (!ok) break;
                 tc_fence_after();
                 uint32_t sv[64];
-                {
-                    uint32_t (&lo)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[0]);
-                    uint32_t (&hi)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[32]);
-                    const uint32_t sa = tmem + lane_off + (uint32_t)(s * 128 + col0);
-                    tmem_ld32_nowait(sa, lo);
-                    tmem_ld32_nowait(sa + 32u, hi);
-                    tmem_wait_ld();
-                }
+                tmem_ld64(tmem + lane_off + (uint32_t)(s * 128 + col0), sv);
                 // the S buffer can be overwritten by S_{j+2} once every warp has read it
                 tc_fence_before();
                 __syncwarp();
@@ -304,14 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 if (!ok) break;
                 tc_fence_after();
                 uint32_t ov[64];
-                {
-                    uint32_t (&lo)[32] = *reinterpret_cast<uint32_t(*)[32]>(&ov[0]);
-                    uint32_t (&hi)[32] = *reinterpret_cast<uint32_t(*)[32]>(&ov[32]);
-                    const uint32_t oa = tmem + lane_off + 256u + (uint32_t)(s * 128 + col0);
-                    tmem_ld32_nowait(oa, lo);
-                    tmem_ld32_nowait(oa + 32u, hi);
-                    tmem_wait_ld();
-                }
+                tmem_ld64(tmem + lane_off + 256u + (uint32_t)(s * 128 + col0), ov);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&o_free[s]);

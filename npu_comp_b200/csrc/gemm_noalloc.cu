@@ -11,11 +11,15 @@
 // fixed-size array in the library's own device globals instead.
 //
 // The array lives in every device that loads the library until the process
-// exits.  Every call shares it and it keeps the last call's contents; the
-// split-K partials are fully overwritten before they are read, so nothing
-// has to be cleared.  Calls that overlap on the GPU (different streams, or
+// exits.  Every call shares it and it keeps the last call's contents.  Its
+// first kSkinnyCounterBytes hold the tile counters of the few-token (M <= 64)
+// kernel, which start at zero (the array is zero-initialised when the module
+// loads) and which every completed call leaves at zero; nothing else is ever
+// written there.  The rest holds split-K partials, fully overwritten before
+// they are read.  Calls that overlap on the GPU (different streams, or
 // different host threads on the same device) race on the array.
 #include "common.cuh"
+#include "gemm_w8a16_skinny.h"
 
 #include <mutex>
 
@@ -55,11 +59,16 @@ extern "C" int npub_w8a16_gemm_noalloc(const void* A, int64_t lda, const int8_t*
                                        float alpha, void* stream) {
     if (M < 0 || N < 0 || K < 0) return NPUB_ERR_INVALID_ARG;
     const size_t need = npub_w8a16_gemm_workspace(M, N, K);
-    if (need > (size_t)NPUB_NOALLOC_SCRATCH_BYTES) return NPUB_ERR_SCRATCH_LIMIT;
+    // Few-token calls take the array from its start (counters first); split-K
+    // partials of other calls start after the counter region.
+    const bool skinny = npub::w8a16_skinny_fits(M, N);
+    const size_t off = skinny ? 0 : npub::kSkinnyCounterBytes;
+    if (need > (size_t)NPUB_NOALLOC_SCRATCH_BYTES - off) return NPUB_ERR_SCRATCH_LIMIT;
     void* ws = nullptr;
     if (need > 0) {
         const int rc = noalloc_scratch(&ws);
         if (rc != NPUB_OK) return rc;
+        ws = static_cast<unsigned char*>(ws) + off;
     }
     return npub_w8a16_gemm(A, lda, Wq, ldw, scale, C, ldc, R, ldr, M, N, K, alpha, ws, need, stream);
 }

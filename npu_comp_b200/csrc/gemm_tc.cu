@@ -23,6 +23,7 @@
 #include "common.cuh"
 #include "gemm_tc.h"
 #include "gemm_w8a16_pair.h"
+#include "gemm_w8a16_skinny.h"
 
 #include <cudaTypedefs.h>
 
@@ -415,7 +416,7 @@ int run_gemm(GemmParams& p, bool a_int8, int bt, int grid_x, int grid_y, int bat
 // Aop = weights [N, K] (128-row side), Bop = activations [M, K] (token side).
 static size_t linear_workspace(int M, int N, int K, bool w_int8) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
-    if (w_int8) return w8a16_pair_workspace(M, N, K);
+    if (w_int8) return w8a16_skinny_fits(M, N) ? w8a16_skinny_workspace(M, N, K) : w8a16_pair_workspace(M, N, K);
     const int bt = pick_bt(M);
     const int tiles = ((N + BM - 1) / BM) * ((M + bt - 1) / bt);
     const int k_tiles = (K + BK - 1) / BK;
@@ -477,6 +478,8 @@ static int linear(bool w_int8, const void* A, int64_t lda, const void* W, int64_
     NPUB_CHECK_ARG(ldc >= N);
     NPUB_CHECK_ARG(!R || ldr >= N);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (w_int8 && w8a16_skinny_fits(M, N))
+        return w8a16_skinny_run(A, lda, W, ldw, scale, C, ldc, R, ldr, M, N, K, alpha, ws, ws_bytes, st);
     if (w_int8) return linear_w8a16_pair(A, lda, W, ldw, scale, C, ldc, R, ldr, M, N, K, alpha, ws, ws_bytes, st);
 
     GemmParams p;

@@ -1,0 +1,562 @@
+// W8A16 GEMM for few tokens (M <= 64: decode steps), HBM-bound on the int8
+// weight stream.
+//
+//   C[t, n] = fp16( alpha * scale[n] * sum_k A[t, k] * Wq[n, k] )  (+ R[t, n])
+//
+// D = Wq * A^T is computed in 128-row weight tiles (the MMA's M side) against
+// all M tokens at once (the MMA's N side, BT = 32 or 64 columns).  The design
+// follows from the weight stream being the whole cost:
+//
+//  * stream-K: the (tile, 128-wide K step) units are cut into one contiguous
+//    range per CTA, grid = SM count, so every SM streams the same number of
+//    weight bytes whatever N / 128 is.  A tile cut between CTAs is finished by
+//    whichever of its CTAs arrives last on the tile's counter (one counter per
+//    32-row quarter, so each epilogue warp works alone): every piece stores an
+//    fp32 partial, and the last one sums the pieces in CTA order -- a fixed
+//    order, so results do not depend on timing.  No CTA waits on another.
+//  * a CTA works on its cut tiles first (the head of its last tile, then the
+//    tail of its first) and on its whole tiles after, so the partial-sum
+//    round trips through L2 overlap the main loop instead of ending it.
+//  * the converted weights never touch shared memory: converter warps read
+//    the int8 tile (128-byte swizzled, conflict-free), turn it into fp16 in
+//    registers and store it into tensor memory with tcgen05.st, where the
+//    MMA reads it as the A operand (tcgen05.mma with A in TMEM).  Shared
+//    memory carries only the TMA traffic.
+//  * an int8 stage is released as soon as it is converted, not when the MMA
+//    is done with it, so the 8-deep int8 ring (128 KB) is all TMA in flight;
+//    the token ring (L2-resident data, read by every CTA) is 6-8 deep.
+//
+// Roles (512 threads):
+//   warp 0      TMA producer, int8 weights (ring of kS8 x 16 KB)
+//   warp 1      TMEM allocator; MMA issuer
+//   warp 2      TMA producer, fp16 tokens (ring of ST x BT x 128 x 2 B)
+//   warps 4-7   epilogue: TMEM -> scale / residual -> fp16, or fp32 partials
+//   warps 8-15  converters, two groups of four warps taking K steps in turn
+//
+// The tile counters fill the first kSkinnyCounterBytes of the workspace, the
+// same bytes whatever the shape, so they are never overwritten by partials of
+// another call.  They must be zero before the first call on a workspace and
+// every completed call leaves them zero (the last piece of a tile resets its
+// counter).
+//
+// Reference semantics: the NPU matmul (_poc/mysim.cpp:109-113,
+// b_program_examples/npu.py:41-47) with float32 accumulation and an fp16 store.
+#include "common.cuh"
+#include "gemm_tc.h"
+#include "gemm_w8a16_skinny.h"
+
+namespace npub {
+
+namespace skinny {
+
+constexpr int kThreads = 512;
+constexpr int kRows = 128;   // weight rows per tile (MMA M)
+constexpr int kBK = 128;     // K per unit (one 128-byte swizzled int8 row)
+constexpr int kS8 = 8;       // int8 ring depth
+constexpr int kSA = 4;       // fp16 weight stages in TMEM (kBK / 2 columns each)
+constexpr int kGroups = 2;   // converter groups
+constexpr int kAcols = kBK / 2;
+constexpr int kAcol0 = 128;  // first TMEM column of the A stages (accumulators use [0, 2 BT))
+constexpr uint32_t kTmemCols = 512;
+static_assert(kS8 % kGroups == 0 && kSA % kGroups == 0, "converter groups take alternate K steps");
+static_assert(kAcol0 + kSA * kAcols <= (int)kTmemCols, "tensor memory budget");
+
+template <int BT>
+struct Smem {
+    static constexpr int kST = BT == 32 ? 8 : 6;  // token ring depth
+    static constexpr int kTokChunk = BT * 128;    // 64 fp16 of K for BT tokens
+    static constexpr int kTok = 2 * kTokChunk;
+    static constexpr int kA8 = kRows * kBK;
+    static constexpr int kBars = 8 * (2 * kS8 + 2 * kST + 2 * kSA + 4) + 16;
+    static constexpr int kTotal = kST * kTok + kS8 * kA8 + kBars + 1024;
+};
+
+__device__ __forceinline__ uint32_t perm_lo(uint32_t u) { return __byte_perm(u, 0x64646464u, 0x5140); }
+__device__ __forceinline__ uint32_t perm_hi(uint32_t u) { return __byte_perm(u, 0x64646464u, 0x5342); }
+__device__ __forceinline__ uint32_t sub1152(uint32_t h) {
+    __half2 v = *reinterpret_cast<__half2*>(&h);
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+    __half2 r = __hsub2(v, bias);
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+// 16 int8 -> 8 fp16 pairs (even K in the low half), exact: (q ^ 0x80) placed in
+// the mantissa of 1024.0, minus 1152.
+__device__ __forceinline__ void cvt16(uint4 raw, uint32_t* o) {
+    const uint32_t w0 = raw.x ^ 0x80808080u, w1 = raw.y ^ 0x80808080u, w2 = raw.z ^ 0x80808080u,
+                   w3 = raw.w ^ 0x80808080u;
+    o[0] = sub1152(perm_lo(w0));
+    o[1] = sub1152(perm_hi(w0));
+    o[2] = sub1152(perm_lo(w1));
+    o[3] = sub1152(perm_hi(w1));
+    o[4] = sub1152(perm_lo(w2));
+    o[5] = sub1152(perm_hi(w2));
+    o[6] = sub1152(perm_lo(w3));
+    o[7] = sub1152(perm_hi(w3));
+}
+
+// 32 lanes x 32 columns of 32 bit from registers into tensor memory.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    __syncwarp();  // .sync.aligned: the whole warp, converged
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+        "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+        "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+        "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+    __syncwarp();
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16, A K-major in tensor memory
+// (one row per lane, two fp16 per 32-bit column).
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// L2 (.cg) float4 store / load of the fp32 partials.  Volatile asm with a
+// memory clobber: the loads of other CTAs' partials must stay behind the
+// counter check and the fence that precede them (the compiler treats a
+// plain asm load as free to move).
+__device__ __forceinline__ void st_cg_f4(float4* ptr, float4 v) {
+    asm volatile("st.global.cg.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ float4 ld_cg_f4(const float4* ptr) {
+    float4 v;
+    asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(ptr)
+                 : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void set_err(int* err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
+
+// Units [start(c), start(c+1)) belong to CTA c; owner(u) inverts that.
+__device__ __forceinline__ int64_t unit_start(int64_t c, int64_t U, int64_t G) { return c * U / G; }
+__device__ __forceinline__ int64_t unit_owner(int64_t u, int64_t U, int64_t G) { return ((u + 1) * G - 1) / U; }
+
+// The segments of one CTA's unit range: one per tile it touches.
+struct Range {
+    int64_t u0, u1;
+    int KT, tA, tB, nseg;
+    bool cutA, cutB;  // first / last tile only partly in the range
+};
+
+__device__ __forceinline__ Range make_range(int64_t u0, int64_t u1, int KT) {
+    Range r;
+    r.u0 = u0;
+    r.u1 = u1;
+    r.KT = KT;
+    r.tA = (int)(u0 / KT);
+    r.tB = (int)((u1 - 1) / KT);
+    r.nseg = u1 > u0 ? r.tB - r.tA + 1 : 0;
+    r.cutA = u0 != (int64_t)r.tA * KT || u1 < (int64_t)(r.tA + 1) * KT;
+    r.cutB = r.nseg >= 2 && u1 != (int64_t)(r.tB + 1) * KT;
+    return r;
+}
+
+struct Seg {
+    int tile, k0, nk;  // K steps [k0, k0 + nk) of the tile
+    bool full;         // the whole tile: finished here, no partial
+    bool first;        // the range's first tile (partial slot 0, else 1)
+};
+
+// i-th segment in processing order: the cut last tile, the cut first tile,
+// then the whole tiles in order.
+__device__ __forceinline__ Seg seg_in_order(const Range& r, int i) {
+    int t;
+    const int lead = (r.cutB ? 1 : 0) + (r.cutA ? 1 : 0);
+    if (i < lead) {
+        t = (r.cutB && i == 0) ? r.tB : r.tA;
+    } else {
+        t = r.tA + (r.cutA ? 1 : 0) + (i - lead);
+    }
+    Seg s;
+    s.tile = t;
+    const int64_t ts = (int64_t)t * r.KT, te = ts + r.KT;
+    const int64_t a = r.u0 > ts ? r.u0 : ts, b = r.u1 < te ? r.u1 : te;
+    s.k0 = (int)(a - ts);
+    s.nk = (int)(b - a);
+    s.full = s.nk == r.KT;
+    s.first = t == r.tA;
+    return s;
+}
+
+template <int BT>
+__global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_constant__ SkinnyParams p) {
+    using L = Smem<BT>;
+    constexpr int kST = L::kST;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sTok = smem;                      // kST x kTok (1024-aligned)
+    uint8_t* sA8 = sTok + kST * L::kTok;       // kS8 x kA8  (1024-aligned)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sA8 + kS8 * L::kA8);
+    uint64_t* full8 = bars;                    // [kS8] int8 tile landed
+    uint64_t* empty8 = full8 + kS8;            // [kS8] int8 tile converted (4 warps)
+    uint64_t* tok_full = empty8 + kS8;         // [kST] token tile landed
+    uint64_t* tok_empty = tok_full + kST;      // [kST] MMA done with the token tile
+    uint64_t* a_full = tok_empty + kST;        // [kSA] fp16 weights in TMEM (4 warps)
+    uint64_t* a_empty = a_full + kSA;          // [kSA] MMA done with the TMEM stage
+    uint64_t* acc_full = a_empty + kSA;        // [2] accumulator ready
+    uint64_t* acc_empty = acc_full + 2;        // [2] epilogue drained the accumulator (4 warps)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int KT = p.k_steps;
+    const int64_t U = (int64_t)p.n_tiles * KT, G = gridDim.x;
+    const Range rg = make_range(unit_start(blockIdx.x, U, G), unit_start((int64_t)blockIdx.x + 1, U, G), KT);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kS8; ++s) {
+            mbar_init(&full8[s], 1);
+            mbar_init(&empty8[s], 4);
+        }
+        for (int s = 0; s < kST; ++s) {
+            mbar_init(&tok_full[s], 1);
+            mbar_init(&tok_empty[s], 1);
+        }
+        for (int s = 0; s < kSA; ++s) {
+            mbar_init(&a_full[s], 4);
+            mbar_init(&a_empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&p.tmW);
+        prefetch_tmap(&p.tmX);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    int never = 0;
+    volatile int* no_abort = &never;
+
+    if (warp == 0 || warp == 2) {
+        // ------------------------------------------------------------ producers
+        if (lane == 0) {
+            const bool weights = warp == 0;
+            const int depth = weights ? kS8 : kST;
+            uint64_t* full = weights ? full8 : tok_full;
+            uint64_t* empty = weights ? empty8 : tok_empty;
+            uint32_t g = 0;
+            bool ok = true;
+            for (int i = 0; i < rg.nseg && ok; ++i) {
+                const Seg sg = seg_in_order(rg, i);
+                for (int j = 0; j < sg.nk; ++j, ++g) {
+                    const int k = (sg.k0 + j) * kBK;
+                    const int s = (int)(g % (uint32_t)depth);
+                    const uint32_t ph = (g / (uint32_t)depth) & 1u;
+                    if (*abort_flag || !mbar_wait_bounded(&empty[s], ph ^ 1u, abort_flag)) {
+                        *abort_flag = 1;
+                        set_err(p.err, weights ? 0x301 : 0x302);
+                        ok = false;
+                        break;
+                    }
+                    if (weights) {
+                        mbar_arrive_expect_tx(&full[s], (uint32_t)L::kA8);
+                        tma_load_3d(sA8 + s * L::kA8, &p.tmW, &full[s], k, sg.tile * kRows, 0);
+                    } else {
+                        mbar_arrive_expect_tx(&full[s], (uint32_t)L::kTok);
+                        tma_load_3d(sTok + s * L::kTok, &p.tmX, &full[s], k, 0, 0);
+                        tma_load_3d(sTok + s * L::kTok + L::kTokChunk, &p.tmX, &full[s], k + 64, 0, 0);
+                    }
+                }
+            }
+            // Every load issued has landed before the CTA may exit.
+            for (uint32_t j = 0; j < (uint32_t)depth && j < g; ++j) {
+                const uint32_t gg = g - 1 - j;
+                if (!mbar_wait_bounded(&full[gg % (uint32_t)depth], (gg / (uint32_t)depth) & 1u, no_abort,
+                                       200000000ull))
+                    set_err(p.err, 0x303);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_f16(kRows, BT);
+            uint32_t g = 0;
+            bool ok = true;
+            for (int t = 0; t < rg.nseg && ok; ++t) {
+                const Seg sg = seg_in_order(rg, t);
+                const uint32_t b = (uint32_t)t & 1u, bph = ((uint32_t)t >> 1) & 1u;
+                if (!mbar_wait_bounded(&acc_empty[b], bph ^ 1u, abort_flag)) {
+                    ok = false;
+                    set_err(p.err, 0x304);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t dcol = tmem + b * (uint32_t)BT;
+                for (int i = 0; i < sg.nk; ++i, ++g) {
+                    const int sa = (int)(g % kSA), st = (int)(g % kST);
+                    if (!mbar_wait_bounded(&a_full[sa], (g / kSA) & 1u, abort_flag) ||
+                        !mbar_wait_bounded(&tok_full[st], (g / kST) & 1u, abort_flag)) {
+                        ok = false;
+                        set_err(p.err, 0x305);
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t acol = tmem + (uint32_t)(kAcol0 + sa * kAcols);
+                    const uint32_t bbase = smem_u32(sTok + st * L::kTok);
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        const uint32_t baddr = bbase + (uint32_t)((kk >> 2) * L::kTokChunk + (kk & 3) * 32);
+                        tc_mma_f16_ts(dcol, acol + (uint32_t)(kk * 8), umma_desc_sw128(baddr), idesc,
+                                      (i > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    tc_commit(&a_empty[sa]);
+                    tc_commit(&tok_empty[st]);
+                }
+                if (!ok) break;
+                tc_commit(&acc_full[b]);
+            }
+            if (!ok) *abort_flag = 1;
+        }
+    } else if (warp >= 8) {
+        // ------------------------------------------------------------ converters
+        const int grp = (warp - 8) >> 2;
+        const int q = warp & 3;  // TMEM lane quadrant of this warp
+        const int row = 32 * q + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+        const int64_t total = rg.u1 - rg.u0;
+        for (uint32_t g = (uint32_t)grp; (int64_t)g < total; g += kGroups) {
+            const int s8 = (int)(g % kS8), sa = (int)(g % kSA);
+            if (!mbar_wait_bounded(&full8[s8], (g / kS8) & 1u, abort_flag) ||
+                !mbar_wait_bounded(&a_empty[sa], ((g / kSA) & 1u) ^ 1u, abort_flag)) {
+                *abort_flag = 1;
+                set_err(p.err, 0x306);
+                break;
+            }
+            tc_fence_after();
+            const uint8_t* src = sA8 + s8 * L::kA8 + row * kBK;
+            uint4 raw[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                raw[j] = *reinterpret_cast<const uint4*>(src + ((j ^ (row & 7)) << 4));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty8[s8]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint32_t r[32];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) cvt16(raw[4 * h + j], &r[8 * j]);
+                tmem_st32(lane_base + (uint32_t)(kAcol0 + sa * kAcols + 32 * h), r);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&a_full[sa]);
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3;
+        const int r = 32 * q + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+        const int M = p.M;
+        for (int t = 0; t < rg.nseg; ++t) {
+            const Seg sg = seg_in_order(rg, t);
+            const uint32_t b = (uint32_t)t & 1u, bph = ((uint32_t)t >> 1) & 1u;
+            const int n = sg.tile * kRows + r;
+            const bool nrow = n < p.N;
+            // the scale load is in flight while the accumulator is waited for
+            const float sc = p.alpha * ((p.scale && nrow) ? __half2float(__ldg(p.scale + n)) : 1.0f);
+            bool have = mbar_wait_bounded(&acc_full[b], bph, abort_flag);
+            if (!have) set_err(p.err, 0x307);
+            have = __all_sync(0xffffffffu, have);
+            if (!have) {
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            if (sg.full) {
+                for (int c0 = 0; c0 < BT && c0 < M; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(lane_base + b * (uint32_t)BT + (uint32_t)c0, v);
+                    if (!nrow) continue;
+                    float rv[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        rv[j] = (p.R && c0 + j < M) ? __half2float(__ldg(p.R + (int64_t)(c0 + j) * p.ldr + n)) : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (c0 + j < M) p.C[(int64_t)(c0 + j) * p.ldc + n] = __float2half_rn(v[j] * sc + rv[j]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[b]);
+                continue;
+            }
+            // A piece of a tile shared with other CTAs: store the fp32 partial,
+            // [slot][row][BT], one 16-column chunk of this row per float4 x 4.
+            const int64_t slot = 2 * (int64_t)blockIdx.x + (sg.first ? 0 : 1);
+            float4* mine = reinterpret_cast<float4*>(p.part + (slot * kRows + r) * BT);
+            for (int c0 = 0; c0 < BT && c0 < M; c0 += 16) {
+                float v[16];
+                tmem_ld16(lane_base + b * (uint32_t)BT + (uint32_t)c0, v);
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    st_cg_f4(mine + c0 / 4 + j, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
+            const int64_t c_first = unit_owner((int64_t)sg.tile * KT, U, G);
+            const int64_t c_last = unit_owner((int64_t)sg.tile * KT + KT - 1, U, G);
+            __threadfence();
+            __syncwarp();
+            unsigned old = 0;
+            if (lane == 0) old = atomicAdd(p.cnt + 4 * sg.tile + q, 1u);
+            old = __shfl_sync(0xffffffffu, old, 0);
+            if (old != (unsigned)(c_last - c_first)) continue;
+            // Last piece in: sum every piece in CTA order, finish the rows.
+            __threadfence();
+            if (lane == 0) p.cnt[4 * sg.tile + q] = 0u;  // left zero for the next call
+            for (int c0 = 0; c0 < BT && c0 < M; c0 += 16) {
+                float4 acc[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int64_t c = c_first; c <= c_last; c += 2) {
+                    // two pieces' loads in flight before either is added
+                    const bool two = c + 1 <= c_last;
+                    const int64_t sl0 = 2 * c + (unit_start(c, U, G) / KT == sg.tile ? 0 : 1);
+                    const int64_t sl1 = two ? 2 * (c + 1) + (unit_start(c + 1, U, G) / KT == sg.tile ? 0 : 1) : sl0;
+                    const float4* p0 = reinterpret_cast<const float4*>(p.part + (sl0 * kRows + r) * BT) + c0 / 4;
+                    const float4* p1 = reinterpret_cast<const float4*>(p.part + (sl1 * kRows + r) * BT) + c0 / 4;
+                    float4 x0[4], x1[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        x0[j] = ld_cg_f4(p0 + j);
+                        x1[j] = ld_cg_f4(p1 + j);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        acc[j].x += x0[j].x;
+                        acc[j].y += x0[j].y;
+                        acc[j].z += x0[j].z;
+                        acc[j].w += x0[j].w;
+                    }
+                    if (two) {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            acc[j].x += x1[j].x;
+                            acc[j].y += x1[j].y;
+                            acc[j].z += x1[j].z;
+                            acc[j].w += x1[j].w;
+                        }
+                    }
+                }
+                if (!nrow) continue;
+                const float v[16] = {acc[0].x, acc[0].y, acc[0].z, acc[0].w, acc[1].x, acc[1].y, acc[1].z, acc[1].w,
+                                     acc[2].x, acc[2].y, acc[2].z, acc[2].w, acc[3].x, acc[3].y, acc[3].z, acc[3].w};
+                float rv[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    rv[j] = (p.R && c0 + j < M) ? __half2float(__ldg(p.R + (int64_t)(c0 + j) * p.ldr + n)) : 0.0f;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (c0 + j < M) p.C[(int64_t)(c0 + j) * p.ldc + n] = __float2half_rn(v[j] * sc + rv[j]);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+template <int BT>
+static int launch(const SkinnyParams& p, int grid, cudaStream_t st) {
+    using L = Smem<BT>;
+    static_assert(L::kTotal <= 232448, "shared memory budget");
+    auto kern = w8a16_skinny_kernel<BT>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+    if (e != cudaSuccess) {
+        npub_internal_set_cuda_error(e);
+        return NPUB_ERR_CUDA;
+    }
+    kern<<<grid, kThreads, L::kTotal, st>>>(p);
+    return npub_internal_launch_status();
+}
+
+}  // namespace skinny
+
+int skinny_bt(int M) { return M <= 32 ? 32 : 64; }
+
+static int skinny_grid(int N, int K) {
+    const int64_t units = (int64_t)((N + skinny::kRows - 1) / skinny::kRows) * ((K + skinny::kBK - 1) / skinny::kBK);
+    const int sms = num_sms();
+    return (int)(units < sms ? units : sms);
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+bool w8a16_skinny_fits(int M, int N) {
+    return M > 0 && M <= kSkinnyMaxM && N > 0 &&
+           (size_t)4 * ((N + skinny::kRows - 1) / skinny::kRows) * sizeof(unsigned) <= kSkinnyCounterBytes;
+}
+
+size_t w8a16_skinny_workspace(int M, int N, int K) {
+    if (!w8a16_skinny_fits(M, N) || K <= 0) return 0;
+    return kSkinnyCounterBytes + (size_t)2 * skinny_grid(N, K) * skinny_bt(M) * skinny::kRows * sizeof(float);
+}
+
+int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C, int64_t ldc,
+                     const void* R, int64_t ldr, int M, int N, int K, float alpha, void* ws, size_t ws_bytes,
+                     cudaStream_t st) {
+    if (!w8a16_skinny_fits(M, N)) return NPUB_ERR_INVALID_ARG;
+    const size_t need = w8a16_skinny_workspace(M, N, K);
+    if (!ws || ws_bytes < need) return NPUB_ERR_WORKSPACE;
+    if (!npub_aligned(ws, 16)) return NPUB_ERR_INVALID_ARG;
+    const int bt = skinny_bt(M);
+    SkinnyParams p;
+    memset(&p, 0, sizeof(p));
+    int rc = make_tmap_3d(&p.tmW, true, W, (uint64_t)K, (uint64_t)N, 1, (uint64_t)ldw, (uint64_t)ldw * N,
+                          skinny::kRows, 1, true, skinny::kBK);
+    if (rc) return rc;
+    rc = make_tmap_3d(&p.tmX, false, A, (uint64_t)K, (uint64_t)M, 1, (uint64_t)lda, (uint64_t)lda * M, (uint32_t)bt,
+                      1, true);
+    if (rc) return rc;
+    p.M = M;
+    p.N = N;
+    p.k_steps = (K + skinny::kBK - 1) / skinny::kBK;
+    p.n_tiles = (N + skinny::kRows - 1) / skinny::kRows;
+    p.C = reinterpret_cast<__half*>(C);
+    p.ldc = ldc;
+    p.R = reinterpret_cast<const __half*>(R);
+    p.ldr = ldr;
+    p.scale = reinterpret_cast<const __half*>(scale);
+    p.alpha = alpha;
+    p.cnt = reinterpret_cast<unsigned*>(ws);
+    p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kSkinnyCounterBytes);
+    p.err = npub_internal_device_error_word();
+    const int grid = skinny_grid(N, K);
+    return bt == 32 ? skinny::launch<32>(p, grid, st) : skinny::launch<64>(p, grid, st);
+}
+
+}  // namespace npub

@@ -1,0 +1,41 @@
+// Internal interface of the stream-K W8A16 GEMM for few tokens
+// (gemm_w8a16_skinny.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace npub {
+
+// Token counts up to this use the stream-K kernel (one token tile, BT = 32 or 64).
+constexpr int kSkinnyMaxM = 64;
+
+struct SkinnyParams {
+    CUtensorMap tmW;  // int8 weights [N, K]: box {128, 128, 1}, 128-byte swizzle
+    CUtensorMap tmX;  // fp16 activations [M, K]: box {64, BT, 1}, 128-byte swizzle
+    int M, N, k_steps, n_tiles;
+    __half* C;
+    int64_t ldc;
+    const __half* R;
+    int64_t ldr;
+    const __half* scale;
+    float alpha;
+    float* part;    // [2 x grid][BT][128] fp32 partial tiles
+    unsigned* cnt;  // [n_tiles][4] pieces arrived per tile and 32-row quarter (zero between calls)
+    int* err;
+};
+
+// Tile counters at the start of every workspace of this kernel: a fixed
+// region (never partial sums), 4 per 128-row tile, so N <= 524288.
+constexpr size_t kSkinnyCounterBytes = 64 << 10;
+
+// Whether (M, N) runs on the stream-K kernel.
+bool w8a16_skinny_fits(int M, int N);
+size_t w8a16_skinny_workspace(int M, int N, int K);
+int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C, int64_t ldc,
+                     const void* R, int64_t ldr, int M, int N, int K, float alpha, void* ws, size_t ws_bytes,
+                     cudaStream_t st);
+
+}  // namespace npub

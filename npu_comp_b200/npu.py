@@ -67,6 +67,30 @@ def _workspace(nbytes: int, device) -> Tuple[Optional[torch.Tensor], int]:
     return ws[off:off + nbytes], nbytes
 
 
+# The few-token W8A16 kernel (M <= 64) keeps tile counters in the first 64 KiB
+# of its workspace; they must start at zero and every call leaves them at zero.
+# One zero-filled buffer per (device, stream) serves all such calls and
+# nothing else; a grown buffer replaces the old one, which is kept alive for
+# CUDA graphs that captured its address.
+_SKINNY_MAX_M = 64
+_SKINNY_COUNTER_BYTES = 64 << 10
+_zeroed_ws = {}
+_retired_ws = []
+
+
+def _zeroed_workspace(nbytes: int, device) -> Tuple[Optional[torch.Tensor], int]:
+    if nbytes <= 0:
+        return None, 0
+    key = (device.index if device.index is not None else torch.cuda.current_device(), _stream())
+    buf = _zeroed_ws.get(key)
+    if buf is None or buf.numel() < nbytes:
+        if buf is not None:
+            _retired_ws.append(buf)
+        buf = torch.zeros(max(nbytes, 4 << 20), dtype=torch.uint8, device=device)
+        _zeroed_ws[key] = buf
+    return buf, buf.numel()
+
+
 # -------------------------------------------------------------- W8A16 matmul
 
 # When a list, every matmul() call appends (start_event, end_event, flops, int8)
@@ -118,7 +142,10 @@ def matmul(A: torch.Tensor, W: torch.Tensor, scale: Optional[torch.Tensor] = Non
         _need(tuple(residual.shape) == (M, N), "residual must be [M, N]")
     int8 = W.dtype == torch.int8
     wsq = "npub_w8a16_gemm_workspace" if int8 else "npub_f16_gemm_workspace"
-    ws, wsb = _workspace(_lib.query(wsq, M, N, K), A.device)
+    if int8 and M <= _SKINNY_MAX_M and (N + 127) // 128 * 16 <= _SKINNY_COUNTER_BYTES:
+        ws, wsb = _zeroed_workspace(_lib.query(wsq, M, N, K), A.device)
+    else:
+        ws, wsb = _workspace(_lib.query(wsq, M, N, K), A.device)
     fn = "npub_w8a16_gemm" if int8 else "npub_f16_gemm"
     ev = gemm_events
     if ev is not None:

@@ -101,21 +101,28 @@ def test_batched_prefill_equals_single_prompts(cuda_device):
         assert e <= 2e-3
 
 
-def test_decode_step_matches_prefill(cuda_device):
-    """Prefill of T tokens filling the KV cache, then one decode step for token
-    T, equals row T of a prefill over T+1 tokens."""
+def test_decode_step_matches_reference_and_prefill(cuda_device):
+    """Llama-7B layer: prefill of T = 127 tokens per sequence fills the KV cache,
+    then one decode step for token T.  The decode row must match row T of the
+    float64 layer reference over T + 1 tokens (TOL), and row T of a GPU prefill
+    over T + 1 tokens (two fp16 paths, each within TOL of the reference: 2 TOL)."""
+    rng = np.random.default_rng(5)
     cfg = llama.LLAMA_7B
-    w = llama.make_layer(cfg, seed=5, device=cuda_device)
-    g = torch.Generator(device=cuda_device).manual_seed(4)
-    B, T = 2, 300
-    x = torch.randn((B * (T + 1), cfg.d), generator=g, device=cuda_device).half()
-    full = llama.layer_prefill(x, w, cfg, batch=B).float().view(B, T + 1, cfg.d)
-    kc = torch.zeros((B, cfg.kv_heads, 512, cfg.head_dim), dtype=torch.float16, device=cuda_device)
+    W = random_float_layer(cfg, rng)
+    w = llama.layer_from_float(cfg, W, cuda_device)
+    B, T = 2, 127
+    x = rng.standard_normal((B, T + 1, cfg.d)).astype(np.float16)
+    xt = torch.from_numpy(x).to(cuda_device)
+    full = llama.layer_prefill(xt.reshape(B * (T + 1), cfg.d), w, cfg, batch=B).float().view(B, T + 1, cfg.d)
+    kc = torch.zeros((B, cfg.kv_heads, 256, cfg.head_dim), dtype=torch.float16, device=cuda_device)
     vc = torch.zeros_like(kc)
-    xp = x.view(B, T + 1, cfg.d)[:, :T].reshape(B * T, cfg.d).contiguous()
-    llama.layer_prefill(xp, w, cfg, batch=B, kv_out=(kc, vc))
-    xd = x.view(B, T + 1, cfg.d)[:, T].contiguous()
+    llama.layer_prefill(xt[:, :T].reshape(B * T, cfg.d).contiguous(), w, cfg, batch=B, kv_out=(kc, vc))
     pos = torch.full((B,), T, dtype=torch.int32, device=cuda_device)
-    yd = llama.layer_decode(xd, w, cfg, kc, vc, pos, ctx_max=T + 1).float()
+    yd = llama.layer_decode(xt[:, T].contiguous(), w, cfg, kc, vc, pos, ctx_max=T + 1).float()
+    cos, sin = ref.rope_tables(T + 1, cfg.head_dim)
+    qw = ref.quantized_weights(W, cfg.heads, cfg.kv_heads)
+    for b in range(B):
+        yr = ref.ref_layer(qw, x[b], cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.eps, cos, sin)[T]
+        assert ref.rel_err(yd[b].cpu().numpy(), yr) <= TOL
     e = ((yd - full[:, T]).abs().max() / full[:, T].abs().max()).item()
-    assert e <= TOL
+    assert e <= 2 * TOL

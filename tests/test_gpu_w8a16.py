@@ -51,7 +51,8 @@ def test_quantizer_bit_exact(cuda_device, rng, K, N):
 
 
 SHAPES = [(64, 512, 512), (1, 1000, 256), (8, 64, 64), (128, 128, 64), (200, 300, 160), (129, 257, 96),
-          (333, 777, 1024), (64, 12288, 4096), (64, 4096, 1376), (512, 256, 11008), (2048, 4096, 4096)]
+          (333, 777, 1024), (64, 12288, 4096), (64, 4096, 1376), (512, 256, 11008), (2048, 4096, 4096),
+          (32, 22016, 4096), (48, 1000, 4096), (16, 11008, 512), (64, 4096, 11008), (3, 128, 16)]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
@@ -89,6 +90,71 @@ def test_w8a16_exact_known_answer(cuda_device, rng):
     C = nb.matmul(to_dev(A, cuda_device), to_dev(q, cuda_device), to_dev(s, cuda_device)).cpu().numpy()
     exact = ref.w8a16_ref(A, q, s)
     assert np.array_equal(C, exact.astype(np.float16))
+
+
+@pytest.mark.parametrize("M,N,K", [(40, 1000, 4096), (64, 384, 11008), (7, 4096, 128)])
+def test_w8a16_decode_exact_known_answer(cuda_device, rng, M, N, K):
+    """Decode shapes (M <= 64) run the stream-K kernel, whose tiles are cut
+    between CTAs and summed from fp32 partials.  With small integers every
+    partial sum is an exact fp32 integer, so any cut must give the exact value."""
+    A = rng.integers(-3, 4, (M, K)).astype(np.float16)
+    q = rng.integers(-4, 5, (N, K)).astype(np.int8)
+    s = (2.0 ** rng.integers(-12, -6, N)).astype(np.float16)
+    R = rng.integers(-8, 9, (M, N)).astype(np.float16)
+    C = nb.matmul(to_dev(A, cuda_device), to_dev(q, cuda_device), to_dev(s, cuda_device),
+                  residual=to_dev(R, cuda_device)).cpu().numpy()
+    exact = ref.w8a16_ref(A, q, s, residual=R)
+    assert np.array_equal(C, exact.astype(np.float16))
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 12288, 4096), (32, 22016, 4096), (64, 4096, 11008)])
+def test_w8a16_decode_repeatable(cuda_device, M, N, K):
+    """Tiles cut between CTAs are summed by whichever piece arrives last; the
+    sum must not depend on which one that was, nor race with the pieces'
+    stores: eight back-to-back calls give the same bits, within tolerance."""
+    g = torch.Generator(device=cuda_device).manual_seed(M + N)
+    q = torch.randint(-127, 128, (N, K), generator=g, device=cuda_device, dtype=torch.int8)
+    s = (torch.rand(N, generator=g, device=cuda_device) * 1e-3 + 1e-3).half()
+    A = torch.randn((M, K), generator=g, device=cuda_device).half()
+    ref = (A.float() @ q.float().t()) * s.float()[None, :]
+    first = nb.matmul(A, q, s)
+    assert ((first.float() - ref).abs().max() / ref.abs().max()).item() <= TOL
+    for _ in range(7):
+        assert torch.equal(nb.matmul(A, q, s), first)
+
+
+def test_w8a16_decode_shapes_share_one_workspace(cuda_device):
+    """A decode layer's GEMMs (different N and K) run back to back on one
+    workspace: the tile counters of one shape must not be disturbed by another
+    shape's partial sums.  Run the sequence twice."""
+    g = torch.Generator(device=cuda_device).manual_seed(9)
+    shapes = [(2, 1024, 512), (2, 512, 512), (2, 2752, 512), (2, 512, 1376), (5, 300, 4096), (64, 130, 256)]
+    mats = []
+    for M, N, K in shapes:
+        q = torch.randint(-127, 128, (N, K), generator=g, device=cuda_device, dtype=torch.int8)
+        s = (torch.rand(N, generator=g, device=cuda_device) * 1e-3 + 1e-3).half()
+        A = torch.randn((M, K), generator=g, device=cuda_device).half()
+        mats.append((A, q, s, (A.float() @ q.float().t()) * s.float()[None, :]))
+    for _ in range(2):
+        for A, q, s, ref in mats:
+            C = nb.matmul(A, q, s).float()
+            assert ((C - ref).abs().max() / ref.abs().max()).item() <= TOL
+
+
+def test_w8a16_decode_strided_alpha(cuda_device, rng):
+    M, N, K = 20, 700, 1024
+    A = rng.standard_normal((M, K)).astype(np.float16)
+    q = rng.integers(-127, 128, (N, K)).astype(np.int8)
+    s = (rng.uniform(0.5, 2, N) * 1e-3).astype(np.float16)
+    R = rng.standard_normal((M, N)).astype(np.float16)
+    out = torch.zeros((M, N + 40), dtype=torch.float16, device=cuda_device)[:, 16:16 + N]
+    nb.matmul(to_dev(A, cuda_device), to_dev(q, cuda_device), to_dev(s, cuda_device), out=out,
+              residual=to_dev(R, cuda_device), alpha=0.25)
+    got = out.float().cpu().numpy()
+    assert ref.rel_err(got, ref.w8a16_ref(A, q, s, residual=R, alpha=0.25)) <= TOL
+    full = torch.zeros((M, N + 40), dtype=torch.float16, device=cuda_device)
+    full[:, 16:16 + N] = out
+    assert not full[:, :16].any() and not full[:, 16 + N:].any()  # nothing written outside the view
 
 
 def test_w8a16_split_k_deterministic(cuda_device, rng):
