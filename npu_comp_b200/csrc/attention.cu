@@ -58,6 +58,7 @@ struct DecodeArgs {
     int heads, kv_heads, splits, chunk;
     float scale_log2;  // scale * log2(e)
     float* part;       // [bh, splits, hd + 2] when splits > 1
+    int* err;          // device error word
 };
 
 __device__ __forceinline__ void ld8f(const __half* p, float (&f)[8]) {
@@ -187,6 +188,249 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_attn_kernel(const Decod
             }
         }
     }
+}
+
+// Streaming decode attention: one CTA per (sequence, kv head, context split)
+// serves all G = heads / kv_heads query heads of the group, so a K/V row is
+// read from HBM once.  K and V of 64 consecutive keys are contiguous in the
+// cache ([cap, 128] per (sequence, kv head)), so each stage is two 16 KB bulk
+// copies (cp.async.bulk, no tensor map) into a 3-deep shared-memory ring,
+// issued by a producer warp; with two CTAs per SM that keeps ~192 KB of HBM
+// reads in flight per SM.  Each of the four compute warps owns 16 keys of
+// every stage and keeps its own online softmax (no block barrier per stage):
+//   scores: a half-warp per key, 16 lanes x 8 dims, four shuffles;
+//   P V:    lane l accumulates dims [4 l, 4 l + 4) of every query head;
+// the warps release a stage through an mbarrier and are merged once at the end.
+constexpr int kStKeys = 64;
+constexpr int kStBytes = kStKeys * kDecHd * 2;  // one of K or V per stage
+constexpr int kStStages = 3;
+constexpr int kStWarps = 4;                     // compute warps; warp 4 is the producer
+constexpr int kStThreads = (kStWarps + 1) * 32;
+
+template <int G>
+constexpr int stream_smem() {
+    return kStStages * 2 * kStBytes + 16 * kStStages + 128;
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+template <int G>
+__global__ void __launch_bounds__(kStThreads) decode_attn_stream_kernel(const DecodeArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + kStStages * 2 * kStBytes);
+    uint64_t* empty = full + kStStages;
+    static_assert(kStWarps * G * (kDecHd + 2) * 4 <= kStStages * 2 * kStBytes, "merge area reuses the ring");
+
+    const int bk = blockIdx.x;  // sequence * kv_heads + kv head
+    const int b = bk / a.kv_heads, kvh = bk % a.kv_heads;
+    const int split = blockIdx.y;
+    const int len = (int)min((int64_t)(a.lens ? a.lens[b] : a.ctx), a.cap);
+    const int c0 = split * a.chunk;
+    const int c1 = min(len, c0 + a.chunk);
+    const int nkeys = c1 > c0 ? c1 - c0 : 0;
+    const int nst = (nkeys + kStKeys - 1) / kStKeys;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kStWarps);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    int never = 0;
+    volatile int* no_abort = &never;
+
+    float m[G], l[G], acc[G][4];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[g][e] = 0.0f;
+    }
+
+    if (warp == kStWarps) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            const __half* kbase = a.kc + ((int64_t)b * a.kv_heads + kvh) * a.cap * kDecHd;
+            const __half* vbase = a.vc + ((int64_t)b * a.kv_heads + kvh) * a.cap * kDecHd;
+            int i = 0;
+            for (; i < nst; ++i) {
+                const int slot = i % kStStages;
+                if (i >= kStStages &&
+                    !mbar_wait_bounded(&empty[slot], ((uint32_t)(i / kStStages) & 1u) ^ 1u, no_abort)) {
+                    if (a.err) atomicCAS(a.err, 0, 0x401);
+                    break;
+                }
+                const int k0 = c0 + i * kStKeys;
+                const uint32_t bytes = (uint32_t)min(kStKeys, c1 - k0) * kDecHd * 2;
+                mbar_arrive_expect_tx(&full[slot], 2 * bytes);
+                bulk_load(ring + slot * 2 * kStBytes, kbase + (int64_t)k0 * kDecHd, bytes, &full[slot]);
+                bulk_load(ring + slot * 2 * kStBytes + kStBytes, vbase + (int64_t)k0 * kDecHd, bytes, &full[slot]);
+            }
+            // every copy issued has landed before the ring is reused or the CTA exits
+            for (int j = i - kStStages < 0 ? 0 : i - kStStages; j < i; ++j)
+                if (!mbar_wait_bounded(&full[j % kStStages], (uint32_t)(j / kStStages) & 1u, no_abort, 200000000ull) &&
+                    a.err)
+                    atomicCAS(a.err, 0, 0x402);
+        }
+    } else {
+        // ------------------------------------------------------------ compute warps
+        const int hw = lane >> 4, l16 = lane & 15;
+        float q[G][8];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float f[8];
+            ld8f(a.q + (int64_t)b * a.ldq + (int64_t)(kvh * G + g) * kDecHd + 8 * l16, f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) q[g][e] = f[e] * a.scale_log2;
+        }
+        for (int i = 0; i < nst; ++i) {
+            const int slot = i % kStStages;
+            const bool ok = mbar_wait_bounded(&full[slot], (uint32_t)(i / kStStages) & 1u, no_abort);
+            if (!__all_sync(0xffffffffu, ok)) {
+                if (lane == 0 && a.err) atomicCAS(a.err, 0, 0x403);
+                break;
+            }
+            const uint8_t* Ks = ring + slot * 2 * kStBytes;
+            const uint8_t* Vs = Ks + kStBytes;
+            const int n = min(kStKeys, c1 - (c0 + i * kStKeys));
+            // scores of keys 16 warp + 2 it + hw, it = 0..7
+            float sc[G][8];
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+                const int key = 16 * warp + 2 * it + hw;
+                const uint4 raw = *reinterpret_cast<const uint4*>(Ks + key * (kDecHd * 2) + l16 * 16);
+                const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+                float kf[8];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 t = __half22float2(h2[e]);
+                    kf[2 * e] = t.x;
+                    kf[2 * e + 1] = t.y;
+                }
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float x = 0.0f;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) x = fmaf(q[g][e], kf[e], x);
+                    x += __shfl_xor_sync(0xffffffffu, x, 8);
+                    x += __shfl_xor_sync(0xffffffffu, x, 4);
+                    x += __shfl_xor_sync(0xffffffffu, x, 2);
+                    x += __shfl_xor_sync(0xffffffffu, x, 1);
+                    sc[g][it] = key < n ? x : -INFINITY;
+                }
+            }
+            // online softmax over this warp's 16 keys
+            float p[G][8];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float mx = sc[g][0];
+#pragma unroll
+                for (int it = 1; it < 8; ++it) mx = fmaxf(mx, sc[g][it]);
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                const float mn = fmaxf(m[g], mx);
+                const float corr = (m[g] == -INFINITY) ? 0.0f : exp2f(m[g] - mn);
+                float sum = 0.0f;
+#pragma unroll
+                for (int it = 0; it < 8; ++it) {
+                    p[g][it] = sc[g][it] == -INFINITY ? 0.0f : exp2f(sc[g][it] - mn);
+                    sum += p[g][it];
+                }
+                sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+                l[g] = l[g] * corr + sum;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[g][e] *= corr;
+                m[g] = mn == -INFINITY ? m[g] : mn;
+            }
+            // P V: lane owns dims 4 lane .. 4 lane + 3
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    const int key = 16 * warp + 2 * it + hh;
+                    if (key < n) {  // warp-uniform; rows past n may hold stale bytes
+                        const uint2 raw = *reinterpret_cast<const uint2*>(Vs + key * (kDecHd * 2) + lane * 8);
+                        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+                        const float2 v01 = __half22float2(h2[0]), v23 = __half22float2(h2[1]);
+#pragma unroll
+                        for (int g = 0; g < G; ++g) {
+                            const float pk = __shfl_sync(0xffffffffu, p[g][it], hh * 16);
+                            acc[g][0] = fmaf(pk, v01.x, acc[g][0]);
+                            acc[g][1] = fmaf(pk, v01.y, acc[g][1]);
+                            acc[g][2] = fmaf(pk, v23.x, acc[g][2]);
+                            acc[g][3] = fmaf(pk, v23.y, acc[g][3]);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+    }
+    // merge the four warps (the ring is idle now: every copy has landed and been read)
+    __syncthreads();
+    float* mg = reinterpret_cast<float*>(ring);  // [warp][g][130]: acc[128], m, l
+    if (warp < kStWarps) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float* row = mg + (warp * G + g) * (kDecHd + 2);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) row[4 * lane + e] = acc[g][e];
+            if (lane == 0) {
+                row[kDecHd] = m[g];
+                row[kDecHd + 1] = l[g];
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < kDecHd) {
+        const int d = threadIdx.x;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float M = -INFINITY;
+            for (int w = 0; w < kStWarps; ++w) M = fmaxf(M, mg[(w * G + g) * (kDecHd + 2) + kDecHd]);
+            float L = 0.0f, A = 0.0f;
+            for (int w = 0; w < kStWarps; ++w) {
+                const float* row = mg + (w * G + g) * (kDecHd + 2);
+                const float c = row[kDecHd] == -INFINITY ? 0.0f : exp2f(row[kDecHd] - M);
+                L += row[kDecHd + 1] * c;
+                A += row[d] * c;
+            }
+            const int h = kvh * G + g;
+            if (a.splits == 1) {
+                a.out[(int64_t)b * a.ldo + (int64_t)h * kDecHd + d] = __float2half_rn(L > 0.0f ? A / L : 0.0f);
+            } else {
+                float* pp = a.part + (((int64_t)b * a.heads + h) * a.splits + split) * (kDecHd + 2);
+                pp[d] = A;
+                if (d == 0) {
+                    pp[kDecHd] = M;
+                    pp[kDecHd + 1] = L;
+                }
+            }
+        }
+    }
+}
+
+template <int G>
+static int launch_stream(const DecodeArgs& a, int batch, int kv_heads, int splits, cudaStream_t st) {
+    auto kern = decode_attn_stream_kernel<G>;
+    constexpr int smem = stream_smem<G>();
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) {
+        npub_internal_set_cuda_error(e);
+        return NPUB_ERR_CUDA;
+    }
+    kern<<<dim3(batch * kv_heads, splits), kStThreads, smem, st>>>(a);
+    return npub_internal_launch_status();
 }
 
 __global__ void decode_combine_kernel(const float* __restrict__ part, int splits, int heads, __half* __restrict__ out,
@@ -396,8 +640,20 @@ extern "C" int npub_attention_decode(const void* q, int64_t ldq, const void* k_c
         if (!workspace || workspace_bytes < need) return NPUB_ERR_WORKSPACE;
         a.part = reinterpret_cast<float*>(workspace);
     }
-    decode_attn_kernel<<<dim3(bh, splits), kDecWarps * 32, 0, st>>>(a);
-    int rc = npub_internal_launch_status();
+    a.err = npub_internal_device_error_word();
+    const int group = heads / kv_heads;
+    int rc;
+    if (group == 1 || group == 2 || group == 4 || group == 8) {
+        switch (group) {
+            case 1: rc = launch_stream<1>(a, batch, kv_heads, splits, st); break;
+            case 2: rc = launch_stream<2>(a, batch, kv_heads, splits, st); break;
+            case 4: rc = launch_stream<4>(a, batch, kv_heads, splits, st); break;
+            default: rc = launch_stream<8>(a, batch, kv_heads, splits, st); break;
+        }
+    } else {
+        decode_attn_kernel<<<dim3(bh, splits), kDecWarps * 32, 0, st>>>(a);
+        rc = npub_internal_launch_status();
+    }
     if (rc || splits == 1) return rc;
     decode_combine_kernel<<<bh, kDecHd, 0, st>>>(a.part, splits, heads, a.out, ldo);
     return npub_internal_launch_status();

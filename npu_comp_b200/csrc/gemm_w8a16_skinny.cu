@@ -31,7 +31,8 @@
 //   warp 1      TMEM allocator; MMA issuer
 //   warp 2      TMA producer, fp16 tokens (ring of ST x BT x 128 x 2 B)
 //   warps 4-7   epilogue: TMEM -> scale / residual -> fp16, or fp32 partials
-//   warps 8-15  converters, two groups of four warps taking K steps in turn
+//   warps 8-15  converters: every K step, warp 8 + 4h + q converts bytes
+//               [64 h, 64 h + 64) of the rows of TMEM lane quadrant q
 //
 // The tile counters fill the first kSkinnyCounterBytes of the workspace, the
 // same bytes whatever the shape, so they are never overwritten by partials of
@@ -53,12 +54,11 @@ constexpr int kThreads = 512;
 constexpr int kRows = 128;   // weight rows per tile (MMA M)
 constexpr int kBK = 128;     // K per unit (one 128-byte swizzled int8 row)
 constexpr int kS8 = 8;       // int8 ring depth
-constexpr int kSA = 4;       // fp16 weight stages in TMEM (kBK / 2 columns each)
-constexpr int kGroups = 2;   // converter groups
+constexpr int kSA = 6;       // fp16 weight stages in TMEM (kBK / 2 columns each)
+constexpr int kConvWarps = 8;  // every converter warp works on every K step (half a row each)
 constexpr int kAcols = kBK / 2;
-constexpr int kAcol0 = 128;  // first TMEM column of the A stages (accumulators use [0, 2 BT))
+constexpr int kAcol0 = 128;  // first TMEM column of the A stages (accumulators use [0, 2 BT) <= 128)
 constexpr uint32_t kTmemCols = 512;
-static_assert(kS8 % kGroups == 0 && kSA % kGroups == 0, "converter groups take alternate K steps");
 static_assert(kAcol0 + kSA * kAcols <= (int)kTmemCols, "tensor memory budget");
 
 template <int BT>
@@ -205,10 +205,10 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
     uint8_t* sA8 = sTok + kST * L::kTok;       // kS8 x kA8  (1024-aligned)
     uint64_t* bars = reinterpret_cast<uint64_t*>(sA8 + kS8 * L::kA8);
     uint64_t* full8 = bars;                    // [kS8] int8 tile landed
-    uint64_t* empty8 = full8 + kS8;            // [kS8] int8 tile converted (4 warps)
+    uint64_t* empty8 = full8 + kS8;            // [kS8] int8 tile read by the 8 converter warps
     uint64_t* tok_full = empty8 + kS8;         // [kST] token tile landed
     uint64_t* tok_empty = tok_full + kST;      // [kST] MMA done with the token tile
-    uint64_t* a_full = tok_empty + kST;        // [kSA] fp16 weights in TMEM (4 warps)
+    uint64_t* a_full = tok_empty + kST;        // [kSA] fp16 weights in TMEM (8 converter warps)
     uint64_t* a_empty = a_full + kSA;          // [kSA] MMA done with the TMEM stage
     uint64_t* acc_full = a_empty + kSA;        // [2] accumulator ready
     uint64_t* acc_empty = acc_full + 2;        // [2] epilogue drained the accumulator (4 warps)
@@ -223,14 +223,14 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
     if (threadIdx.x == 0) {
         for (int s = 0; s < kS8; ++s) {
             mbar_init(&full8[s], 1);
-            mbar_init(&empty8[s], 4);
+            mbar_init(&empty8[s], kConvWarps);
         }
         for (int s = 0; s < kST; ++s) {
             mbar_init(&tok_full[s], 1);
             mbar_init(&tok_empty[s], 1);
         }
         for (int s = 0; s < kSA; ++s) {
-            mbar_init(&a_full[s], 4);
+            mbar_init(&a_full[s], kConvWarps);
             mbar_init(&a_empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -337,12 +337,12 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
         }
     } else if (warp >= 8) {
         // ------------------------------------------------------------ converters
-        const int grp = (warp - 8) >> 2;
-        const int q = warp & 3;  // TMEM lane quadrant of this warp
+        const int half = (warp - 8) >> 2;  // which 64 bytes of K of the row
+        const int q = warp & 3;            // TMEM lane quadrant of this warp
         const int row = 32 * q + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
         const int64_t total = rg.u1 - rg.u0;
-        for (uint32_t g = (uint32_t)grp; (int64_t)g < total; g += kGroups) {
+        for (uint32_t g = 0; (int64_t)g < total; ++g) {
             const int s8 = (int)(g % kS8), sa = (int)(g % kSA);
             if (!mbar_wait_bounded(&full8[s8], (g / kS8) & 1u, abort_flag) ||
                 !mbar_wait_bounded(&a_empty[sa], ((g / kSA) & 1u) ^ 1u, abort_flag)) {
@@ -352,19 +352,16 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
             }
             tc_fence_after();
             const uint8_t* src = sA8 + s8 * L::kA8 + row * kBK;
-            uint4 raw[8];
+            uint4 raw[4];
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                raw[j] = *reinterpret_cast<const uint4*>(src + ((j ^ (row & 7)) << 4));
+            for (int j = 0; j < 4; ++j)
+                raw[j] = *reinterpret_cast<const uint4*>(src + (((4 * half + j) ^ (row & 7)) << 4));
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty8[s8]);
+            uint32_t r[32];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                uint32_t r[32];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) cvt16(raw[4 * h + j], &r[8 * j]);
-                tmem_st32(lane_base + (uint32_t)(kAcol0 + sa * kAcols + 32 * h), r);
-            }
+            for (int j = 0; j < 4; ++j) cvt16(raw[j], &r[8 * j]);
+            tmem_st32(lane_base + (uint32_t)(kAcol0 + sa * kAcols + 32 * half), r);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();

@@ -60,7 +60,9 @@ def test_attention_reference_example(cuda_device, examples):
     assert ref.rel_err(out, examples["attention_ref"]) <= TOL
 
 
-@pytest.mark.parametrize("B,H,KV,ctx,cap", [(4, 8, 4, 300, 320), (2, 4, 4, 4096, 4100), (3, 2, 1, 1, 8)])
+@pytest.mark.parametrize("B,H,KV,ctx,cap", [(4, 8, 4, 300, 320), (2, 4, 4, 4096, 4100), (3, 2, 1, 1, 8),
+                                            (8, 32, 32, 1000, 1024), (2, 16, 2, 777, 800), (2, 6, 2, 200, 256),
+                                            (64, 8, 8, 128, 128)])
 def test_decode_attention(cuda_device, rng, B, H, KV, ctx, cap):
     hd = 128
     q = rng.standard_normal((B, H * hd)).astype(np.float16)
