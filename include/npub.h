@@ -74,12 +74,12 @@ int npub_device_error(int clear);
  * C    fp16 [M, N] (ldc >= N);  R fp16 [M, N] residual added after scaling (NULL = none)
  * K % 16 == 0.  Accumulation is fp32 on the tensor cores (tcgen05).
  * workspace: npub_w8a16_gemm_workspace(M, N, K) bytes (split-K partials);
- * may be NULL when that query returns 0.  For M <= 64 (decode steps, a
- * stream-K kernel) the first 64 KiB of the workspace are tile counters: they
- * must be zero before the first call on that workspace, every completed call
- * leaves them zero again, and nothing else may write them (calls of M > 64,
- * other data, calls running at the same time on other streams).  Re-zero them
- * after a call that reported NPUB_ERR_DEVICE_TIMEOUT. */
+ * may be NULL when that query returns 0.  A non-empty workspace starts with
+ * 64 KiB of tile counters (used by the stream-K kernel that decode-sized M
+ * runs on): they must be zero before the first call on that workspace, every
+ * completed call leaves them zero again, and nothing else may write them
+ * (other data, calls running at the same time on other streams).  Re-zero
+ * them after a call that reported NPUB_ERR_DEVICE_TIMEOUT. */
 int npub_w8a16_gemm(const void* A, int64_t lda, const int8_t* Wq, int64_t ldw, const void* scale, void* C,
                     int64_t ldc, const void* R, int64_t ldr, int M, int N, int K, float alpha, void* workspace,
                     size_t workspace_bytes, void* stream);

@@ -19,7 +19,6 @@
 // they are read.  Calls that overlap on the GPU (different streams, or
 // different host threads on the same device) race on the array.
 #include "common.cuh"
-#include "gemm_w8a16_skinny.h"
 
 #include <mutex>
 
@@ -58,17 +57,14 @@ extern "C" int npub_w8a16_gemm_noalloc(const void* A, int64_t lda, const int8_t*
                                        void* C, int64_t ldc, const void* R, int64_t ldr, int M, int N, int K,
                                        float alpha, void* stream) {
     if (M < 0 || N < 0 || K < 0) return NPUB_ERR_INVALID_ARG;
+    // Every W8A16 workspace layout starts with the counter region, so all
+    // calls can share the array from its start.
     const size_t need = npub_w8a16_gemm_workspace(M, N, K);
-    // Few-token calls take the array from its start (counters first); split-K
-    // partials of other calls start after the counter region.
-    const bool skinny = npub::w8a16_skinny_fits(M, N);
-    const size_t off = skinny ? 0 : npub::kSkinnyCounterBytes;
-    if (need > (size_t)NPUB_NOALLOC_SCRATCH_BYTES - off) return NPUB_ERR_SCRATCH_LIMIT;
+    if (need > (size_t)NPUB_NOALLOC_SCRATCH_BYTES) return NPUB_ERR_SCRATCH_LIMIT;
     void* ws = nullptr;
     if (need > 0) {
         const int rc = noalloc_scratch(&ws);
         if (rc != NPUB_OK) return rc;
-        ws = static_cast<unsigned char*>(ws) + off;
     }
     return npub_w8a16_gemm(A, lda, Wq, ldw, scale, C, ldc, R, ldr, M, N, K, alpha, ws, need, stream);
 }

@@ -416,7 +416,12 @@ int run_gemm(GemmParams& p, bool a_int8, int bt, int grid_x, int grid_y, int bat
 // Aop = weights [N, K] (128-row side), Bop = activations [M, K] (token side).
 static size_t linear_workspace(int M, int N, int K, bool w_int8) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
-    if (w_int8) return w8a16_skinny_fits(M, N) ? w8a16_skinny_workspace(M, N, K) : w8a16_pair_workspace(M, N, K);
+    if (w_int8) {
+        // every W8A16 workspace starts with the stream-K kernel's counter region
+        if (w8a16_use_skinny(M, N, K)) return w8a16_skinny_workspace(M, N, K);
+        const size_t pair = w8a16_pair_workspace(M, N, K);
+        return pair ? kSkinnyCounterBytes + pair : 0;
+    }
     const int bt = pick_bt(M);
     const int tiles = ((N + BM - 1) / BM) * ((M + bt - 1) / bt);
     const int k_tiles = (K + BK - 1) / BK;
@@ -440,8 +445,10 @@ static int linear_w8a16_pair(const void* A, int64_t lda, const void* W, int64_t 
     const int splits = w8a16_pair_splits(M, N, K);
     p.alpha = alpha;
     if (splits > 1) {
+        // partials after the counter region, which only the stream-K kernel uses
         const size_t need = (size_t)splits * M * N * sizeof(float);
-        if (!ws || ws_bytes < need) return NPUB_ERR_WORKSPACE;
+        if (!ws || ws_bytes < kSkinnyCounterBytes + need) return NPUB_ERR_WORKSPACE;
+        ws = static_cast<uint8_t*>(ws) + kSkinnyCounterBytes;
         if (!npub_aligned(ws, 16)) return NPUB_ERR_INVALID_ARG;
         p.out_f32 = 1;
         p.part = reinterpret_cast<float*>(ws);
@@ -478,7 +485,7 @@ static int linear(bool w_int8, const void* A, int64_t lda, const void* W, int64_
     NPUB_CHECK_ARG(ldc >= N);
     NPUB_CHECK_ARG(!R || ldr >= N);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (w_int8 && w8a16_skinny_fits(M, N))
+    if (w_int8 && w8a16_use_skinny(M, N, K))
         return w8a16_skinny_run(A, lda, W, ldw, scale, C, ldc, R, ldr, M, N, K, alpha, ws, ws_bytes, st);
     if (w_int8) return linear_w8a16_pair(A, lda, W, ldw, scale, C, ldc, R, ldr, M, N, K, alpha, ws, ws_bytes, st);
 

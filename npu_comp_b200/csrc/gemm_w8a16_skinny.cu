@@ -518,6 +518,15 @@ bool w8a16_skinny_fits(int M, int N) {
            (size_t)4 * ((N + skinny::kRows - 1) / skinny::kRows) * sizeof(unsigned) <= kSkinnyCounterBytes;
 }
 
+// Measured on B200 (decode-layer shapes, weights streamed from HBM): the
+// stream-K kernel wins where the weight matrix is wide (its tiles spread over
+// every SM); the 2-CTA pair kernel wins on K-long or N <= 8192 matrices at
+// M = 64, where its wider MMAs issue fewer instructions per weight byte.
+bool w8a16_use_skinny(int M, int N, int K) {
+    if (!w8a16_skinny_fits(M, N) || K <= 0) return false;
+    return (M <= 32 && N >= 8192) || N >= 16384;
+}
+
 size_t w8a16_skinny_workspace(int M, int N, int K) {
     if (!w8a16_skinny_fits(M, N) || K <= 0) return 0;
     return kSkinnyCounterBytes + (size_t)2 * skinny_grid(N, K) * skinny_bt(M) * skinny::kRows * sizeof(float);

@@ -31,8 +31,9 @@ struct SkinnyParams {
 // region (never partial sums), 4 per 128-row tile, so N <= 524288.
 constexpr size_t kSkinnyCounterBytes = 64 << 10;
 
-// Whether (M, N) runs on the stream-K kernel.
+// Whether (M, N) can run on the stream-K kernel, and whether it should.
 bool w8a16_skinny_fits(int M, int N);
+bool w8a16_use_skinny(int M, int N, int K);
 size_t w8a16_skinny_workspace(int M, int N, int K);
 int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C, int64_t ldc,
                      const void* R, int64_t ldr, int M, int N, int K, float alpha, void* ws, size_t ws_bytes,

@@ -67,13 +67,11 @@ def _workspace(nbytes: int, device) -> Tuple[Optional[torch.Tensor], int]:
     return ws[off:off + nbytes], nbytes
 
 
-# The few-token W8A16 kernel (M <= 64) keeps tile counters in the first 64 KiB
-# of its workspace; they must start at zero and every call leaves them at zero.
-# One zero-filled buffer per (device, stream) serves all such calls and
-# nothing else; a grown buffer replaces the old one, which is kept alive for
-# CUDA graphs that captured its address.
-_SKINNY_MAX_M = 64
-_SKINNY_COUNTER_BYTES = 64 << 10
+# A W8A16 workspace starts with 64 KiB of tile counters for the few-token
+# (stream-K) kernel; they must start at zero and every call leaves them at
+# zero.  One zero-filled buffer per (device, stream) serves every W8A16 call;
+# a grown buffer replaces the old one, which is kept alive for CUDA graphs
+# that captured its address.
 _zeroed_ws = {}
 _retired_ws = []
 
@@ -142,7 +140,7 @@ def matmul(A: torch.Tensor, W: torch.Tensor, scale: Optional[torch.Tensor] = Non
         _need(tuple(residual.shape) == (M, N), "residual must be [M, N]")
     int8 = W.dtype == torch.int8
     wsq = "npub_w8a16_gemm_workspace" if int8 else "npub_f16_gemm_workspace"
-    if int8 and M <= _SKINNY_MAX_M and (N + 127) // 128 * 16 <= _SKINNY_COUNTER_BYTES:
+    if int8:
         ws, wsb = _zeroed_workspace(_lib.query(wsq, M, N, K), A.device)
     else:
         ws, wsb = _workspace(_lib.query(wsq, M, N, K), A.device)
