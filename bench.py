@@ -227,7 +227,7 @@ def run_ours(args):
                   "parallelism": f"tp{world}", "l2": "inputs larger than L2 (202 MB int8 weights per step)"}
         h_in, d_out = x, y
     elif wl == "decode":
-        B, ctx = 64, 4096
+        B, ctx = args.batch or 64, args.ctx or 4096
         w = llama.make_layer(cfg, seed=0, device=dev, tp=tp)
         hk = cfg.kv_heads // world
         kc = torch.randn((B, hk, ctx + 8, cfg.head_dim), generator=gen, device=dev).half()
@@ -243,8 +243,8 @@ def run_ours(args):
         config = {"workload": "llama7b_layer_decode_w8a16", "batch": B, "kv_len": ctx, "parallelism": f"tp{world}",
                   "l2": "inputs larger than L2 (4.3 GB KV cache per step)"}
         h_in, d_out = x, y
-    else:  # gemm: the layer's gate|up projection alone
-        M, N, K = 2048, 2 * cfg.ffn // world, cfg.d
+    else:  # gemm: the layer's gate|up projection alone (or --shape M,N,K)
+        M, N, K = (2048, 2 * cfg.ffn // world, cfg.d) if not args.shape else map(int, args.shape.split(","))
         Wf = torch.randn((K, N), generator=gen, device=dev) * 0.02
         q, s = npu.quantize_w8(Wf)
         del Wf
@@ -349,7 +349,10 @@ def run_ours(args):
     g_n = sum(1 for *_, i8 in gev if i8) // reps
     achieved = g_flops / (g_ms / 1e3) / 1e12 if g_ms > 0 else None
     peak = tf_burst
-    roof = {"kernel": "w8a16_pair_kernel (tcgen05 cta_group::2 W8A16)", "bound": "tensor", "achieved": achieved,
+    lib = _lib.load()
+    gm = (M, N, K) if wl == "gemm" else (2048, 2 * cfg.ffn // world, cfg.d)
+    gemm_kernel = lib.npub_w8a16_kernel_name(*gm).decode()
+    roof = {"kernel": gemm_kernel, "bound": "tensor", "achieved": achieved,
             "peak": peak, "unit": "TFLOP/s", "frac": (achieved / peak) if achieved else None,
             "peak_source": f"{peak_src} bf16 dense (burst)", "launches_per_step": g_n,
             "flops_per_launch": g_flops / g_n if g_n else None,
@@ -398,9 +401,21 @@ def run_ours(args):
             out["layer_tensor_frac"] = out["layer_tflops"] * world / peak
         if wl == "decode":
             out["breakdown_us"] = breakdown
-            by = llama.decode_bytes(cfg, 64, 4097)
+            by = llama.decode_bytes(cfg, B, ctx + 1)
             out["hbm_gbs"] = by / world / (ms_per_step / 1e3) / 1e9
             out["hbm_frac"] = out["hbm_gbs"] / hbm
+            # the dominant kernel of a decode step is the KV-cache read (attention);
+            # the W8A16 GEMM figures move to their own key
+            kv = 2.0 * B * (cfg.kv_heads // world) * (ctx + 1) * cfg.head_dim * 2
+            att_us = breakdown.get("attention") if breakdown else None
+            a_gbs = kv / (att_us * 1e-6) / 1e9 if att_us else None
+            out["roofline_gemm"] = roof
+            out["roofline"] = {"kernel": "decode_attn_stream_kernel (bulk-copy K/V ring, per-warp online softmax)",
+                               "bound": "hbm", "achieved": a_gbs, "peak": hbm, "unit": "GB/s",
+                               "frac": a_gbs / hbm if a_gbs else None,
+                               "peak_source": f"{peak_src} HBM copy bandwidth", "bytes_per_launch": kv,
+                               "avg_launch_us": att_us,
+                               "traffic": _traffic("decode") if (B, ctx) == (64, 4096) and world == 1 else None}
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -564,6 +579,9 @@ def main():
     ap.add_argument("--workload", choices=["stack", "layer", "decode", "gemm"], default="stack")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch every op from the host instead of a CUDA graph")
+    ap.add_argument("--shape", default=None, help="gemm workload: M,N,K instead of the gate|up projection")
+    ap.add_argument("--batch", type=int, default=None, help="decode workload: sequences (default 64)")
+    ap.add_argument("--ctx", type=int, default=None, help="decode workload: KV length (default 4096)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.steps is None:
@@ -576,16 +594,21 @@ def main():
         if rank != 0:
             return 0
         sys.path.insert(0, HERE)
+        # each step is one ~10 s sample on all host cores; W untimed samples first
+        # (at most 3), then K timed ones (at most 10) so the run stays within minutes
+        warm = min(args.warmup, 3)
+        for _ in range(warm):
+            cpu_reference_rate(all_cores=True)
         rates = []
         kind = sample = None
         cores = 1
-        for i in range(max(1, min(args.steps, 3))):
+        for i in range(max(1, min(args.steps, 10))):
             r, cores, kind, sample = cpu_reference_rate(all_cores=True)
             rates.append(r)
         rate = statistics.median(rates)
         value, unit = _scale_rate(rate, args.workload)
         line = {"impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": world,
-                "steps": len(rates), "warmup": 0, "higher_is_better": True, "vs_baseline": None,
+                "steps": len(rates), "warmup": warm, "higher_is_better": True, "vs_baseline": None,
                 "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": kind,
                                  "sample": sample + " ; GEMM FLOP rate scaled by the layer's FLOPs per token"},
                 "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -84,6 +84,10 @@ int npub_w8a16_gemm(const void* A, int64_t lda, const int8_t* Wq, int64_t ldw, c
                     int64_t ldc, const void* R, int64_t ldr, int M, int N, int K, float alpha, void* workspace,
                     size_t workspace_bytes, void* stream);
 size_t npub_w8a16_gemm_workspace(int M, int N, int K);
+/* Name of the kernel npub_w8a16_gemm runs for this shape (static storage):
+ * the 2-CTA pair kernel, or the stream-K kernel for decode-sized M.  No
+ * reference counterpart (diagnostics). */
+const char* npub_w8a16_kernel_name(int M, int N, int K);
 
 /* Allocation-free W8A16 matmul (no counterpart in the reference, which has no
  * device memory at all).  Same contract and result as npub_w8a16_gemm, for

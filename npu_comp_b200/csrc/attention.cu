@@ -196,7 +196,7 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_attn_kernel(const Decod
 // cache ([cap, 128] per (sequence, kv head)), so each stage is two 16 KB bulk
 // copies (cp.async.bulk, no tensor map) into a 3-deep shared-memory ring,
 // issued by a producer warp; with two CTAs per SM that keeps ~192 KB of HBM
-// reads in flight per SM.  Each of the four compute warps owns 16 keys of
+// reads in flight per SM.  Each of the eight compute warps owns 8 keys of
 // every stage and keeps its own online softmax (no block barrier per stage):
 //   scores: a half-warp per key, 16 lanes x 8 dims, four shuffles;
 //   P V:    lane l accumulates dims [4 l, 4 l + 4) of every query head;
@@ -204,7 +204,8 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_attn_kernel(const Decod
 constexpr int kStKeys = 64;
 constexpr int kStBytes = kStKeys * kDecHd * 2;  // one of K or V per stage
 constexpr int kStStages = 3;
-constexpr int kStWarps = 4;                     // compute warps; warp 4 is the producer
+constexpr int kStWarps = 8;                     // compute warps; warp 8 is the producer
+constexpr int kStKeysPerWarp = kStKeys / kStWarps;  // 8: four pairs of keys per stage
 constexpr int kStThreads = (kStWarps + 1) * 32;
 
 template <int G>
@@ -303,11 +304,12 @@ __global__ void __launch_bounds__(kStThreads) decode_attn_stream_kernel(const De
             const uint8_t* Ks = ring + slot * 2 * kStBytes;
             const uint8_t* Vs = Ks + kStBytes;
             const int n = min(kStKeys, c1 - (c0 + i * kStKeys));
-            // scores of keys 16 warp + 2 it + hw, it = 0..7
-            float sc[G][8];
+            // scores of keys kStKeysPerWarp warp + 2 it + hw
+            constexpr int NP = kStKeysPerWarp / 2;
+            float sc[G][NP];
 #pragma unroll
-            for (int it = 0; it < 8; ++it) {
-                const int key = 16 * warp + 2 * it + hw;
+            for (int it = 0; it < NP; ++it) {
+                const int key = kStKeysPerWarp * warp + 2 * it + hw;
                 const uint4 raw = *reinterpret_cast<const uint4*>(Ks + key * (kDecHd * 2) + l16 * 16);
                 const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
                 float kf[8];
@@ -329,19 +331,19 @@ __global__ void __launch_bounds__(kStThreads) decode_attn_stream_kernel(const De
                     sc[g][it] = key < n ? x : -INFINITY;
                 }
             }
-            // online softmax over this warp's 16 keys
-            float p[G][8];
+            // online softmax over this warp's keys
+            float p[G][NP];
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 float mx = sc[g][0];
 #pragma unroll
-                for (int it = 1; it < 8; ++it) mx = fmaxf(mx, sc[g][it]);
+                for (int it = 1; it < NP; ++it) mx = fmaxf(mx, sc[g][it]);
                 mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
                 const float mn = fmaxf(m[g], mx);
                 const float corr = (m[g] == -INFINITY) ? 0.0f : exp2f(m[g] - mn);
                 float sum = 0.0f;
 #pragma unroll
-                for (int it = 0; it < 8; ++it) {
+                for (int it = 0; it < NP; ++it) {
                     p[g][it] = sc[g][it] == -INFINITY ? 0.0f : exp2f(sc[g][it] - mn);
                     sum += p[g][it];
                 }
@@ -353,10 +355,10 @@ __global__ void __launch_bounds__(kStThreads) decode_attn_stream_kernel(const De
             }
             // P V: lane owns dims 4 lane .. 4 lane + 3
 #pragma unroll
-            for (int it = 0; it < 8; ++it) {
+            for (int it = 0; it < NP; ++it) {
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {
-                    const int key = 16 * warp + 2 * it + hh;
+                    const int key = kStKeysPerWarp * warp + 2 * it + hh;
                     if (key < n) {  // warp-uniform; rows past n may hold stale bytes
                         const uint2 raw = *reinterpret_cast<const uint2*>(Vs + key * (kDecHd * 2) + lane * 8);
                         const __half2* h2 = reinterpret_cast<const __half2*>(&raw);

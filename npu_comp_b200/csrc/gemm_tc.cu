@@ -552,6 +552,12 @@ extern "C" int npub_w8a16_gemm(const void* A, int64_t lda, const int8_t* Wq, int
 
 extern "C" size_t npub_w8a16_gemm_workspace(int M, int N, int K) { return npub::linear_workspace(M, N, K, true); }
 
+extern "C" const char* npub_w8a16_kernel_name(int M, int N, int K) {
+    if (M <= 0 || N <= 0 || K <= 0) return "none";
+    return npub::w8a16_use_skinny(M, N, K) ? "w8a16_skinny_kernel (stream-K, tcgen05 with A in TMEM)"
+                                           : "w8a16_pair_kernel (tcgen05 cta_group::2 W8A16)";
+}
+
 extern "C" int npub_f16_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C,
                              int64_t ldc, const void* R, int64_t ldr, int M, int N, int K, float alpha, void* workspace,
                              size_t workspace_bytes, void* stream) {
