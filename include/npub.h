@@ -198,6 +198,18 @@ size_t npub_attention_decode_workspace(int batch, int heads, int ctx_len, int he
 int npub_kv_append(const void* k_new, int64_t ldk, const void* v_new, int64_t ldv, void* k_cache, void* v_cache,
                    int64_t cap, const int32_t* pos, int pos0, int batch, int kv_heads, int head_dim, void* stream);
 
+/* Decode-step RoPE fused with the KV-cache append (the rope_Q / rope_Kt macros,
+ * llama_layer.py:96-112, plus the cache write of a decode step, which the
+ * reference does not have).  qkv [tokens, ldx] fp16 holds q heads, then k
+ * heads, then v heads (head_dim columns each); q and k are rotated in place
+ * with the positions[t] of each row (the same arithmetic as npub_rope), and
+ * the rotated k and the v heads are written to k_cache / v_cache
+ * [tokens, kv_heads, cap, head_dim] at slot positions[t].  lens (may be NULL)
+ * receives positions[t] + 1.  head_dim % 16 == 0, <= 512; 16-byte aligned. */
+int npub_rope_kv_append(void* qkv, int64_t ldx, int tokens, int q_heads, int kv_heads, int head_dim,
+                        const int32_t* positions, float theta, void* k_cache, void* v_cache, int64_t cap,
+                        int32_t* lens, void* stream);
+
 /* ------------------------------------------------- NPU ISA semantics ----
  * One compute instruction of the NPU over PE buffers (_poc/mysim.cpp:114-141):
  * `word` is the 32-bit instruction (opcodes 0x01-0x13 vector, 0x40-0x43

@@ -275,6 +275,62 @@ __global__ void rope_vec_kernel(__half* x, int64_t ldx, int heads, int hd, const
     }
 }
 
+// Decode-step RoPE fused with the KV-cache append: CTA (t, g) takes heads
+// [8 g, 8 g + 8) of token t's fused QKV row (q heads | k heads | v heads).
+// q and k heads are rotated in place exactly as rope_vec_kernel does; k and v
+// heads are also written to cache[t, h, pos[t], :]; CTA (t, 0) writes
+// lens[t] = pos[t] + 1 (the attention length of the step).
+__global__ void rope_kv_append_kernel(__half* x, int64_t ldx, int hq, int hk, int hd,
+                                      const int32_t* __restrict__ pos, float log2_theta, __half* __restrict__ kc,
+                                      __half* __restrict__ vc, int64_t cap, int32_t* __restrict__ lens) {
+    __shared__ float cs[256], sn[256];
+    const int t = blockIdx.x;
+    const int half = hd / 2;
+    const int p = pos[t];
+    if (lens && blockIdx.y == 0 && threadIdx.x == 0) lens[t] = p + 1;
+    for (int k = threadIdx.x; k < half; k += blockDim.x) {
+        const float inv_freq = exp2f(-(2.0f * (float)k / (float)hd) * log2_theta);
+        float sv, cv;
+        sincosf((float)p * inv_freq, &sv, &cv);
+        cs[k] = cv;
+        sn[k] = sv;
+    }
+    __syncthreads();
+    __half* row = x + (int64_t)t * ldx;
+    const int h0 = blockIdx.y * 8;
+    const int h1 = min(h0 + 8, hq + 2 * hk);
+    const int per_head = half / 8;
+    for (int i = threadIdx.x; i < (h1 - h0) * per_head; i += blockDim.x) {
+        const int hh = h0 + i / per_head, k0 = (i % per_head) * 8;
+        __half* a = row + (int64_t)hh * hd + k0;
+        const uint4 r1 = *reinterpret_cast<const uint4*>(a);
+        const uint4 r2 = *reinterpret_cast<const uint4*>(a + half);
+        uint4 o1 = r1, o2 = r2;
+        if (hh < hq + hk) {  // q and k heads are rotated
+            float x1[8], x2[8], y1[8], y2[8];
+            unpack8(r1, x1);
+            unpack8(r2, x2);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float c = cs[k0 + e], sv = sn[k0 + e];
+                y1[e] = x1[e] * c - x2[e] * sv;
+                y2[e] = x2[e] * c + x1[e] * sv;
+            }
+            o1 = pack8(y1);
+            o2 = pack8(y2);
+            *reinterpret_cast<uint4*>(a) = o1;
+            *reinterpret_cast<uint4*>(a + half) = o2;
+        }
+        if (hh >= hq) {  // k and v heads go to the caches
+            const bool isk = hh < hq + hk;
+            const int kvh = isk ? hh - hq : hh - hq - hk;
+            __half* dst = (isk ? kc : vc) + (((int64_t)t * hk + kvh) * cap + p) * hd + k0;
+            *reinterpret_cast<uint4*>(dst) = o1;
+            *reinterpret_cast<uint4*>(dst + half) = o2;
+        }
+    }
+}
+
 // ------------------------------------------------------------ embedding / argmax
 // out[r, :] = table[ids[r], :]; ids outside [0, vocab) give a zero row.
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const __half* __restrict__ table, int64_t ldt,
@@ -484,6 +540,24 @@ extern "C" int npub_rope(void* x, int64_t ldx, int tokens, int heads, int head_d
     const int64_t work = (int64_t)tokens * heads * (head_dim / 2);
     rope_kernel<<<grid_for(work, 256), 256, 0, st>>>(reinterpret_cast<__half*>(x), ldx, tokens, heads, head_dim,
                                                       positions, pos0, log2f(theta));
+    return npub_internal_launch_status();
+}
+
+extern "C" int npub_rope_kv_append(void* qkv, int64_t ldx, int tokens, int q_heads, int kv_heads, int head_dim,
+                                   const int32_t* positions, float theta, void* k_cache, void* v_cache, int64_t cap,
+                                   int32_t* lens, void* stream) {
+    NPUB_CHECK_ARG(tokens >= 0 && q_heads >= 0 && kv_heads >= 0);
+    if (tokens == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(qkv && positions && k_cache && v_cache && theta > 0.0f && cap > 0);
+    NPUB_CHECK_ARG(head_dim % 16 == 0 && head_dim > 0 && head_dim <= 512);
+    NPUB_CHECK_ARG(ldx >= (int64_t)(q_heads + 2 * kv_heads) * head_dim && ldx % 8 == 0);
+    NPUB_CHECK_ARG(npub_aligned(qkv, 16) && npub_aligned(k_cache, 16) && npub_aligned(v_cache, 16));
+    const int groups = (q_heads + 2 * kv_heads + 7) / 8;
+    if (groups == 0) return NPUB_OK;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    rope_kv_append_kernel<<<dim3(tokens, groups), 64, 0, st>>>(
+        reinterpret_cast<__half*>(qkv), ldx, q_heads, kv_heads, head_dim, positions, log2f(theta),
+        reinterpret_cast<__half*>(k_cache), reinterpret_cast<__half*>(v_cache), cap, lens);
     return npub_internal_launch_status();
 }
 

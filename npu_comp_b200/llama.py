@@ -281,13 +281,9 @@ def layer_decode(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, k_cache: to
     mk("qkv_gemm")
     qkv = npu.matmul(xn, w.wqkv, w.sqkv, out=sc.get("dqkv", (B, (hq + 2 * hk) * hd), device=dev))
     q = qkv[:, : hq * hd]
-    k = qkv[:, hq * hd:(hq + hk) * hd]
-    v = qkv[:, (hq + hk) * hd:]
     mk("rope_kv_append")
-    npu.rope(qkv, hq + hk, hd, positions=pos, theta=cfg.theta)  # q and k heads are adjacent columns
-    npu.kv_append(k, v, k_cache, v_cache, pos=pos)
     lens = sc.get("dlens", (B,), dtype=torch.int32, device=dev)
-    torch.add(pos, 1, out=lens)
+    npu.rope_kv_append(qkv, hq, hk, hd, pos, k_cache, v_cache, theta=cfg.theta, lens=lens)
     mk("attention")
     ctx = npu.attention_decode(q, k_cache, v_cache, heads=hq, kv_heads=hk, lens=lens, ctx_len=ctx_max,
                                out=sc.get("dctx", (B, hq * hd), device=dev))

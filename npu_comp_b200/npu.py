@@ -25,7 +25,7 @@ from ._lib import NpubError  # noqa: F401  (re-exported)
 
 __all__ = [
     "fp16", "quantize_w8", "matmul", "rmsnorm", "add", "swiglu", "softmax", "rope", "attention",
-    "attention_decode", "kv_append", "embed", "argmax", "isa_vector", "f32_to_f16_bits", "f16_bits_to_f32", "NpubError",
+    "attention_decode", "kv_append", "rope_kv_append", "embed", "argmax", "isa_vector", "f32_to_f16_bits", "f16_bits_to_f32", "NpubError",
 ]
 
 
@@ -348,6 +348,28 @@ def kv_append(k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor, v
 
 
 # --------------------------------------------------------- NPU ISA semantics
+
+def rope_kv_append(qkv: torch.Tensor, q_heads: int, kv_heads: int, head_dim: int, positions: torch.Tensor,
+                   k_cache: torch.Tensor, v_cache: torch.Tensor, *, theta: float = 10000.0,
+                   lens: Optional[torch.Tensor] = None) -> None:
+    """Decode step: rope() on the q and k heads of the fused QKV rows (in place)
+    and kv_append() of the rotated k and the v heads at positions[t], in one
+    kernel; lens (int32 [tokens], optional) receives positions + 1."""
+    ldx = _mat(qkv, "qkv", torch.float16)
+    T = qkv.shape[0]
+    _need(qkv.shape[1] >= (q_heads + 2 * kv_heads) * head_dim, "qkv has too few columns")
+    _need(positions.is_cuda and positions.dtype == torch.int32 and positions.numel() == T
+          and positions.is_contiguous(), "positions must be contiguous int32 CUDA [tokens]")
+    for c, n in ((k_cache, "k_cache"), (v_cache, "v_cache")):
+        _need(c.is_cuda and c.dtype == torch.float16 and c.is_contiguous() and c.dim() == 4
+              and tuple(c.shape[:2]) == (T, kv_heads) and c.shape[3] == head_dim,
+              f"{n} must be contiguous fp16 CUDA [tokens, kv_heads, cap, head_dim]")
+    if lens is not None:
+        _need(lens.is_cuda and lens.dtype == torch.int32 and lens.numel() == T and lens.is_contiguous(),
+              "lens must be contiguous int32 CUDA [tokens]")
+    _lib.call("npub_rope_kv_append", qkv.data_ptr(), ldx, T, q_heads, kv_heads, head_dim, positions.data_ptr(),
+              float(theta), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[2], _ptr(lens), _stream())
+
 
 def isa_vector(word: int, in1: torch.Tensor, in2: Optional[torch.Tensor] = None,
                prev_out: Optional[torch.Tensor] = None) -> torch.Tensor:

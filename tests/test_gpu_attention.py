@@ -91,3 +91,22 @@ def test_decode_matches_last_prefill_row(cuda_device, rng):
     o = nb.attention_decode(dev(q[T:T + 1], cuda_device), kc, vc, heads=H, lens=lens, ctx_len=T + 1).float()
     e = ((o[0] - full[T]).abs().max() / full[T].abs().max()).item()
     assert e <= TOL
+
+
+@pytest.mark.parametrize("B,H,KV,hd,cap", [(5, 8, 4, 128, 40), (3, 32, 32, 128, 300), (2, 6, 2, 64, 17)])
+def test_rope_kv_append_matches_separate_ops(cuda_device, B, H, KV, hd, cap):
+    """The fused decode-step op equals rope() on q|k heads, then kv_append(),
+    then lens = pos + 1, bit for bit."""
+    g = torch.Generator(device=cuda_device).manual_seed(B * H + hd)
+    qkv = torch.randn((B, (H + 2 * KV) * hd), generator=g, device=cuda_device).half()
+    pos = torch.randint(0, cap, (B,), generator=g, device=cuda_device, dtype=torch.int32)
+    kc = torch.randn((B, KV, cap, hd), generator=g, device=cuda_device).half()
+    vc = torch.randn_like(kc)
+    q1, kc1, vc1 = qkv.clone(), kc.clone(), vc.clone()
+    nb.rope(q1, H + KV, hd, positions=pos, theta=500000.0)
+    nb.kv_append(q1[:, H * hd:(H + KV) * hd], q1[:, (H + KV) * hd:], kc1, vc1, pos=pos)
+    lens = torch.full((B,), -7, dtype=torch.int32, device=cuda_device)
+    nb.rope_kv_append(qkv, H, KV, hd, pos, kc, vc, theta=500000.0, lens=lens)
+    assert torch.equal(qkv, q1)
+    assert torch.equal(kc, kc1) and torch.equal(vc, vc1)
+    assert torch.equal(lens, pos + 1)
