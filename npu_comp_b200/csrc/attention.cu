@@ -222,6 +222,7 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 
 template <int G>
 __global__ void __launch_bounds__(kStThreads) decode_attn_stream_kernel(const DecodeArgs a) {
+    pdl_trigger();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
     uint64_t* full = reinterpret_cast<uint64_t*>(ring + kStStages * 2 * kStBytes);
@@ -231,6 +232,7 @@ __global__ void __launch_bounds__(kStThreads) decode_attn_stream_kernel(const De
     const int bk = blockIdx.x;  // sequence * kv_heads + kv head
     const int b = bk / a.kv_heads, kvh = bk % a.kv_heads;
     const int split = blockIdx.y;
+    pdl_wait();  // lens, q and the caches come from earlier kernels
     const int len = (int)min((int64_t)(a.lens ? a.lens[b] : a.ctx), a.cap);
     const int c0 = split * a.chunk;
     const int c1 = min(len, c0 + a.chunk);
@@ -431,12 +433,13 @@ static int launch_stream(const DecodeArgs& a, int batch, int kv_heads, int split
         npub_internal_set_cuda_error(e);
         return NPUB_ERR_CUDA;
     }
-    kern<<<dim3(batch * kv_heads, splits), kStThreads, smem, st>>>(a);
-    return npub_internal_launch_status();
+    return launch_pdl(kern, dim3(batch * kv_heads, splits), dim3(kStThreads), smem, st, a);
 }
 
 __global__ void decode_combine_kernel(const float* __restrict__ part, int splits, int heads, __half* __restrict__ out,
                                       int64_t ldo) {
+    pdl_trigger();
+    pdl_wait();
     const int bh = blockIdx.x;
     const int b = bh / heads, h = bh % heads;
     const int d = threadIdx.x;
@@ -657,8 +660,8 @@ extern "C" int npub_attention_decode(const void* q, int64_t ldq, const void* k_c
         rc = npub_internal_launch_status();
     }
     if (rc || splits == 1) return rc;
-    decode_combine_kernel<<<bh, kDecHd, 0, st>>>(a.part, splits, heads, a.out, ldo);
-    return npub_internal_launch_status();
+    return launch_pdl(decode_combine_kernel, dim3(bh), dim3(kDecHd), 0, st, (const float*)a.part, splits, heads,
+                      a.out, ldo);
 }
 
 extern "C" int npub_kv_append(const void* k_new, int64_t ldk, const void* v_new, int64_t ldv, void* k_cache,

@@ -3,6 +3,7 @@
 #include "common.cuh"
 
 #include <atomic>
+#include <cstdlib>
 
 // One int per device context (module globals are instantiated per device).
 __device__ int g_npub_device_error;
@@ -11,6 +12,14 @@ static thread_local int t_last_cuda_error = 0;
 static std::atomic<unsigned long long> g_launches{0};
 
 void npub_internal_set_cuda_error(cudaError_t e) { t_last_cuda_error = (int)e; }
+
+bool npub_internal_pdl_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("NPUB_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
 
 int npub_internal_launch_status() {
     g_launches.fetch_add(1, std::memory_order_relaxed);

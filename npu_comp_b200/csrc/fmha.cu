@@ -56,6 +56,7 @@ __device__ __forceinline__ void set_err(int* err, int code) {
 }
 
 __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_constant__ Params p) {
+    pdl_trigger();
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     if (smem_u32(smem_raw) & 1023u) {  // the swizzled tiles need 1024-byte alignment
         if (threadIdx.x == 0) set_err(p.err, 0x300);
@@ -120,6 +121,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     const uint32_t tmem = *tmem_slot;
     int never = 0;
     volatile int* no_abort = &never;
+    pdl_wait();
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
@@ -372,8 +374,7 @@ int fmha_prefill(const void* q, int64_t ldq, const void* k, int64_t ldk, const v
         npub_internal_set_cuda_error(e);
         return NPUB_ERR_CUDA;
     }
-    fmha_fwd_kernel<<<dim3(p.n_qtiles, heads, batch), kThreads, kSmem, st>>>(p);
-    return npub_internal_launch_status();
+    return launch_pdl(fmha_fwd_kernel, dim3(p.n_qtiles, heads, batch), dim3(kThreads), kSmem, st, p);
 }
 
 }  // namespace npub

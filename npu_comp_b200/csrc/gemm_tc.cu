@@ -78,6 +78,7 @@ __device__ __forceinline__ void set_error(int* err, int code) {
 
 template <bool A_I8, int BT, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
+    pdl_trigger();
     using L = GemmSmem<A_I8, BT, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -134,6 +135,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     const uint32_t tmem = *tmem_slot;
     int never = 0;
     volatile int* no_abort = &never;
+    pdl_wait();
 
     const int zl = z % p.zmod, zh = z / p.zmod;
     const int a_bat = zl / p.za.div + zh * p.za.bat_hi;
@@ -298,6 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N,
                                      const __half* __restrict__ scale, float alpha, const __half* __restrict__ res,
                                      int64_t ldr, __half* __restrict__ out, int64_t ldo) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t total = (int64_t)M * N;
     const int64_t plane = total;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -366,8 +370,7 @@ static int launch_cfg(const GemmParams& p, int grid_x, int grid_y, int grid_z, c
         npub_internal_set_cuda_error(e);
         return NPUB_ERR_CUDA;
     }
-    kern<<<dim3(grid_x, grid_y, grid_z), kThreads, L::kTotal, st>>>(p);
-    return npub_internal_launch_status();
+    return launch_pdl(kern, dim3(grid_x, grid_y, grid_z), dim3(kThreads), L::kTotal, st, p);
 }
 
 template <bool A_I8>
@@ -465,11 +468,10 @@ static int linear_w8a16_pair(const void* A, int64_t lda, const void* W, int64_t 
     int blocks = (int)((total + 255) / 256);
     const int cap = num_sms() * 8;
     if (blocks > cap) blocks = cap;
-    splitk_reduce_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<const float*>(ws), p.splits, M, N,
+    return launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(256), 0, st, reinterpret_cast<const float*>(ws), p.splits, M, N,
                                                  reinterpret_cast<const __half*>(scale), alpha,
                                                  reinterpret_cast<const __half*>(R), ldr, reinterpret_cast<__half*>(C),
                                                  ldc);
-    return npub_internal_launch_status();
 }
 
 static int linear(bool w_int8, const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C,
@@ -534,11 +536,10 @@ static int linear(bool w_int8, const void* A, int64_t lda, const void* W, int64_
     int blocks = (int)((total + 255) / 256);
     const int cap = num_sms() * 8;
     if (blocks > cap) blocks = cap;
-    splitk_reduce_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<const float*>(ws), p.splits, M, N,
+    return launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(256), 0, st, reinterpret_cast<const float*>(ws), p.splits, M, N,
                                                  reinterpret_cast<const __half*>(scale), alpha,
                                                  reinterpret_cast<const __half*>(R), ldr, reinterpret_cast<__half*>(C),
                                                  ldc);
-    return npub_internal_launch_status();
 }
 
 }  // namespace npub

@@ -95,6 +95,7 @@ __device__ __forceinline__ TileCoord tile_coord(const PairParams& p, int tile, i
 template <int BT, int STAGES, int CSTAGES, int G>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<G>(), 1)
     w8a16_pair_kernel(const __grid_constant__ PairParams p) {
+    pdl_trigger();
     using L = Smem<BT, STAGES, CSTAGES>;
     static_assert(STAGES % G == 0 && CSTAGES >= G && CSTAGES >= 2, "see kPairStages*: converter groups take turns");
     extern __shared__ uint8_t smem_raw[];
@@ -149,6 +150,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<G>(), 1)
     const uint32_t tmem = *tmem_slot;
     int never = 0;
     volatile int* no_abort = &never;
+    pdl_wait();
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -354,8 +356,7 @@ static int launch(const PairParams& p, int max_clusters, cudaStream_t st) {
     }
     int clusters = p.n_tiles < max_clusters ? p.n_tiles : max_clusters;
     if (clusters < 1) clusters = 1;
-    kern<<<dim3(2 * clusters, 1, 1), threads_for<G>(), L::kTotal, st>>>(p);
-    return npub_internal_launch_status();
+    return launch_pdl(kern, dim3(2 * clusters, 1, 1), dim3(threads_for<G>()), L::kTotal, st, p);
 }
 
 static std::mutex g_mu;

@@ -197,6 +197,7 @@ __device__ __forceinline__ Seg seg_in_order(const Range& r, int i) {
 
 template <int BT>
 __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_constant__ SkinnyParams p) {
+    pdl_trigger();
     using L = Smem<BT>;
     constexpr int kST = L::kST;
     extern __shared__ uint8_t smem_raw[];
@@ -254,6 +255,16 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
     const uint32_t tmem = *tmem_slot;
     int never = 0;
     volatile int* no_abort = &never;
+    if (warp == 0 && lane == 0) {
+        // the first weight tiles go to L2 while the previous kernel finishes
+        uint32_t n = 0;
+        for (int i = 0; i < rg.nseg && n < (uint32_t)kS8; ++i) {
+            const Seg sg = seg_in_order(rg, i);
+            for (int j = 0; j < sg.nk && n < (uint32_t)kS8; ++j, ++n)
+                tma_prefetch_3d(&p.tmW, (sg.k0 + j) * kBK, sg.tile * kRows, 0);
+        }
+    }
+    pdl_wait();
 
     if (warp == 0 || warp == 2) {
         // ------------------------------------------------------------ producers
@@ -497,8 +508,7 @@ static int launch(const SkinnyParams& p, int grid, cudaStream_t st) {
         npub_internal_set_cuda_error(e);
         return NPUB_ERR_CUDA;
     }
-    kern<<<grid, kThreads, L::kTotal, st>>>(p);
-    return npub_internal_launch_status();
+    return launch_pdl(kern, dim3(grid), dim3(kThreads), L::kTotal, st, p);
 }
 
 }  // namespace skinny

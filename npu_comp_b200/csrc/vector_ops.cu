@@ -63,6 +63,8 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const __half* __restrict__ 
                                                      const __half* __restrict__ r, int64_t ldr, __half* xo,
                                                      int64_t ldxo, const __half* __restrict__ gamma,
                                                      __half* __restrict__ y, int64_t ldy, int d, float eps) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float red[NT / 32];
     const int row = blockIdx.x;
     const int nch = d / kVec;
@@ -104,6 +106,8 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const __half* __restrict__ 
 // ------------------------------------------------------------ SwiGLU
 __global__ void swiglu_vec_kernel(const __half* __restrict__ g, int64_t ldg, const __half* __restrict__ u,
                                   int64_t ldu, __half* __restrict__ h, int64_t ldh, int rows, int cols) {
+    pdl_trigger();
+    pdl_wait();
     const int cpr = cols / kVec;
     const int64_t total = (int64_t)rows * cpr;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -130,6 +134,8 @@ __global__ void swiglu_scalar_kernel(const __half* __restrict__ g, int64_t ldg, 
 // ------------------------------------------------------------ residual add
 __global__ void add_vec_kernel(const __half* __restrict__ a, int64_t lda, const __half* __restrict__ b, int64_t ldb,
                                __half* __restrict__ o, int64_t ldo, int rows, int cols) {
+    pdl_trigger();
+    pdl_wait();
     const int cpr = cols / kVec;
     const int64_t total = (int64_t)rows * cpr;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -244,6 +250,8 @@ __global__ void rope_kernel(__half* x, int64_t ldx, int tokens, int heads, int h
 // (x[i], x[i + hd/2]) are rotated 8 at a time with 128-bit accesses.
 __global__ void rope_vec_kernel(__half* x, int64_t ldx, int heads, int hd, const int32_t* __restrict__ pos, int pos0,
                                 float log2_theta) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float cs[256], sn[256];
     const int t = blockIdx.x;
     const int half = hd / 2;
@@ -283,6 +291,8 @@ __global__ void rope_vec_kernel(__half* x, int64_t ldx, int heads, int hd, const
 __global__ void rope_kv_append_kernel(__half* x, int64_t ldx, int hq, int hk, int hd,
                                       const int32_t* __restrict__ pos, float log2_theta, __half* __restrict__ kc,
                                       __half* __restrict__ vc, int64_t cap, int32_t* __restrict__ lens) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float cs[256], sn[256];
     const int t = blockIdx.x;
     const int half = hd / 2;
@@ -335,6 +345,8 @@ __global__ void rope_kv_append_kernel(__half* x, int64_t ldx, int hq, int hk, in
 // out[r, :] = table[ids[r], :]; ids outside [0, vocab) give a zero row.
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const __half* __restrict__ table, int64_t ldt,
                              int vocab, int d, __half* __restrict__ out, int64_t ldo) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x;
     const int id = ids[r];
     const bool ok = id >= 0 && id < vocab;
@@ -346,6 +358,8 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const __half* __re
 // Row argmax over fp16 logits: the largest value and its smallest index.
 __global__ void argmax_kernel(const __half* __restrict__ x, int64_t ldx, int cols, int32_t* __restrict__ idx,
                               float* __restrict__ val) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float sv[32];
     __shared__ int si[32];
     const __half* row = x + (int64_t)blockIdx.x * ldx;
@@ -464,17 +478,14 @@ extern "C" int npub_rmsnorm(const void* x, int64_t ldx, const void* residual, in
     const __half* gh = reinterpret_cast<const __half*>(gamma);
     __half* yh = reinterpret_cast<__half*>(y);
     const int nch = d / kVec;
-    if (nch <= 128)
-        rmsnorm_kernel<128, 1><<<rows, 128, 0, st>>>(xh, ldx, rh, ldr, xoh, ldxo, gh, yh, ldy, d, eps);
-    else if (nch <= 256)
-        rmsnorm_kernel<256, 1><<<rows, 256, 0, st>>>(xh, ldx, rh, ldr, xoh, ldxo, gh, yh, ldy, d, eps);
-    else if (nch <= 512)
-        rmsnorm_kernel<256, 2><<<rows, 256, 0, st>>>(xh, ldx, rh, ldr, xoh, ldxo, gh, yh, ldy, d, eps);
-    else if (nch <= 1024)
-        rmsnorm_kernel<256, 4><<<rows, 256, 0, st>>>(xh, ldx, rh, ldr, xoh, ldxo, gh, yh, ldy, d, eps);
-    else
-        rmsnorm_kernel<256, 8><<<rows, 256, 0, st>>>(xh, ldx, rh, ldr, xoh, ldxo, gh, yh, ldy, d, eps);
-    return npub_internal_launch_status();
+#define NPUB_RMS(NT, V) launch_pdl(rmsnorm_kernel<NT, V>, dim3(rows), dim3(NT), 0, st, xh, ldx, rh, ldr, xoh, ldxo, gh, \
+                                   yh, ldy, d, eps)
+    if (nch <= 128) return NPUB_RMS(128, 1);
+    if (nch <= 256) return NPUB_RMS(256, 1);
+    if (nch <= 512) return NPUB_RMS(256, 2);
+    if (nch <= 1024) return NPUB_RMS(256, 4);
+    return NPUB_RMS(256, 8);
+#undef NPUB_RMS
 }
 
 extern "C" int npub_swiglu(const void* g, int64_t ldg, const void* u, int64_t ldu, void* h, int64_t ldh, int rows,
@@ -487,9 +498,9 @@ extern "C" int npub_swiglu(const void* g, int64_t ldg, const void* u, int64_t ld
                      npub_aligned(g, 16) && npub_aligned(u, 16) && npub_aligned(h, 16);
     if (vec) {
         const int64_t work = (int64_t)rows * (cols / kVec);
-        swiglu_vec_kernel<<<grid_for(work, 256), 256, 0, st>>>(
-            reinterpret_cast<const __half*>(g), ldg, reinterpret_cast<const __half*>(u), ldu,
-            reinterpret_cast<__half*>(h), ldh, rows, cols);
+        return launch_pdl(swiglu_vec_kernel, dim3(grid_for(work, 256)), dim3(256), 0, st,
+                          reinterpret_cast<const __half*>(g), ldg, reinterpret_cast<const __half*>(u), ldu,
+                          reinterpret_cast<__half*>(h), ldh, rows, cols);
     } else {
         const int64_t work = (int64_t)rows * cols;
         swiglu_scalar_kernel<<<grid_for(work, 256), 256, 0, st>>>(
@@ -533,9 +544,8 @@ extern "C" int npub_rope(void* x, int64_t ldx, int tokens, int heads, int head_d
     NPUB_CHECK_ARG(x && head_dim > 0 && head_dim % 2 == 0 && ldx >= (int64_t)heads * head_dim && theta > 0.0f);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (head_dim % 16 == 0 && head_dim <= 512 && ldx % 8 == 0 && npub_aligned(x, 16)) {
-        rope_vec_kernel<<<tokens, 128, 0, st>>>(reinterpret_cast<__half*>(x), ldx, heads, head_dim, positions, pos0,
-                                                log2f(theta));
-        return npub_internal_launch_status();
+        return launch_pdl(rope_vec_kernel, dim3(tokens), dim3(128), 0, st, reinterpret_cast<__half*>(x), ldx, heads,
+                          head_dim, positions, pos0, log2f(theta));
     }
     const int64_t work = (int64_t)tokens * heads * (head_dim / 2);
     rope_kernel<<<grid_for(work, 256), 256, 0, st>>>(reinterpret_cast<__half*>(x), ldx, tokens, heads, head_dim,
@@ -555,10 +565,9 @@ extern "C" int npub_rope_kv_append(void* qkv, int64_t ldx, int tokens, int q_hea
     const int groups = (q_heads + 2 * kv_heads + 7) / 8;
     if (groups == 0) return NPUB_OK;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    rope_kv_append_kernel<<<dim3(tokens, groups), 64, 0, st>>>(
-        reinterpret_cast<__half*>(qkv), ldx, q_heads, kv_heads, head_dim, positions, log2f(theta),
-        reinterpret_cast<__half*>(k_cache), reinterpret_cast<__half*>(v_cache), cap, lens);
-    return npub_internal_launch_status();
+    return launch_pdl(rope_kv_append_kernel, dim3(tokens, groups), dim3(64), 0, st, reinterpret_cast<__half*>(qkv),
+                      ldx, q_heads, kv_heads, head_dim, positions, log2f(theta), reinterpret_cast<__half*>(k_cache),
+                      reinterpret_cast<__half*>(v_cache), cap, lens);
 }
 
 extern "C" int npub_quantize_w8(const float* W, int64_t ldw, int K, int N, int8_t* Wq, int64_t ldq, void* scale,
@@ -583,8 +592,8 @@ extern "C" int npub_add(const void* a, int64_t lda, const void* b, int64_t ldb, 
     const __half* bh = reinterpret_cast<const __half*>(b);
     __half* oh = reinterpret_cast<__half*>(out);
     if (vec)
-        add_vec_kernel<<<grid_for((int64_t)rows * (cols / kVec), 256), 256, 0, st>>>(ah, lda, bh, ldb, oh, ldo, rows,
-                                                                                    cols);
+        return launch_pdl(add_vec_kernel, dim3(grid_for((int64_t)rows * (cols / kVec), 256)), dim3(256), 0, st, ah, lda,
+                          bh, ldb, oh, ldo, rows, cols);
     else
         add_scalar_kernel<<<grid_for((int64_t)rows * cols, 256), 256, 0, st>>>(ah, lda, bh, ldb, oh, ldo, rows, cols);
     return npub_internal_launch_status();
@@ -596,9 +605,8 @@ extern "C" int npub_embed(const int32_t* ids, int n, const void* table, int64_t 
     if (n == 0) return NPUB_OK;
     NPUB_CHECK_ARG(ids && table && out && vocab > 0 && d > 0 && d % kVec == 0 && ldt >= d && ldo >= d);
     NPUB_CHECK_ARG(ldt % kVec == 0 && ldo % kVec == 0 && npub_aligned(table, 16) && npub_aligned(out, 16));
-    embed_kernel<<<n, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        ids, reinterpret_cast<const __half*>(table), ldt, vocab, d, reinterpret_cast<__half*>(out), ldo);
-    return npub_internal_launch_status();
+    return launch_pdl(embed_kernel, dim3(n), dim3(128), 0, reinterpret_cast<cudaStream_t>(stream), ids,
+                      reinterpret_cast<const __half*>(table), ldt, vocab, d, reinterpret_cast<__half*>(out), ldo);
 }
 
 extern "C" int npub_argmax_rows(const void* x, int64_t ldx, int rows, int cols, int32_t* idx, float* val,
@@ -606,7 +614,6 @@ extern "C" int npub_argmax_rows(const void* x, int64_t ldx, int rows, int cols, 
     NPUB_CHECK_ARG(rows >= 0);
     if (rows == 0) return NPUB_OK;
     NPUB_CHECK_ARG(x && idx && cols > 0 && ldx >= cols);
-    argmax_kernel<<<rows, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(reinterpret_cast<const __half*>(x), ldx,
-                                                                           cols, idx, val);
-    return npub_internal_launch_status();
+    return launch_pdl(argmax_kernel, dim3(rows), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+                      reinterpret_cast<const __half*>(x), ldx, cols, idx, val);
 }
