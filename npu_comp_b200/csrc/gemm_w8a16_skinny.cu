@@ -7,7 +7,7 @@
 // all M tokens at once (the MMA's N side, BT = 32 or 64 columns).  The design
 // follows from the weight stream being the whole cost:
 //
-//  * stream-K: the (tile, 128-wide K step) units are cut into one contiguous
+//  * stream-K: the (tile, 256-wide K step) units are cut into one contiguous
 //    range per CTA, grid = SM count, so every SM streams the same number of
 //    weight bytes whatever N / 128 is.  A tile cut between CTAs is finished by
 //    whichever of its CTAs arrives last on the tile's counter (one counter per
@@ -23,16 +23,19 @@
 //    MMA reads it as the A operand (tcgen05.mma with A in TMEM).  Shared
 //    memory carries only the TMA traffic.
 //  * an int8 stage is released as soon as it is converted, not when the MMA
-//    is done with it, so the 8-deep int8 ring (128 KB) is all TMA in flight;
-//    the token ring (L2-resident data, read by every CTA) is 6-8 deep.
+//    is done with it, so the 4-deep int8 ring (128 KB) is all TMA in flight;
+//    the token ring (L2-resident data, read by every CTA) is 3-4 deep.
+//  * a K step is 256 wide: 16 MMAs per barrier wait and commit, which keeps
+//    the single MMA thread's fixed per-step cost off the critical path.
 //
 // Roles (512 threads):
-//   warp 0      TMA producer, int8 weights (ring of kS8 x 16 KB)
+//   warp 0      TMA producer, int8 weights (ring of kS8 x 32 KB)
 //   warp 1      TMEM allocator; MMA issuer
 //   warp 2      TMA producer, fp16 tokens (ring of ST x BT x 128 x 2 B)
 //   warps 4-7   epilogue: TMEM -> scale / residual -> fp16, or fp32 partials
-//   warps 8-15  converters: every K step, warp 8 + 4h + q converts bytes
-//               [64 h, 64 h + 64) of the rows of TMEM lane quadrant q
+//   warps 8-15  converters: every K step, warp 8 + 4h + q converts int8 box h
+//               (bytes [128 h, 128 h + 128) of the step) of the rows of TMEM
+//               lane quadrant q
 //
 // The tile counters fill the first kSkinnyCounterBytes of the workspace, the
 // same bytes whatever the shape, so they are never overwritten by partials of
@@ -46,15 +49,19 @@
 #include "gemm_tc.h"
 #include "gemm_w8a16_skinny.h"
 
+#include <cstdlib>
+#include <cstring>
+
 namespace npub {
 
 namespace skinny {
 
 constexpr int kThreads = 512;
 constexpr int kRows = 128;   // weight rows per tile (MMA M)
-constexpr int kBK = 128;     // K per unit (one 128-byte swizzled int8 row)
-constexpr int kS8 = 8;       // int8 ring depth
-constexpr int kSA = 6;       // fp16 weight stages in TMEM (kBK / 2 columns each)
+constexpr int kBK = 256;     // K per unit: two 128-byte swizzled int8 boxes per row, 16 MMAs per wait
+constexpr int kBox8 = 128;   // int8 bytes of a row per TMA box (the 128-byte swizzle span)
+constexpr int kS8 = 4;       // int8 ring depth (32 KB stages)
+constexpr int kSA = 3;       // fp16 weight stages in TMEM (kBK / 2 columns each)
 constexpr int kConvWarps = 8;  // every converter warp works on every K step (half a row each)
 constexpr int kAcols = kBK / 2;
 constexpr int kAcol0 = 128;  // first TMEM column of the A stages (accumulators use [0, 2 BT) <= 128)
@@ -63,9 +70,10 @@ static_assert(kAcol0 + kSA * kAcols <= (int)kTmemCols, "tensor memory budget");
 
 template <int BT>
 struct Smem {
-    static constexpr int kST = BT == 32 ? 8 : 6;  // token ring depth
+    static constexpr int kST = BT == 32 ? 4 : 3;  // token ring depth
     static constexpr int kTokChunk = BT * 128;    // 64 fp16 of K for BT tokens
-    static constexpr int kTok = 2 * kTokChunk;
+    static constexpr int kTok = (kBK / 64) * kTokChunk;
+    static constexpr int kA8Box = kRows * kBox8;
     static constexpr int kA8 = kRows * kBK;
     static constexpr int kBars = 8 * (2 * kS8 + 2 * kST + 2 * kSA + 4) + 16;
     static constexpr int kTotal = kST * kTok + kS8 * kA8 + kBars + 1024;
@@ -261,7 +269,8 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
         for (int i = 0; i < rg.nseg && n < (uint32_t)kS8; ++i) {
             const Seg sg = seg_in_order(rg, i);
             for (int j = 0; j < sg.nk && n < (uint32_t)kS8; ++j, ++n)
-                tma_prefetch_3d(&p.tmW, (sg.k0 + j) * kBK, sg.tile * kRows, 0);
+                for (int c = 0; c < kBK / kBox8; ++c)
+                    tma_prefetch_3d(&p.tmW, (sg.k0 + j) * kBK + c * kBox8, sg.tile * kRows, 0);
         }
     }
     pdl_wait();
@@ -289,11 +298,15 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                     }
                     if (weights) {
                         mbar_arrive_expect_tx(&full[s], (uint32_t)L::kA8);
-                        tma_load_3d(sA8 + s * L::kA8, &p.tmW, &full[s], k, sg.tile * kRows, 0);
+#pragma unroll
+                        for (int c = 0; c < kBK / kBox8; ++c)
+                            tma_load_3d(sA8 + s * L::kA8 + c * L::kA8Box, &p.tmW, &full[s], k + c * kBox8,
+                                        sg.tile * kRows, 0);
                     } else {
                         mbar_arrive_expect_tx(&full[s], (uint32_t)L::kTok);
-                        tma_load_3d(sTok + s * L::kTok, &p.tmX, &full[s], k, 0, 0);
-                        tma_load_3d(sTok + s * L::kTok + L::kTokChunk, &p.tmX, &full[s], k + 64, 0, 0);
+#pragma unroll
+                        for (int c = 0; c < kBK / 64; ++c)
+                            tma_load_3d(sTok + s * L::kTok + c * L::kTokChunk, &p.tmX, &full[s], k + 64 * c, 0, 0);
                     }
                 }
             }
@@ -362,17 +375,20 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                 break;
             }
             tc_fence_after();
-            const uint8_t* src = sA8 + s8 * L::kA8 + row * kBK;
-            uint4 raw[4];
+            // this warp's half of the row: int8 box `half` (128 bytes, 128-byte swizzle)
+            const uint8_t* src = sA8 + s8 * L::kA8 + half * L::kA8Box + row * kBox8;
+            uint4 raw[8];
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                raw[j] = *reinterpret_cast<const uint4*>(src + (((4 * half + j) ^ (row & 7)) << 4));
+            for (int j = 0; j < 8; ++j) raw[j] = *reinterpret_cast<const uint4*>(src + ((j ^ (row & 7)) << 4));
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty8[s8]);
-            uint32_t r[32];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) cvt16(raw[j], &r[8 * j]);
-            tmem_st32(lane_base + (uint32_t)(kAcol0 + sa * kAcols + 32 * half), r);
+            for (int h = 0; h < 2; ++h) {
+                uint32_t r[32];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) cvt16(raw[4 * h + j], &r[8 * j]);
+                tmem_st32(lane_base + (uint32_t)(kAcol0 + sa * kAcols + 64 * half + 32 * h), r);
+            }
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -446,33 +462,26 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                 float4 acc[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int64_t c = c_first; c <= c_last; c += 2) {
-                    // two pieces' loads in flight before either is added
-                    const bool two = c + 1 <= c_last;
-                    const int64_t sl0 = 2 * c + (unit_start(c, U, G) / KT == sg.tile ? 0 : 1);
-                    const int64_t sl1 = two ? 2 * (c + 1) + (unit_start(c + 1, U, G) / KT == sg.tile ? 0 : 1) : sl0;
-                    const float4* p0 = reinterpret_cast<const float4*>(p.part + (sl0 * kRows + r) * BT) + c0 / 4;
-                    const float4* p1 = reinterpret_cast<const float4*>(p.part + (sl1 * kRows + r) * BT) + c0 / 4;
-                    float4 x0[4], x1[4];
+                for (int64_t c = c_first; c <= c_last; c += 4) {
+                    // up to four pieces' loads in flight, then added in CTA order
+                    float4 x[4][4];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        x0[j] = ld_cg_f4(p0 + j);
-                        x1[j] = ld_cg_f4(p1 + j);
+                    for (int i = 0; i < 4; ++i) {
+                        const int64_t cc = c + i <= c_last ? c + i : c;
+                        const int64_t sl = 2 * cc + (unit_start(cc, U, G) / KT == sg.tile ? 0 : 1);
+                        const float4* pp = reinterpret_cast<const float4*>(p.part + (sl * kRows + r) * BT) + c0 / 4;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) x[i][j] = ld_cg_f4(pp + j);
                     }
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        acc[j].x += x0[j].x;
-                        acc[j].y += x0[j].y;
-                        acc[j].z += x0[j].z;
-                        acc[j].w += x0[j].w;
-                    }
-                    if (two) {
+                    for (int i = 0; i < 4; ++i) {
+                        if (c + i > c_last) break;
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
-                            acc[j].x += x1[j].x;
-                            acc[j].y += x1[j].y;
-                            acc[j].z += x1[j].z;
-                            acc[j].w += x1[j].w;
+                            acc[j].x += x[i][j].x;
+                            acc[j].y += x[i][j].y;
+                            acc[j].z += x[i][j].z;
+                            acc[j].w += x[i][j].w;
                         }
                     }
                 }
@@ -515,10 +524,15 @@ static int launch(const SkinnyParams& p, int grid, cudaStream_t st) {
 
 int skinny_bt(int M) { return M <= 32 ? 32 : 64; }
 
+// One CTA per SM, but at least a quarter of a tile's K steps per CTA: a tile
+// is cut into at most ~5 pieces, which bounds the fixup of small matrices.
 static int skinny_grid(int N, int K) {
-    const int64_t units = (int64_t)((N + skinny::kRows - 1) / skinny::kRows) * ((K + skinny::kBK - 1) / skinny::kBK);
+    const int64_t kt = (K + skinny::kBK - 1) / skinny::kBK;
+    const int64_t units = (int64_t)((N + skinny::kRows - 1) / skinny::kRows) * kt;
+    const int64_t min_units = (kt + 3) / 4;
+    const int64_t want = (units + min_units - 1) / min_units;
     const int sms = num_sms();
-    return (int)(units < sms ? units : sms);
+    return (int)(want < sms ? want : sms);
 }
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -532,8 +546,23 @@ bool w8a16_skinny_fits(int M, int N) {
 // stream-K kernel wins where the weight matrix is wide (its tiles spread over
 // every SM); the 2-CTA pair kernel wins on K-long or N <= 8192 matrices at
 // M = 64, where its wider MMAs issue fewer instructions per weight byte.
+// NPUB_W8A16_KERNEL=pair or =skinny in the environment overrides the choice
+// (where the shape allows it), for measuring both kernels on one shape.
+static int kernel_override() {
+    static const int v = [] {
+        const char* e = getenv("NPUB_W8A16_KERNEL");
+        if (!e) return 0;
+        if (!strcmp(e, "pair")) return 1;
+        if (!strcmp(e, "skinny")) return 2;
+        return 0;
+    }();
+    return v;
+}
+
 bool w8a16_use_skinny(int M, int N, int K) {
     if (!w8a16_skinny_fits(M, N) || K <= 0) return false;
+    const int o = kernel_override();
+    if (o) return o == 2;
     return (M <= 32 && N >= 8192) || N >= 16384;
 }
 
@@ -553,7 +582,7 @@ int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, con
     SkinnyParams p;
     memset(&p, 0, sizeof(p));
     int rc = make_tmap_3d(&p.tmW, true, W, (uint64_t)K, (uint64_t)N, 1, (uint64_t)ldw, (uint64_t)ldw * N,
-                          skinny::kRows, 1, true, skinny::kBK);
+                          skinny::kRows, 1, true, skinny::kBox8);
     if (rc) return rc;
     rc = make_tmap_3d(&p.tmX, false, A, (uint64_t)K, (uint64_t)M, 1, (uint64_t)lda, (uint64_t)lda * M, (uint32_t)bt,
                       1, true);
