@@ -417,7 +417,9 @@ def run_ours(args):
                                "avg_launch_us": att_us,
                                "traffic": _traffic("decode") if (B, ctx) == (64, 4096) and world == 1 else None}
     if world > 1:
+        torch.cuda.synchronize()
         dist.barrier()
+        tp.close()
         dist.destroy_process_group()
     return out
 
@@ -549,7 +551,9 @@ def run_stack(args):
                if st.graph is not None else "eager"}
     st.release()
     if world > 1:
+        torch.cuda.synchronize()
         dist.barrier()
+        tp.close()
         dist.destroy_process_group()
     return out
 

@@ -226,6 +226,24 @@ int npub_f32_to_f16(const float* x, uint16_t* y, int64_t n, void* stream);
 /* fp16 -> fp32 (the cmodel's load of the G-buffer). */
 int npub_f16_to_f32(const uint16_t* x, float* y, int64_t n, void* stream);
 
+/* ---------------------------------------------- tensor-parallel all-reduce --
+ * One-shot fp16 all-reduce over NVLink peer memory for the decode-sized
+ * reductions after the row-parallel O and down projections (the TP sharding
+ * of the layer; the single-NPU reference has no counterpart).  Set-up: every
+ * rank calls npub_comm_create (allocates 2 x max_bytes of IPC-shareable
+ * staging plus flags; writes npub_comm_handle_bytes() bytes of handle), the
+ * handles are all-gathered in rank order by the caller (e.g. torch.distributed),
+ * then npub_comm_open maps the peers.  npub_allreduce_f16 sums n fp16 elements
+ * (n % 8 == 0, n * 2 <= max_bytes, 16-byte aligned; in may equal out) over
+ * the ranks in rank order with fp32 accumulation: every rank gets the same
+ * bits.  All ranks must make the same sequence of calls; waits on peers are
+ * bounded (2 s) and report NPUB_ERR_DEVICE_TIMEOUT through npub_device_error. */
+size_t npub_comm_handle_bytes(void);
+int npub_comm_create(int world, int rank, size_t max_bytes, void** comm, void* handle_out);
+int npub_comm_open(void* comm, const void* all_handles);
+int npub_allreduce_f16(void* comm, const void* in, void* out, int64_t n, void* stream);
+int npub_comm_destroy(void* comm);
+
 #ifdef __cplusplus
 }
 #endif

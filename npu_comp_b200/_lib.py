@@ -58,6 +58,11 @@ SIGNATURES = {
     "npub_isa_vector": (_i, [_u32, _p, _p, _p, _p, _i64, _p]),
     "npub_f32_to_f16": (_i, [_p, _p, _i64, _p]),
     "npub_f16_to_f32": (_i, [_p, _p, _i64, _p]),
+    "npub_comm_handle_bytes": (_sz, []),
+    "npub_comm_create": (_i, [_i, _i, _sz, ctypes.POINTER(ctypes.c_void_p), _p]),
+    "npub_comm_open": (_i, [_p, _p]),
+    "npub_allreduce_f16": (_i, [_p, _p, _p, _i64, _p]),
+    "npub_comm_destroy": (_i, [_p]),
 }
 
 _lock = threading.Lock()

@@ -84,15 +84,32 @@ class LayerWeights:
 
 @dataclass
 class TP:
-    """Tensor-parallel context: rank/size and the process group (None = 1 GPU)."""
+    """Tensor-parallel context: rank/size and the process group (None = 1 GPU).
+
+    all_reduce sums decode-sized fp16 tensors (<= 1 MB) with the NVLink
+    peer-memory kernel of npu_comp_b200.comm and larger ones with NCCL."""
     rank: int = 0
     size: int = 1
     group: Optional[object] = None
+    peer: Optional[object] = None
 
     def all_reduce(self, t: torch.Tensor) -> None:
-        if self.size > 1:
-            import torch.distributed as dist
-            dist.all_reduce(t, group=self.group)
+        if self.size <= 1:
+            return
+        import torch.distributed as dist
+        from . import comm
+        if t.is_cuda:
+            if self.peer is None and comm.enabled() and dist.get_backend(self.group) == "nccl":
+                self.peer = comm.PeerAllReduce(self.group, t.device)
+            if self.peer is not None and self.peer.fits(t):
+                self.peer.all_reduce_(t)
+                return
+        dist.all_reduce(t, group=self.group)
+
+    def close(self) -> None:
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
 
 def _shard_rows(q: torch.Tensor, s: torch.Tensor, blocks: List[range]) -> (torch.Tensor, torch.Tensor):
@@ -388,6 +405,11 @@ class LlamaStack:
         self.use_graph = use_graph
         self.graph = None
         self.positions = torch.arange(prompt_len, device=device, dtype=torch.int32).repeat(batch)
+        if tp.size > 1 and tp.peer is None:  # set up outside any graph capture
+            import torch.distributed as dist
+            from . import comm
+            if comm.enabled() and dist.get_backend(tp.group) == "nccl":
+                tp.peer = comm.PeerAllReduce(tp.group, device)
 
     # -- greedy selection over the (possibly vocab-sharded) lm_head
     def _next_ids(self, xl: torch.Tensor) -> None:

@@ -56,6 +56,7 @@ def _worker(rank, world, port, q):
             ed = ((yd.float() - yd1.float()).abs().max() / yd1.float().abs().max()).item()
             q.put((e, ed))
         dist.barrier()
+        tp.close()
     finally:
         dist.destroy_process_group()
 
@@ -75,3 +76,73 @@ def test_tp2_layer_matches_single_gpu():
         assert p.exitcode == 0
     assert e <= TOL, e
     assert ed <= TOL, ed
+
+
+def _ar_worker(rank, world, port, q):
+    import datetime
+    import torch.distributed as dist
+    from npu_comp_b200 import comm
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        peer = comm.PeerAllReduce(dist.group.WORLD, dev, max_bytes=1 << 20)
+        errs, same = [], []
+        sizes = [32 * 4096, 8, 4096 * 64, 1000 * 8, 32 * 4096, (1 << 20) // 2]
+        for i, n in enumerate(sizes * 2):
+            g = torch.Generator(device=dev).manual_seed(1000 * i + rank)
+            x = torch.randn(n, generator=g, device=dev).half()
+            allx = [torch.empty_like(x) for _ in range(world)]
+            dist.all_gather(allx, x)
+            ref = torch.stack([a.float() for a in allx]).sum(0)
+            peer.all_reduce_(x)
+            errs.append(((x.float() - ref).abs().max() / ref.abs().max()).item())
+            got = [torch.empty_like(x) for _ in range(world)]
+            dist.all_gather(got, x)
+            same.append(all(torch.equal(got[0], o) for o in got))
+        # replayed from a CUDA graph: the per-block epochs advance on the device
+        x = torch.ones(32 * 4096, device=dev, dtype=torch.float16) * (rank + 1)
+        y = x.clone()
+        gr = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(gr, stream=s):
+                y.copy_(x)
+                peer.all_reduce_(y)
+        torch.cuda.synchronize()
+        graph_ok = True
+        for _ in range(5):
+            gr.replay()
+            torch.cuda.synchronize()
+            graph_ok &= bool((y.float() == world * (world + 1) / 2).all())
+        del gr
+        torch.cuda.synchronize()
+        dist.barrier()
+        peer.close()
+        if rank == 0:
+            q.put((max(errs), all(same), graph_ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_allreduce_2gpu():
+    """npub_allreduce_f16 on 2 GPUs: the fp32 sum within fp16 rounding, the same
+    bits on every rank, across message sizes and from a replayed CUDA graph."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ar_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    err, same, graph_ok = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert err <= 1e-3, err
+    assert same
+    assert graph_ok
