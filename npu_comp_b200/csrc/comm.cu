@@ -30,7 +30,7 @@
 namespace npub {
 
 constexpr int kCommMaxRanks = 8;
-constexpr int kCommMaxBlocks = 64;
+constexpr int kCommMaxBlocks = 256;  // fixed regions: 4 KB each at max_bytes = 1 MB
 constexpr int kCommThreads = 256;
 
 struct CommDev {
@@ -57,12 +57,13 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
+// Relaxed system-scope load: coherent with the peers' writes (no stale
+// cache line) and, unlike a volatile load, free to overlap with the others.
+__device__ __forceinline__ uint4 ld_relaxed_sys_v4(const void* p) {
     uint4 v;
-    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+    asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p)
-                 : "memory");
+                 : "l"(p));
     return v;
 }
 
@@ -110,12 +111,18 @@ __global__ void __launch_bounds__(kCommThreads) allreduce_oneshot_kernel(const C
     if (ok_s) {
         // 4. sum slice b over the ranks, in rank order
         for (int64_t i = v0 + threadIdx.x; i < v1; i += blockDim.x) {
+            // every rank's vector in flight before the first is added
+            uint4 u[kCommMaxRanks];
+#pragma unroll
+            for (int r = 0; r < kCommMaxRanks; ++r)
+                if (r < c.world) u[r] = ld_relaxed_sys_v4(reinterpret_cast<const uint4*>(c.data[r] + off) + i);
             float acc[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) acc[k] = 0.0f;
-            for (int r = 0; r < c.world; ++r) {
-                const uint4 u = ld_volatile_v4(reinterpret_cast<const uint4*>(c.data[r] + off) + i);
-                const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+            for (int r = 0; r < kCommMaxRanks; ++r) {
+                if (r >= c.world) break;
+                const __half2* h2 = reinterpret_cast<const __half2*>(&u[r]);
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     const float2 f = __half22float2(h2[k]);
