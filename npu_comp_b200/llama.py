@@ -305,9 +305,7 @@ def layer_decode(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, k_cache: to
     ctx = npu.attention_decode(q, k_cache, v_cache, heads=hq, kv_heads=hk, lens=lens, ctx_len=ctx_max,
                                out=sc.get("dctx", (B, hq * hd), device=dev))
     mk("o_gemm")
-    attn = npu.matmul(ctx, w.wo, w.so, out=sc.get("dattn", (B, d), device=dev))
-    mk("all_reduce")
-    tp.all_reduce(attn)
+    attn = _row_parallel(ctx, w.wo, w.so, tp, sc.get("dattn", (B, d), device=dev), mk)
     mk("rmsnorm")
     h = sc.get("dh", (B, d), device=dev)
     hn, _ = npu.rmsnorm(attn, w.g2, cfg.eps, residual=x, residual_out=h, out=sc.get("dhn", (B, d), device=dev))
@@ -316,14 +314,26 @@ def layer_decode(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, k_cache: to
     mk("swiglu")
     a = npu.swiglu(gu, out=sc.get("dact", (B, w.ffn), device=dev))
     mk("down_gemm")
-    ffn = npu.matmul(a, w.wd, w.sd, out=sc.get("dffn", (B, d), device=dev))
-    mk("all_reduce")
-    tp.all_reduce(ffn)
+    ffn = _row_parallel(a, w.wd, w.sd, tp, sc.get("dffn", (B, d), device=dev), mk)
     mk("residual")
     y = out if out is not None else torch.empty((B, d), dtype=torch.float16, device=dev)
     npu.add(ffn, h, out=y)
     mk.end()
     return y
+
+
+def _row_parallel(a: torch.Tensor, wq: torch.Tensor, s: torch.Tensor, tp: TP, out: torch.Tensor, mk) -> torch.Tensor:
+    """Row-parallel projection of a decode step followed by its all-reduce: one
+    fused GEMM + peer-memory reduction kernel when the shape allows, else the
+    GEMM and then TP.all_reduce."""
+    if tp.size > 1 and tp.peer is not None and tp.peer.gemm_fits(a.shape[0], wq.shape[0]):
+        tp.peer.matmul_allreduce(a, wq, s, out=out)
+        mk("all_reduce")  # fused into the GEMM
+        return out
+    npu.matmul(a, wq, s, out=out)
+    mk("all_reduce")
+    tp.all_reduce(out)
+    return out
 
 
 def layer_flops(cfg: LlamaConfig, tokens: int, ctx: int, causal: bool = True) -> float:
