@@ -380,8 +380,10 @@ __global__ void __launch_bounds__(kStThreads) decode_attn_stream_kernel(const De
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
     }
-    // merge the four warps (the ring is idle now: every copy has landed and been read)
-    __syncthreads();
+    // merge the compute warps (the ring is idle now: every copy has landed and
+    // been read); only lane 0 of the producer warp ran the copy loop, hence the
+    // thread-counting barrier
+    cta_sync_divergent();
     float* mg = reinterpret_cast<float*>(ring);  // [warp][g][130]: acc[128], m, l
     if (warp < kStWarps) {
 #pragma unroll

@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(kCommThreads) allreduce_oneshot_kernel(const C
             if (err) atomicCAS(err, 0, 0x501);
         }
     }
-    __syncthreads();
+    cta_sync_divergent();  // lanes < world spun alone
     if (ok_s) {
         // 4. sum slice b over the ranks, in rank order
         for (int64_t i = v0 + threadIdx.x; i < v1; i += blockDim.x) {

@@ -135,6 +135,11 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -259,8 +264,16 @@ __device__ __forceinline__ uint32_t nclusters_x() {
     asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
     return r;
 }
+// CTA-wide barrier for code where lanes of a warp may arrive separately
+// (role loops run by lane 0 only).  The non-.aligned form counts threads, not
+// warps: __syncthreads() (bar.sync, .aligned) was measured here to release
+// threads before every warp of such a CTA had arrived, even after __syncwarp().
+__device__ __forceinline__ void cta_sync_divergent() { asm volatile("barrier.sync 0;" ::: "memory"); }
+
+// Cluster-wide barrier; the non-.aligned forms, for the same reason as
+// cta_sync_divergent (callers reach it from lane-0-only role loops).
 __device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 // Shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t local_addr, uint32_t rank) {

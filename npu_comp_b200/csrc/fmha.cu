@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         tmem_relinquish();
     }
     tc_fence_before();
-    __syncthreads();
+    cta_sync_divergent();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     int never = 0;
@@ -335,8 +335,9 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         }
     }
 
+    // Lane 0 alone ran some warps' role loops: a thread-counting barrier.
     tc_fence_before();
-    __syncthreads();
+    cta_sync_divergent();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, 512);

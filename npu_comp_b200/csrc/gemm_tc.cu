@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         tmem_relinquish();
     }
     tc_fence_before();
-    __syncthreads();
+    cta_sync_divergent();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     int never = 0;
@@ -288,8 +288,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         }
     }
 
+    // Lane 0 alone ran some warps' role loops: a thread-counting barrier.
     tc_fence_before();
-    __syncthreads();
+    cta_sync_divergent();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, BT);

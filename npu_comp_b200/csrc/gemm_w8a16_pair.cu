@@ -333,8 +333,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<G>(), 1)
         }
     }
 
+    // Lane 0 alone ran some warps' role loops: a thread-counting barrier.
     tc_fence_before();
-    __syncthreads();
+    cta_sync_divergent();
     cluster_sync();  // no CTA leaves while its peer may still signal or read it
     if (warp == 1) {
         tc_fence_after();

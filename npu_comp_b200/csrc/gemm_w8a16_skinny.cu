@@ -9,14 +9,17 @@
 //
 //  * stream-K: the (tile, 256-wide K step) units are cut into one contiguous
 //    range per CTA, grid = SM count, so every SM streams the same number of
-//    weight bytes whatever N / 128 is.  A tile cut between CTAs is finished by
-//    whichever of its CTAs arrives last on the tile's counter (one counter per
-//    32-row quarter, so each epilogue warp works alone): every piece stores an
-//    fp32 partial, and the last one sums the pieces in CTA order -- a fixed
-//    order, so results do not depend on timing.  No CTA waits on another.
-//  * a CTA works on its cut tiles first (the head of its last tile, then the
-//    tail of its first) and on its whole tiles after, so the partial-sum
-//    round trips through L2 overlap the main loop instead of ending it.
+//    weight bytes whatever N / 128 is.  A CTA walks its range in order, so a
+//    tile cut between CTAs is the last tile of the CTA holding its first K
+//    step (the tile's finisher) and the first tile of every other CTA holding
+//    a piece of it.  Those other pieces are therefore done early: each stores
+//    an fp32 partial and bumps the tile's counter (one per 32-row quarter, so
+//    each epilogue warp works alone).  The finisher, at the end of its range,
+//    waits for the counter, adds the partials to its own accumulator (read
+//    straight from TMEM) in CTA order -- a fixed order, so results do not
+//    depend on timing -- and stores the tile.  Only finishers wait, and only
+//    on pieces that other CTAs compute first, so no wait can close a cycle;
+//    grid <= SM count with one CTA per SM keeps every CTA resident.
 //  * the converted weights never touch shared memory: converter warps read
 //    the int8 tile (128-byte swizzled, conflict-free), turn it into fp16 in
 //    registers and store it into tensor memory with tcgen05.st, where the
@@ -160,7 +163,6 @@ __device__ __forceinline__ int64_t unit_owner(int64_t u, int64_t U, int64_t G) {
 struct Range {
     int64_t u0, u1;
     int KT, tA, tB, nseg;
-    bool cutA, cutB;  // first / last tile only partly in the range
 };
 
 __device__ __forceinline__ Range make_range(int64_t u0, int64_t u1, int KT) {
@@ -171,27 +173,17 @@ __device__ __forceinline__ Range make_range(int64_t u0, int64_t u1, int KT) {
     r.tA = (int)(u0 / KT);
     r.tB = (int)((u1 - 1) / KT);
     r.nseg = u1 > u0 ? r.tB - r.tA + 1 : 0;
-    r.cutA = u0 != (int64_t)r.tA * KT || u1 < (int64_t)(r.tA + 1) * KT;
-    r.cutB = r.nseg >= 2 && u1 != (int64_t)(r.tB + 1) * KT;
     return r;
 }
 
 struct Seg {
     int tile, k0, nk;  // K steps [k0, k0 + nk) of the tile
     bool full;         // the whole tile: finished here, no partial
-    bool first;        // the range's first tile (partial slot 0, else 1)
 };
 
-// i-th segment in processing order: the cut last tile, the cut first tile,
-// then the whole tiles in order.
+// i-th segment in processing order: the range's tiles in ascending order.
 __device__ __forceinline__ Seg seg_in_order(const Range& r, int i) {
-    int t;
-    const int lead = (r.cutB ? 1 : 0) + (r.cutA ? 1 : 0);
-    if (i < lead) {
-        t = (r.cutB && i == 0) ? r.tB : r.tA;
-    } else {
-        t = r.tA + (r.cutA ? 1 : 0) + (i - lead);
-    }
+    const int t = r.tA + i;
     Seg s;
     s.tile = t;
     const int64_t ts = (int64_t)t * r.KT, te = ts + r.KT;
@@ -199,7 +191,6 @@ __device__ __forceinline__ Seg seg_in_order(const Range& r, int i) {
     s.k0 = (int)(a - ts);
     s.nk = (int)(b - a);
     s.full = s.nk == r.KT;
-    s.first = t == r.tA;
     return s;
 }
 
@@ -258,13 +249,14 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
         tmem_relinquish();
     }
     tc_fence_before();
-    __syncthreads();
+    cta_sync_divergent();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     int never = 0;
     volatile int* no_abort = &never;
-    if (warp == 0 && lane == 0) {
+    if (warp == 3 && lane == 0) {
         // the first weight tiles go to L2 while the previous kernel finishes
+        // (an otherwise idle warp, so the producer's first load is not held up)
         uint32_t n = 0;
         for (int i = 0; i < rg.nseg && n < (uint32_t)kS8; ++i) {
             const Seg sg = seg_in_order(rg, i);
@@ -407,6 +399,80 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
             const bool nrow = n < p.N;
             // the scale load is in flight while the accumulator is waited for
             const float sc = p.alpha * ((p.scale && nrow) ? __half2float(__ldg(p.scale + n)) : 1.0f);
+            // A tile cut between CTAs: its finisher is the CTA holding its first
+            // K step; every other piece is the first tile of its CTA, whose one
+            // partial slot it fills.
+            int64_t c_first = blockIdx.x, c_last = blockIdx.x;
+            if (!sg.full) {
+                c_first = unit_owner((int64_t)sg.tile * KT, U, G);
+                c_last = unit_owner((int64_t)sg.tile * KT + KT - 1, U, G);
+            }
+            const bool finisher = !sg.full && c_first == (int64_t)blockIdx.x;
+            unsigned* cnt = p.cnt + 4 * sg.tile + q;
+            // The finisher's epilogue warps wait for the other pieces while its
+            // own MMAs run (they were computed first, so the wait is short) and
+            // sum them in CTA order into S; the tile is own + S.
+            float S[BT];
+            if (finisher) {
+                bool ok = true;
+                if (lane == 0) {
+                    const unsigned want = (unsigned)(c_last - c_first);
+                    ok = ld_acquire_gpu(cnt) >= want;
+                    if (!ok) {
+                        const uint64_t t0 = globaltimer_ns();
+                        for (uint32_t it = 1;; ++it) {
+                            if (ld_acquire_gpu(cnt) >= want) {
+                                ok = true;
+                                break;
+                            }
+                            if ((it & 255u) == 0 && (*abort_flag || globaltimer_ns() - t0 > 2000000000ull)) break;
+                        }
+                    }
+                    if (ok) *cnt = 0u;  // left zero for the next call
+                }
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                if (!ok) {
+                    set_err(p.err, 0x309);
+                    *abort_flag = 1;
+                    break;
+                }
+                __threadfence();
+                {
+                    // the first later piece straight into S, all loads in flight
+                    const float4* pp = reinterpret_cast<const float4*>(p.part + ((c_first + 1) * kRows + r) * BT);
+#pragma unroll
+                    for (int c0 = 0; c0 < BT; c0 += 16) {
+                        if (c0 < M) {
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const float4 x = ld_cg_f4(pp + c0 / 4 + j);
+                                S[c0 + 4 * j] = x.x;
+                                S[c0 + 4 * j + 1] = x.y;
+                                S[c0 + 4 * j + 2] = x.z;
+                                S[c0 + 4 * j + 3] = x.w;
+                            }
+                        }
+                    }
+                }
+                for (int64_t c = c_first + 2; c <= c_last; ++c) {
+                    const float4* pp = reinterpret_cast<const float4*>(p.part + (c * kRows + r) * BT);
+#pragma unroll
+                    for (int c0 = 0; c0 < BT; c0 += 16) {
+                        if (c0 < M) {
+                            float4 x[4];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) x[j] = ld_cg_f4(pp + c0 / 4 + j);
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                S[c0 + 4 * j] += x[j].x;
+                                S[c0 + 4 * j + 1] += x[j].y;
+                                S[c0 + 4 * j + 2] += x[j].z;
+                                S[c0 + 4 * j + 3] += x[j].w;
+                            }
+                        }
+                    }
+                }
+            }
             bool have = mbar_wait_bounded(&acc_full[b], bph, abort_flag);
             if (!have) set_err(p.err, 0x307);
             have = __all_sync(0xffffffffu, have);
@@ -517,68 +583,45 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                 if (ar) ar_finish();
                 continue;
             }
-            // A piece of a tile shared with other CTAs: store the fp32 partial,
-            // [slot][row][BT], one 16-column chunk of this row per float4 x 4.
-            const int64_t slot = 2 * (int64_t)blockIdx.x + (sg.first ? 0 : 1);
-            float4* mine = reinterpret_cast<float4*>(p.part + (slot * kRows + r) * BT);
-            for (int c0 = 0; c0 < BT && c0 < M; c0 += 16) {
-                float v[16];
-                tmem_ld16(lane_base + b * (uint32_t)BT + (uint32_t)c0, v);
+            if (!finisher) {
+                // a later piece: fp32 partial [slot = CTA][row][BT], then publish it
+                float4* mine = reinterpret_cast<float4*>(p.part + ((int64_t)blockIdx.x * kRows + r) * BT);
+                for (int c0 = 0; c0 < BT && c0 < M; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(lane_base + b * (uint32_t)BT + (uint32_t)c0, v);
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    st_cg_f4(mine + c0 / 4 + j, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+                    for (int j = 0; j < 4; ++j)
+                        st_cg_f4(mine + c0 / 4 + j, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[b]);
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) atomicAdd(cnt, 1u);
+                continue;
+            }
+            // the finisher: own accumulator + S, scaled and stored
+#pragma unroll
+            for (int c0 = 0; c0 < BT; c0 += 16) {
+                if (c0 < M) {
+                    float v[16];
+                    tmem_ld16(lane_base + b * (uint32_t)BT + (uint32_t)c0, v);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] += S[c0 + j];
+                    emit(c0, v);
+                }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[b]);
-            const int64_t c_first = unit_owner((int64_t)sg.tile * KT, U, G);
-            const int64_t c_last = unit_owner((int64_t)sg.tile * KT + KT - 1, U, G);
-            __threadfence();
-            __syncwarp();
-            unsigned old = 0;
-            if (lane == 0) old = atomicAdd(p.cnt + 4 * sg.tile + q, 1u);
-            old = __shfl_sync(0xffffffffu, old, 0);
-            if (old != (unsigned)(c_last - c_first)) continue;
-            // Last piece in: sum every piece in CTA order, finish the rows.
-            __threadfence();
-            if (lane == 0) p.cnt[4 * sg.tile + q] = 0u;  // left zero for the next call
-            for (int c0 = 0; c0 < BT && c0 < M; c0 += 16) {
-                float4 acc[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int64_t c = c_first; c <= c_last; c += 4) {
-                    // up to four pieces' loads in flight, then added in CTA order
-                    float4 x[4][4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int64_t cc = c + i <= c_last ? c + i : c;
-                        const int64_t sl = 2 * cc + (unit_start(cc, U, G) / KT == sg.tile ? 0 : 1);
-                        const float4* pp = reinterpret_cast<const float4*>(p.part + (sl * kRows + r) * BT) + c0 / 4;
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) x[i][j] = ld_cg_f4(pp + j);
-                    }
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        if (c + i > c_last) break;
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            acc[j].x += x[i][j].x;
-                            acc[j].y += x[i][j].y;
-                            acc[j].z += x[i][j].z;
-                            acc[j].w += x[i][j].w;
-                        }
-                    }
-                }
-                const float v[16] = {acc[0].x, acc[0].y, acc[0].z, acc[0].w, acc[1].x, acc[1].y, acc[1].z, acc[1].w,
-                                     acc[2].x, acc[2].y, acc[2].z, acc[2].w, acc[3].x, acc[3].y, acc[3].z, acc[3].w};
-                emit(c0, v);
-            }
             if (ar) ar_finish();
         }
     }
 
+    // Lane 0 alone ran some warps' role loops: a thread-counting barrier.
     tc_fence_before();
-    __syncthreads();
+    cta_sync_divergent();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
@@ -620,10 +663,12 @@ bool w8a16_skinny_fits(int M, int N) {
            (size_t)4 * ((N + skinny::kRows - 1) / skinny::kRows) * sizeof(unsigned) <= kSkinnyCounterBytes;
 }
 
-// Measured on B200 (decode-layer shapes, weights streamed from HBM): the
-// stream-K kernel wins where the weight matrix is wide (its tiles spread over
-// every SM); the 2-CTA pair kernel wins on K-long or N <= 8192 matrices at
-// M = 64, where its wider MMAs issue fewer instructions per weight byte.
+// Measured on B200 (decode-layer shapes, weights streamed from HBM, CUDA
+// graph replay): the stream-K kernel wins on every matrix with N >= 8192 and,
+// at M <= 32, on K-long ones (4096 x 11008: 22.1 vs 23.3 us); the 2-CTA pair
+// kernel wins on the small square ones (4096 x 4096: 12.8 vs 14.3 us at
+// M = 32) and on K-long ones at M = 64, where its wider MMAs issue fewer
+// instructions per weight byte.
 // NPUB_W8A16_KERNEL=pair or =skinny in the environment overrides the choice
 // (where the shape allows it), for measuring both kernels on one shape.
 static int kernel_override() {
@@ -641,12 +686,12 @@ bool w8a16_use_skinny(int M, int N, int K) {
     if (!w8a16_skinny_fits(M, N) || K <= 0) return false;
     const int o = kernel_override();
     if (o) return o == 2;
-    return (M <= 32 && N >= 8192) || N >= 16384;
+    return N >= 8192 || (M <= 32 && K >= 8192);
 }
 
 size_t w8a16_skinny_workspace(int M, int N, int K) {
     if (!w8a16_skinny_fits(M, N) || K <= 0) return 0;
-    return kSkinnyCounterBytes + (size_t)2 * skinny_grid(N, K) * skinny_bt(M) * skinny::kRows * sizeof(float);
+    return kSkinnyCounterBytes + (size_t)skinny_grid(N, K) * skinny_bt(M) * skinny::kRows * sizeof(float);
 }
 
 int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C, int64_t ldc,
