@@ -210,6 +210,18 @@ int npub_rope_kv_append(void* qkv, int64_t ldx, int tokens, int q_heads, int kv_
                         const int32_t* positions, float theta, void* k_cache, void* v_cache, int64_t cap,
                         int32_t* lens, void* stream);
 
+/* Prompt counterpart of npub_rope_kv_append (prefill; the reference rotates
+ * q and k with the same macros, llama_layer.py:96-112, and keeps no cache).
+ * qkv holds tokens = batch * tokens_per_seq rows, row r belonging to sequence
+ * r / tokens_per_seq; q and k are rotated in place with positions[r], and the
+ * rotated k and the v heads are written to k_cache / v_cache
+ * [batch, kv_heads, cap, head_dim] at slot positions[r].  A row whose
+ * position lies outside [0, cap) is rotated but not stored.  One kernel in
+ * place of npub_rope and two strided cache copies. */
+int npub_rope_kv_store(void* qkv, int64_t ldx, int tokens, int tokens_per_seq, int q_heads, int kv_heads,
+                       int head_dim, const int32_t* positions, float theta, void* k_cache, void* v_cache, int64_t cap,
+                       void* stream);
+
 /* ------------------------------------------------- NPU ISA semantics ----
  * One compute instruction of the NPU over PE buffers (_poc/mysim.cpp:114-141):
  * `word` is the 32-bit instruction (opcodes 0x01-0x13 vector, 0x40-0x43

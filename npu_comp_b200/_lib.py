@@ -55,6 +55,7 @@ SIGNATURES = {
     "npub_attention_decode_workspace": (_sz, [_i, _i, _i, _i]),
     "npub_kv_append": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _p, _i, _i, _i, _i, _p]),
     "npub_rope_kv_append": (_i, [_p, _i64, _i, _i, _i, _i, _p, _f, _p, _p, _i64, _p, _p]),
+    "npub_rope_kv_store": (_i, [_p, _i64, _i, _i, _i, _i, _i, _p, _f, _p, _p, _i64, _p]),
     "npub_isa_vector": (_i, [_u32, _p, _p, _p, _p, _i64, _p]),
     "npub_f32_to_f16": (_i, [_p, _p, _i64, _p]),
     "npub_f16_to_f32": (_i, [_p, _p, _i64, _p]),

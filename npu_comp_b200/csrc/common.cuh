@@ -403,4 +403,69 @@ __device__ __forceinline__ float ex2_approx(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
+
+// ---- int8 weight conversion into tensor memory (W8A16 kernels)
+__device__ __forceinline__ uint32_t i8_perm_lo(uint32_t u) { return __byte_perm(u, 0x64646464u, 0x5140); }
+__device__ __forceinline__ uint32_t i8_perm_hi(uint32_t u) { return __byte_perm(u, 0x64646464u, 0x5342); }
+__device__ __forceinline__ uint32_t f16x2_sub1152(uint32_t h) {
+    __half2 v = *reinterpret_cast<__half2*>(&h);
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+    __half2 r = __hsub2(v, bias);
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+// 16 int8 -> 8 fp16 pairs (even K in the low half), exact: (q ^ 0x80) placed in
+// the mantissa of 1024.0 (0x6400 | byte), minus 1152.
+__device__ __forceinline__ void i8x16_to_f16x2(uint4 raw, uint32_t* o) {
+    const uint32_t w0 = raw.x ^ 0x80808080u, w1 = raw.y ^ 0x80808080u, w2 = raw.z ^ 0x80808080u,
+                   w3 = raw.w ^ 0x80808080u;
+    o[0] = f16x2_sub1152(i8_perm_lo(w0));
+    o[1] = f16x2_sub1152(i8_perm_hi(w0));
+    o[2] = f16x2_sub1152(i8_perm_lo(w1));
+    o[3] = f16x2_sub1152(i8_perm_hi(w1));
+    o[4] = f16x2_sub1152(i8_perm_lo(w2));
+    o[5] = f16x2_sub1152(i8_perm_hi(w2));
+    o[6] = f16x2_sub1152(i8_perm_lo(w3));
+    o[7] = f16x2_sub1152(i8_perm_hi(w3));
+}
+
+// 32 lanes x 32 columns of 32 bit from registers into tensor memory.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    __syncwarp();  // .sync.aligned: the whole warp, converged
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+        "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+        "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+        "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+    __syncwarp();
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16, A K-major in tensor memory
+// (one row per lane, two fp16 per 32-bit column).
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// The same with A in tensor memory for a 2-CTA pair (issued by the even CTA;
+// each CTA's tensor memory holds its 128 rows of A).
+__device__ __forceinline__ void tc_mma_f16_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                                   uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
 }  // namespace npub

@@ -23,6 +23,7 @@
 #include "common.cuh"
 #include "gemm_tc.h"
 #include "gemm_w8a16_pair.h"
+#include "gemm_w8a16_pair_ts.h"
 #include "gemm_w8a16_skinny.h"
 
 #include <cudaTypedefs.h>
@@ -423,6 +424,7 @@ static size_t linear_workspace(int M, int N, int K, bool w_int8) {
     if (w_int8) {
         // every W8A16 workspace starts with the stream-K kernel's counter region
         if (w8a16_use_skinny(M, N, K)) return w8a16_skinny_workspace(M, N, K);
+        if (w8a16_use_pair_ts(M, N, K)) return 0;
         const size_t pair = w8a16_pair_workspace(M, N, K);
         return pair ? kSkinnyCounterBytes + pair : 0;
     }
@@ -490,6 +492,8 @@ static int linear(bool w_int8, const void* A, int64_t lda, const void* W, int64_
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (w_int8 && w8a16_use_skinny(M, N, K))
         return w8a16_skinny_run(A, lda, W, ldw, scale, C, ldc, R, ldr, M, N, K, alpha, ws, ws_bytes, st);
+    if (w_int8 && w8a16_use_pair_ts(M, N, K))
+        return w8a16_pair_ts_run(A, lda, W, ldw, scale, C, ldc, R, ldr, M, N, K, alpha, st);
     if (w_int8) return linear_w8a16_pair(A, lda, W, ldw, scale, C, ldc, R, ldr, M, N, K, alpha, ws, ws_bytes, st);
 
     GemmParams p;
@@ -556,8 +560,9 @@ extern "C" size_t npub_w8a16_gemm_workspace(int M, int N, int K) { return npub::
 
 extern "C" const char* npub_w8a16_kernel_name(int M, int N, int K) {
     if (M <= 0 || N <= 0 || K <= 0) return "none";
-    return npub::w8a16_use_skinny(M, N, K) ? "w8a16_skinny_kernel (stream-K, tcgen05 with A in TMEM)"
-                                           : "w8a16_pair_kernel (tcgen05 cta_group::2 W8A16)";
+    if (npub::w8a16_use_skinny(M, N, K)) return "w8a16_skinny_kernel (stream-K, tcgen05 with A in TMEM)";
+    if (npub::w8a16_use_pair_ts(M, N, K)) return "w8a16_pair_ts_kernel (tcgen05 cta_group::2, A in TMEM)";
+    return "w8a16_pair_kernel (tcgen05 cta_group::2 W8A16)";
 }
 
 extern "C" int npub_f16_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C,

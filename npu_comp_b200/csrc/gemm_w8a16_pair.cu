@@ -54,20 +54,12 @@ struct Smem {
     static constexpr int kTotal = STAGES * (kBh + kA8) + CSTAGES * kA16 + kBars + 1024;
 };
 
-__device__ __forceinline__ uint32_t perm_lo(uint32_t u) { return __byte_perm(u, 0x64646464u, 0x5140); }
-__device__ __forceinline__ uint32_t perm_hi(uint32_t u) { return __byte_perm(u, 0x64646464u, 0x5342); }
-__device__ __forceinline__ uint32_t sub1152(uint32_t h) {
-    __half2 v = *reinterpret_cast<__half2*>(&h);
-    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
-    __half2 r = __hsub2(v, bias);
-    return *reinterpret_cast<uint32_t*>(&r);
-}
 // 16 int8 -> 16 fp16, exact: (q ^ 0x80) placed in the mantissa of 1024.0, minus 1152.
 __device__ __forceinline__ void cvt16(uint4 raw, uint4& lo, uint4& hi) {
     const uint32_t w0 = raw.x ^ 0x80808080u, w1 = raw.y ^ 0x80808080u, w2 = raw.z ^ 0x80808080u,
                    w3 = raw.w ^ 0x80808080u;
-    lo = make_uint4(sub1152(perm_lo(w0)), sub1152(perm_hi(w0)), sub1152(perm_lo(w1)), sub1152(perm_hi(w1)));
-    hi = make_uint4(sub1152(perm_lo(w2)), sub1152(perm_hi(w2)), sub1152(perm_lo(w3)), sub1152(perm_hi(w3)));
+    lo = make_uint4(f16x2_sub1152(i8_perm_lo(w0)), f16x2_sub1152(i8_perm_hi(w0)), f16x2_sub1152(i8_perm_lo(w1)), f16x2_sub1152(i8_perm_hi(w1)));
+    hi = make_uint4(f16x2_sub1152(i8_perm_lo(w2)), f16x2_sub1152(i8_perm_hi(w2)), f16x2_sub1152(i8_perm_lo(w3)), f16x2_sub1152(i8_perm_hi(w3)));
 }
 
 __device__ __forceinline__ void set_err(int* err, int code) {

@@ -288,7 +288,10 @@ __global__ void rope_vec_kernel(__half* x, int64_t ldx, int heads, int hd, const
 // q and k heads are rotated in place exactly as rope_vec_kernel does; k and v
 // heads are also written to cache[t, h, pos[t], :]; CTA (t, 0) writes
 // lens[t] = pos[t] + 1 (the attention length of the step).
-__global__ void rope_kv_append_kernel(__half* x, int64_t ldx, int hq, int hk, int hd,
+// Row t belongs to sequence t / tps (tps = 1 for a decode step); blockIdx.y
+// takes heads [hpb * y, hpb * y + hpb).  A position outside [0, cap) is
+// rotated but not stored.
+__global__ void rope_kv_append_kernel(__half* x, int64_t ldx, int hq, int hk, int hd, int tps, int hpb,
                                       const int32_t* __restrict__ pos, float log2_theta, __half* __restrict__ kc,
                                       __half* __restrict__ vc, int64_t cap, int32_t* __restrict__ lens) {
     pdl_trigger();
@@ -307,8 +310,10 @@ __global__ void rope_kv_append_kernel(__half* x, int64_t ldx, int hq, int hk, in
     }
     __syncthreads();
     __half* row = x + (int64_t)t * ldx;
-    const int h0 = blockIdx.y * 8;
-    const int h1 = min(h0 + 8, hq + 2 * hk);
+    const int64_t seq = t / tps;
+    const bool store = p >= 0 && (int64_t)p < cap;
+    const int h0 = blockIdx.y * hpb;
+    const int h1 = min(h0 + hpb, hq + 2 * hk);
     const int per_head = half / 8;
     for (int i = threadIdx.x; i < (h1 - h0) * per_head; i += blockDim.x) {
         const int hh = h0 + i / per_head, k0 = (i % per_head) * 8;
@@ -331,10 +336,10 @@ __global__ void rope_kv_append_kernel(__half* x, int64_t ldx, int hq, int hk, in
             *reinterpret_cast<uint4*>(a) = o1;
             *reinterpret_cast<uint4*>(a + half) = o2;
         }
-        if (hh >= hq) {  // k and v heads go to the caches
+        if (hh >= hq && store) {  // k and v heads go to the caches
             const bool isk = hh < hq + hk;
             const int kvh = isk ? hh - hq : hh - hq - hk;
-            __half* dst = (isk ? kc : vc) + (((int64_t)t * hk + kvh) * cap + p) * hd + k0;
+            __half* dst = (isk ? kc : vc) + ((seq * hk + kvh) * cap + p) * hd + k0;
             *reinterpret_cast<uint4*>(dst) = o1;
             *reinterpret_cast<uint4*>(dst + half) = o2;
         }
@@ -566,8 +571,30 @@ extern "C" int npub_rope_kv_append(void* qkv, int64_t ldx, int tokens, int q_hea
     if (groups == 0) return NPUB_OK;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     return launch_pdl(rope_kv_append_kernel, dim3(tokens, groups), dim3(64), 0, st, reinterpret_cast<__half*>(qkv),
-                      ldx, q_heads, kv_heads, head_dim, positions, log2f(theta), reinterpret_cast<__half*>(k_cache),
-                      reinterpret_cast<__half*>(v_cache), cap, lens);
+                      ldx, q_heads, kv_heads, head_dim, 1, 8, positions, log2f(theta),
+                      reinterpret_cast<__half*>(k_cache), reinterpret_cast<__half*>(v_cache), cap, lens);
+}
+
+extern "C" int npub_rope_kv_store(void* qkv, int64_t ldx, int tokens, int tokens_per_seq, int q_heads, int kv_heads,
+                                  int head_dim, const int32_t* positions, float theta, void* k_cache, void* v_cache,
+                                  int64_t cap, void* stream) {
+    NPUB_CHECK_ARG(tokens >= 0 && q_heads >= 0 && kv_heads >= 0);
+    if (tokens == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(tokens_per_seq > 0 && tokens % tokens_per_seq == 0);
+    NPUB_CHECK_ARG(qkv && positions && k_cache && v_cache && theta > 0.0f && cap > 0);
+    NPUB_CHECK_ARG(head_dim % 16 == 0 && head_dim > 0 && head_dim <= 512);
+    NPUB_CHECK_ARG(ldx >= (int64_t)(q_heads + 2 * kv_heads) * head_dim && ldx % 8 == 0);
+    NPUB_CHECK_ARG(npub_aligned(qkv, 16) && npub_aligned(k_cache, 16) && npub_aligned(v_cache, 16));
+    // a block rotates/stores up to 32 heads of one row (8 vectors of 8 per
+    // head at head_dim 128: one per thread)
+    const int hpb = 32;
+    const int groups = (q_heads + 2 * kv_heads + hpb - 1) / hpb;
+    if (groups == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(groups <= 65535);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    return launch_pdl(rope_kv_append_kernel, dim3(tokens, groups), dim3(256), 0, st, reinterpret_cast<__half*>(qkv),
+                      ldx, q_heads, kv_heads, head_dim, tokens_per_seq, hpb, positions, log2f(theta),
+                      reinterpret_cast<__half*>(k_cache), reinterpret_cast<__half*>(v_cache), cap, nullptr);
 }
 
 extern "C" int npub_quantize_w8(const float* W, int64_t ldw, int K, int N, int8_t* Wq, int64_t ldq, void* scale,

@@ -245,9 +245,11 @@ def layer_prefill(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, *, batch: 
     k = qkv[:, hq * hd:(hq + hk) * hd]
     v = qkv[:, (hq + hk) * hd:]
     mk("rope")
-    npu.rope(qkv, hq + hk, hd, positions=positions, theta=cfg.theta)  # q and k heads are adjacent columns
     if kv_out is not None:
-        _store_prompt_kv(k, v, kv_out, batch, T, hk, hd)
+        # q, k rotated in place and the prompt's K, V stored into the caches, one kernel
+        npu.rope_kv_store(qkv, hq, hk, hd, positions, kv_out[0], kv_out[1], tokens_per_seq=T, theta=cfg.theta)
+    else:
+        npu.rope(qkv, hq + hk, hd, positions=positions, theta=cfg.theta)  # q and k heads are adjacent columns
     mk("attention")
     ctx = npu.attention(q, k, v, hq, hk, head_dim=hd, batch=batch, causal=True,
                         out=sc.get("ctx", (BT, hq * hd), device=dev))
@@ -272,13 +274,6 @@ def layer_prefill(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, *, batch: 
     npu.add(ffn, h, out=y)
     mk.end()
     return y
-
-
-def _store_prompt_kv(k, v, kv_out, batch, T, hk, hd):
-    kc, vc = kv_out
-    # [batch*T, hk*hd] -> [batch, hk, T, hd] into the first T slots of the caches
-    kc[:, :, :T, :].copy_(k.reshape(batch, T, hk, hd).transpose(1, 2))
-    vc[:, :, :T, :].copy_(v.reshape(batch, T, hk, hd).transpose(1, 2))
 
 
 def layer_decode(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, k_cache: torch.Tensor, v_cache: torch.Tensor,

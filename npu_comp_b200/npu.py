@@ -25,7 +25,7 @@ from ._lib import NpubError  # noqa: F401  (re-exported)
 
 __all__ = [
     "fp16", "quantize_w8", "matmul", "rmsnorm", "add", "swiglu", "softmax", "rope", "attention",
-    "attention_decode", "kv_append", "rope_kv_append", "embed", "argmax", "isa_vector", "f32_to_f16_bits", "f16_bits_to_f32", "NpubError",
+    "attention_decode", "kv_append", "rope_kv_append", "rope_kv_store", "embed", "argmax", "isa_vector", "f32_to_f16_bits", "f16_bits_to_f32", "NpubError",
 ]
 
 
@@ -369,6 +369,29 @@ def rope_kv_append(qkv: torch.Tensor, q_heads: int, kv_heads: int, head_dim: int
               "lens must be contiguous int32 CUDA [tokens]")
     _lib.call("npub_rope_kv_append", qkv.data_ptr(), ldx, T, q_heads, kv_heads, head_dim, positions.data_ptr(),
               float(theta), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[2], _ptr(lens), _stream())
+
+
+def rope_kv_store(qkv: torch.Tensor, q_heads: int, kv_heads: int, head_dim: int, positions: torch.Tensor,
+                  k_cache: torch.Tensor, v_cache: torch.Tensor, *, tokens_per_seq: int,
+                  theta: float = 10000.0) -> None:
+    """Prefill: rope() on the q and k heads of the fused QKV rows of `batch`
+    prompts (rows r = b * tokens_per_seq + i, in place) and the rotated k and the
+    v heads written to the caches [batch, kv_heads, cap, head_dim] at
+    positions[r], in one kernel."""
+    ldx = _mat(qkv, "qkv", torch.float16)
+    T = qkv.shape[0]
+    _need(tokens_per_seq > 0 and T % tokens_per_seq == 0, "rows must be a whole number of sequences")
+    _need(qkv.shape[1] >= (q_heads + 2 * kv_heads) * head_dim, "qkv has too few columns")
+    _need(positions.is_cuda and positions.dtype == torch.int32 and positions.numel() == T
+          and positions.is_contiguous(), "positions must be contiguous int32 CUDA [tokens]")
+    batch = T // tokens_per_seq
+    for c, nm in ((k_cache, "k_cache"), (v_cache, "v_cache")):
+        _need(c.is_cuda and c.dtype == torch.float16 and c.is_contiguous() and c.dim() == 4
+              and tuple(c.shape[:2]) == (batch, kv_heads) and c.shape[3] == head_dim,
+              f"{nm} must be contiguous fp16 CUDA [batch, kv_heads, cap, head_dim]")
+    _lib.call("npub_rope_kv_store", qkv.data_ptr(), ldx, T, tokens_per_seq, q_heads, kv_heads, head_dim,
+              positions.data_ptr(), float(theta), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[2],
+              _stream())
 
 
 def isa_vector(word: int, in1: torch.Tensor, in2: Optional[torch.Tensor] = None,

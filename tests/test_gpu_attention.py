@@ -93,6 +93,34 @@ def test_decode_matches_last_prefill_row(cuda_device, rng):
     assert e <= TOL
 
 
+@pytest.mark.parametrize("B,T,H,KV,hd,cap", [(3, 37, 8, 4, 128, 50), (2, 64, 32, 32, 128, 80), (4, 9, 6, 2, 64, 9),
+                                              (1, 5, 40, 8, 128, 5)])
+def test_rope_kv_store_matches_separate_ops(cuda_device, B, T, H, KV, hd, cap):
+    """The fused prefill op equals rope() on q|k heads of every prompt row, then
+    a strided copy of the rotated k and the v heads into cache slots
+    [b, h, positions[r]], bit for bit; rows whose position is outside
+    [0, cap) are rotated but leave the caches alone."""
+    g = torch.Generator(device=cuda_device).manual_seed(B * T + H)
+    qkv = torch.randn((B * T, (H + 2 * KV) * hd), generator=g, device=cuda_device).half()
+    pos = torch.arange(T, device=cuda_device, dtype=torch.int32).repeat(B) + 2
+    pos[T - 1] = cap + 3  # first prompt's last row: out of range, not stored
+    kc = torch.randn((B, KV, cap, hd), generator=g, device=cuda_device).half()
+    vc = torch.randn_like(kc)
+    q1, kc1, vc1 = qkv.clone(), kc.clone(), vc.clone()
+    nb.rope(q1, H + KV, hd, positions=pos, theta=10000.0)
+    k1 = q1[:, H * hd:(H + KV) * hd].reshape(B, T, KV, hd)
+    v1 = q1[:, (H + KV) * hd:].reshape(B, T, KV, hd)
+    for b in range(B):
+        for t in range(T):
+            p = int(pos[b * T + t])
+            if 0 <= p < cap:
+                kc1[b, :, p] = k1[b, t]
+                vc1[b, :, p] = v1[b, t]
+    nb.rope_kv_store(qkv, H, KV, hd, pos, kc, vc, tokens_per_seq=T, theta=10000.0)
+    assert torch.equal(qkv, q1)
+    assert torch.equal(kc, kc1) and torch.equal(vc, vc1)
+
+
 @pytest.mark.parametrize("B,H,KV,hd,cap", [(5, 8, 4, 128, 40), (3, 32, 32, 128, 300), (2, 6, 2, 64, 17)])
 def test_rope_kv_append_matches_separate_ops(cuda_device, B, H, KV, hd, cap):
     """The fused decode-step op equals rope() on q|k heads, then kv_append(),

@@ -52,7 +52,8 @@ def test_quantizer_bit_exact(cuda_device, rng, K, N):
 
 SHAPES = [(64, 512, 512), (1, 1000, 256), (8, 64, 64), (128, 128, 64), (200, 300, 160), (129, 257, 96),
           (333, 777, 1024), (64, 12288, 4096), (64, 4096, 1376), (512, 256, 11008), (2048, 4096, 4096),
-          (32, 22016, 4096), (48, 1000, 4096), (16, 11008, 512), (64, 4096, 11008), (3, 128, 16)]
+          (32, 22016, 4096), (48, 1000, 4096), (16, 11008, 512), (64, 4096, 11008), (3, 128, 16),
+          (400, 300, 160), (1000, 777, 1376), (385, 257, 96), (4096, 512, 4096)]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
@@ -90,6 +91,21 @@ def test_w8a16_exact_known_answer(cuda_device, rng):
     C = nb.matmul(to_dev(A, cuda_device), to_dev(q, cuda_device), to_dev(s, cuda_device)).cpu().numpy()
     exact = ref.w8a16_ref(A, q, s)
     assert np.array_equal(C, exact.astype(np.float16))
+
+
+@pytest.mark.parametrize("M,N,K", [(500, 600, 384), (1000, 256, 4096), (384, 1000, 1376)])
+def test_w8a16_prefill_exact_known_answer(cuda_device, rng, M, N, K):
+    """Prefill shapes (M >= 384) run the tensor-memory pair kernel: 256 x 192
+    tiles, ragged in every dimension here.  Small integers keep every sum exact."""
+    A = rng.integers(-3, 4, (M, K)).astype(np.float16)
+    q = rng.integers(-4, 5, (N, K)).astype(np.int8)
+    s = (2.0 ** rng.integers(-12, -6, N)).astype(np.float16)
+    R = rng.integers(-8, 9, (M, N)).astype(np.float16)
+    out = torch.zeros((M, N + 16), dtype=torch.float16, device=cuda_device)[:, 8:8 + N]
+    nb.matmul(to_dev(A, cuda_device), to_dev(q, cuda_device), to_dev(s, cuda_device), out=out,
+              residual=to_dev(R, cuda_device))
+    exact = ref.w8a16_ref(A, q, s, residual=R)
+    assert np.array_equal(out.cpu().numpy(), exact.astype(np.float16))
 
 
 @pytest.mark.parametrize("M,N,K", [(40, 1000, 4096), (64, 384, 11008), (7, 4096, 128)])
@@ -200,3 +216,36 @@ def test_invalid_shapes_raise(cuda_device):
         nb.matmul(A, q)  # K = 24 is not a multiple of 16
     with pytest.raises(ValueError):
         nb.matmul(A, torch.zeros((8, 16), dtype=torch.int8, device=cuda_device))  # K mismatch
+
+
+_PAIR_TS_CHECK = r"""
+import numpy as np, torch, sys
+sys.path.insert(0, sys.argv[1])
+import npu_comp_b200 as nb
+from npu_comp_b200 import _lib
+from oracle import ref
+dev = torch.device("cuda", 0)
+rng = np.random.default_rng(11)
+for M, N, K in [(500, 600, 384), (385, 257, 1376), (2048, 4096, 4096)]:
+    assert _lib.load().npub_w8a16_kernel_name(M, N, K).decode().startswith("w8a16_pair_ts_kernel")
+    A = rng.integers(-3, 4, (M, K)).astype(np.float16)
+    q = rng.integers(-4, 5, (N, K)).astype(np.int8)
+    s = (2.0 ** rng.integers(-12, -6, N)).astype(np.float16)
+    R = rng.integers(-8, 9, (M, N)).astype(np.float16)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    C = nb.matmul(t(A), t(q), t(s), residual=t(R)).cpu().numpy()
+    assert np.array_equal(C, ref.w8a16_ref(A, q, s, residual=R).astype(np.float16)), (M, N, K)
+print("PAIR_TS_OK")
+"""
+
+
+def test_w8a16_pair_ts_kernel_opt_in(cuda_device):
+    """The tensor-memory pair kernel is opt-in (NPUB_W8A16_KERNEL=pair_ts, read
+    once per process): run it in a child process on exact known answers."""
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, NPUB_W8A16_KERNEL="pair_ts")
+    r = subprocess.run([sys.executable, "-c", _PAIR_TS_CHECK, root], env=env, cwd=root, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0 and "PAIR_TS_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
