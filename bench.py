@@ -498,9 +498,11 @@ def run_stack(args):
     g_flops = sum(f for _, _, f, i8 in gev if i8)
     g_n = sum(1 for *_, i8 in gev if i8)
     achieved = g_flops / (g_ms / 1e3) / 1e12 if g_ms > 0 else None
+    # the prefill GEMMs run back to back for hundreds of ms under the power cap:
+    # the sustained figure is their denominator (burst is for a kernel timed alone)
     roof = {"kernel": "w8a16_pair_kernel (tcgen05 cta_group::2 W8A16)", "bound": "tensor", "achieved": achieved,
-            "peak": tf_burst, "unit": "TFLOP/s", "frac": achieved / tf_burst if achieved else None,
-            "peak_source": f"{peak_src} bf16 dense (burst)", "launches_per_prefill": g_n,
+            "peak": tf_sust, "unit": "TFLOP/s", "frac": achieved / tf_sust if achieved else None,
+            "peak_source": f"{peak_src} bf16 dense (sustained)", "launches_per_prefill": g_n,
             "avg_launch_us": g_ms * 1e3 / g_n if g_n else None, "traffic": _traffic("stack"),
             "share_of_prefill": g_ms / pre_ms if pre_ms else None}
 

@@ -84,6 +84,16 @@ int npub_w8a16_gemm(const void* A, int64_t lda, const int8_t* Wq, int64_t ldw, c
                     int64_t ldc, const void* R, int64_t ldr, int M, int N, int K, float alpha, void* workspace,
                     size_t workspace_bytes, void* stream);
 size_t npub_w8a16_gemm_workspace(int M, int N, int K);
+/* Gate|up projection fused with SwiGLU (llama_layer.py:143-150: silu(x Wg) *
+ * (x Wu), legalize.py:130-149).  Wq [2F, K] int8 holds the gate and up rows
+ * interleaved -- row 2c is gate channel c, row 2c + 1 up channel c, and
+ * scale [2F] likewise -- and C [M, F] (row stride ldc) receives
+ * fp16(silu(g) * u) with g, u the fp16-rounded projections: the bits of
+ * npub_w8a16_gemm into an [M, 2F] buffer followed by npub_swiglu on its even
+ * and odd columns, without the [M, 2F] round trip through memory.  Workspace
+ * as npub_w8a16_gemm for (M, 2F, K). */
+int npub_w8a16_gemm_swiglu(const void* A, int64_t lda, const int8_t* Wq, int64_t ldw, const void* scale, void* C,
+                           int64_t ldc, int M, int F, int K, void* workspace, size_t workspace_bytes, void* stream);
 /* Name of the kernel npub_w8a16_gemm runs for this shape (static storage):
  * the 2-CTA pair kernel, or the stream-K kernel for decode-sized M.  No
  * reference counterpart (diagnostics). */

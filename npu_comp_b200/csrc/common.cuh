@@ -468,4 +468,26 @@ __device__ __forceinline__ void tc_mma_f16_pair_ts(uint32_t d_tmem, uint32_t a_t
         "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+
+// SwiGLU of one fp16-rounded gate / up pair (legalize.py:130-149): the one
+// expression every kernel that forms it uses, so fused and separate paths
+// give the same bits.  CUDA's fast exp and divide intrinsics: in a GEMM
+// epilogue the full-precision forms cost more issue slots than the rest of
+// the epilogue; their error (a few ulp of fp32) is far below the fp16 store.
+// For g below about -88, exp overflows and the quotient is 0, as silu(g) ~ 0.
+__device__ __forceinline__ float swiglu_f(float g, float u) { return __fdividef(g, 1.0f + __expf(-g)) * u; }
+
+// The SwiGLU epilogue of a W8A16 gate|up tile with interleaved rows: lanes
+// 2i and 2i + 1 hold gate and up of one channel for the same 16 tokens
+// (fp16-rounded values).  The even lane forms tokens 0-7, the odd lane
+// tokens 8-15; `out` gets the 8 results and *first the token offset (0 / 8).
+__device__ __forceinline__ void swiglu_pair16(const float (&mine)[16], int lane, float (&out)[8], int* first) {
+    const bool odd = lane & 1;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float other = __shfl_xor_sync(0xffffffffu, odd ? mine[j] : mine[8 + j], 1);
+        out[j] = odd ? swiglu_f(other, mine[8 + j]) : swiglu_f(mine[j], other);
+    }
+    *first = odd ? 8 : 0;
+}
 }  // namespace npub

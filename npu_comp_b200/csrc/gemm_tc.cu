@@ -316,6 +316,31 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
     }
 }
 
+// Split-K reduction of a gate|up projection with interleaved rows (2c gate,
+// 2c + 1 up) fused with SwiGLU: out [M, N/2].  g and u are rounded to fp16
+// exactly as splitk_reduce_kernel would store them.
+__global__ void splitk_reduce_swiglu_kernel(const float* __restrict__ part, int splits, int M, int N,
+                                            const __half* __restrict__ scale, float alpha, __half* __restrict__ out,
+                                            int64_t ldo) {
+    pdl_trigger();
+    pdl_wait();
+    const int F = N / 2;
+    const int64_t total = (int64_t)M * F;
+    const int64_t plane = (int64_t)M * N;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int m = (int)(i / F), c = (int)(i - (int64_t)m * F);
+        const int64_t e = (int64_t)m * N + 2 * c;
+        float ga = 0.0f, ua = 0.0f;
+        for (int s = 0; s < splits; ++s) {
+            ga += part[s * plane + e];
+            ua += part[s * plane + e + 1];
+        }
+        const float g = __half2float(__float2half_rn(ga * alpha * (scale ? __half2float(scale[2 * c]) : 1.0f)));
+        const float u = __half2float(__float2half_rn(ua * alpha * (scale ? __half2float(scale[2 * c + 1]) : 1.0f)));
+        out[(int64_t)m * ldo + c] = __float2half_rn(swiglu_f(g, u));
+    }
+}
+
 // ------------------------------------------------------------------ host side
 
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -438,7 +463,7 @@ static size_t linear_workspace(int M, int N, int K, bool w_int8) {
 // W8A16 on 2-CTA pairs: weights are the 256-row MMA side, tokens the BT side.
 static int linear_w8a16_pair(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C,
                              int64_t ldc, const void* R, int64_t ldr, int M, int N, int K, float alpha, void* ws,
-                             size_t ws_bytes, cudaStream_t st) {
+                             size_t ws_bytes, cudaStream_t st, int swiglu = 0) {
     PairParams p;
     memset(&p, 0, sizeof(p));
     const int bt = pair_bt(M);
@@ -464,13 +489,18 @@ static int linear_w8a16_pair(const void* A, int64_t lda, const void* W, int64_t 
         p.R = reinterpret_cast<const __half*>(R);
         p.ldr = ldr;
         p.scale = reinterpret_cast<const __half*>(scale);
+        p.swiglu = swiglu;
     }
     rc = w8a16_pair_run(p, M, N, K, st);
     if (rc || p.splits == 1) return rc;
-    const int64_t total = (int64_t)M * N;
+    const int64_t total = (int64_t)M * (swiglu ? N / 2 : N);
     int blocks = (int)((total + 255) / 256);
     const int cap = num_sms() * 8;
     if (blocks > cap) blocks = cap;
+    if (swiglu)
+        return launch_pdl(splitk_reduce_swiglu_kernel, dim3(blocks), dim3(256), 0, st,
+                          reinterpret_cast<const float*>(ws), p.splits, M, N, reinterpret_cast<const __half*>(scale),
+                          alpha, reinterpret_cast<__half*>(C), ldc);
     return launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(256), 0, st, reinterpret_cast<const float*>(ws), p.splits, M, N,
                                                  reinterpret_cast<const __half*>(scale), alpha,
                                                  reinterpret_cast<const __half*>(R), ldr, reinterpret_cast<__half*>(C),
@@ -557,6 +587,28 @@ extern "C" int npub_w8a16_gemm(const void* A, int64_t lda, const int8_t* Wq, int
 }
 
 extern "C" size_t npub_w8a16_gemm_workspace(int M, int N, int K) { return npub::linear_workspace(M, N, K, true); }
+
+extern "C" int npub_w8a16_gemm_swiglu(const void* A, int64_t lda, const int8_t* Wq, int64_t ldw, const void* scale,
+                                      void* C, int64_t ldc, int M, int F, int K, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+    NPUB_CHECK_ARG(M >= 0 && F >= 0 && K >= 0);
+    if (M == 0 || F == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(A && Wq && C);
+    NPUB_CHECK_ARG(K % 16 == 0 && K > 0);
+    NPUB_CHECK_ARG(lda >= K && lda % 8 == 0 && npub_aligned(A, 16));
+    NPUB_CHECK_ARG(ldw >= K && ldw % 16 == 0 && npub_aligned(Wq, 16));
+    NPUB_CHECK_ARG(ldc >= F);
+    NPUB_CHECK_ARG(F <= (1 << 29));
+    const int N = 2 * F;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    // the tensor-memory pair kernel has no SwiGLU epilogue: the shared-memory
+    // pair kernel serves every M > 64 here
+    if (npub::w8a16_use_skinny(M, N, K))
+        return npub::w8a16_skinny_run(A, lda, Wq, ldw, scale, C, ldc, nullptr, 0, M, N, K, 1.0f, workspace,
+                                      workspace_bytes, st, nullptr, 1);
+    return npub::linear_w8a16_pair(A, lda, Wq, ldw, scale, C, ldc, nullptr, 0, M, N, K, 1.0f, workspace,
+                                   workspace_bytes, st, 1);
+}
 
 extern "C" const char* npub_w8a16_kernel_name(int M, int N, int K) {
     if (M <= 0 || N <= 0 || K <= 0) return "none";

@@ -299,8 +299,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<G>(), 1)
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] = 0.0f;
                 }
-                if (!arow) continue;
                 const int tb = tc.b0 + c0;
+                if (p.swiglu && !p.out_f32) {
+                    // gate row 2c and up row 2c + 1 sit in adjacent lanes (see
+                    // the stream-K kernel): the even lane stores channel c
+                    float gu[16], o[8];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) gu[j] = __half2float(__float2half_rn(v[j] * sc));
+                    int t0;
+                    swiglu_pair16(gu, lane, o, &t0);
+                    if (arow) {
+                        __half* dst = p.C + a / 2;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            if (tb + t0 + j < p.M) dst[(int64_t)(tb + t0 + j) * p.ldc] = __float2half_rn(o[j]);
+                    }
+                    continue;
+                }
+                if (!arow) continue;
                 if (p.out_f32) {
                     float* o = p.part + obase;
 #pragma unroll

@@ -68,6 +68,7 @@ struct PairParams {
     float alpha;
     float* part;
     int* err;
+    int swiglu;             // 1: rows 2c / 2c+1 are gate / up; C [M, N/2] = fp16(silu(g) * u)
 };
 
 int pair_bt(int M);

@@ -441,6 +441,21 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                 ar_mine = p.ar.stage[p.ar.rank] + ((size_t)(ar_e & 1u) * kArSlots + qs) * kArSlotFloats + lane * 64;
             }
             auto emit = [&](int c0, const float (&v)[16]) {
+                if (p.swiglu) {
+                    // gate row 2c and up row 2c + 1 sit in adjacent lanes: both
+                    // are rounded to fp16 as a separate GEMM would store them,
+                    // and the pair forms fp16(silu(g) * u) for channel c
+                    float gu[16], o[8];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) gu[j] = __half2float(__float2half_rn(v[j] * sc));
+                    int t0;
+                    swiglu_pair16(gu, lane, o, &t0);
+                    if (!nrow) return;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (c0 + t0 + j < M) p.C[(int64_t)(c0 + t0 + j) * p.ldc + n / 2] = __float2half_rn(o[j]);
+                    return;
+                }
                 if (ar) {
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
@@ -644,8 +659,9 @@ size_t w8a16_skinny_workspace(int M, int N, int K) {
 
 int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C, int64_t ldc,
                      const void* R, int64_t ldr, int M, int N, int K, float alpha, void* ws, size_t ws_bytes,
-                     cudaStream_t st, const SkinnyAR* ar) {
+                     cudaStream_t st, const SkinnyAR* ar, int swiglu) {
     if (!w8a16_skinny_fits(M, N)) return NPUB_ERR_INVALID_ARG;
+    if (swiglu && (N % 2 || R || (ar && ar->world > 1))) return NPUB_ERR_INVALID_ARG;
     if (ar && ar->world > 1 && (N + skinny::kRows - 1) / skinny::kRows * 4 > kArSlots) return NPUB_ERR_UNSUPPORTED;
     const size_t need = w8a16_skinny_workspace(M, N, K);
     if (!ws || ws_bytes < need) return NPUB_ERR_WORKSPACE;
@@ -672,6 +688,7 @@ int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, con
     p.cnt = reinterpret_cast<unsigned*>(ws);
     p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kSkinnyCounterBytes);
     p.err = npub_internal_device_error_word();
+    p.swiglu = swiglu ? 1 : 0;
     const int grid = skinny_grid(N, K);
     if (ar && ar->world > 1) {
         p.ar = *ar;

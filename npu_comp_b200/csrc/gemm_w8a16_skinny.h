@@ -38,10 +38,11 @@ struct SkinnyParams {
     int64_t ldr;
     const __half* scale;
     float alpha;
-    float* part;    // [2 x grid][BT][128] fp32 partial tiles
+    float* part;    // [grid][128][BT] fp32 partial tiles
     unsigned* cnt;  // [n_tiles][4] pieces arrived per tile and 32-row quarter (zero between calls)
     int* err;
     SkinnyAR ar;
+    int swiglu;     // 1: rows 2c / 2c+1 are gate / up; C [M, N/2] = fp16(silu(g) * u)
 };
 
 // Tile counters at the start of every workspace of this kernel: a fixed
@@ -54,6 +55,6 @@ bool w8a16_use_skinny(int M, int N, int K);
 size_t w8a16_skinny_workspace(int M, int N, int K);
 int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C, int64_t ldc,
                      const void* R, int64_t ldr, int M, int N, int K, float alpha, void* ws, size_t ws_bytes,
-                     cudaStream_t st, const SkinnyAR* ar = nullptr);
+                     cudaStream_t st, const SkinnyAR* ar = nullptr, int swiglu = 0);
 
 }  // namespace npub

@@ -116,7 +116,7 @@ __global__ void swiglu_vec_kernel(const __half* __restrict__ g, int64_t ldg, con
         unpack8(*reinterpret_cast<const uint4*>(g + (int64_t)rr * ldg + c), gv);
         unpack8(*reinterpret_cast<const uint4*>(u + (int64_t)rr * ldu + c), uv);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) o[k] = gv[k] / (1.0f + expf(-gv[k])) * uv[k];
+        for (int k = 0; k < 8; ++k) o[k] = swiglu_f(gv[k], uv[k]);
         *reinterpret_cast<uint4*>(h + (int64_t)rr * ldh + c) = pack8(o);
     }
 }
@@ -127,7 +127,7 @@ __global__ void swiglu_scalar_kernel(const __half* __restrict__ g, int64_t ldg, 
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int rr = (int)(i / cols), c = (int)(i - (int64_t)rr * cols);
         const float gv = __half2float(g[(int64_t)rr * ldg + c]), uv = __half2float(u[(int64_t)rr * ldu + c]);
-        h[(int64_t)rr * ldh + c] = __float2half_rn(gv / (1.0f + expf(-gv)) * uv);
+        h[(int64_t)rr * ldh + c] = __float2half_rn(swiglu_f(gv, uv));
     }
 }
 

@@ -67,8 +67,8 @@ class LayerWeights:
     sqkv: torch.Tensor       # fp16 [(hq + 2*hkv)*hd]
     wo: torch.Tensor         # int8 [d, hq*hd]   (local K slice)
     so: torch.Tensor         # fp16 [d]
-    wgu: torch.Tensor        # int8 [2*f, d]     rows: gate (local) | up (local)
-    sgu: torch.Tensor        # fp16 [2*f]
+    wgu: torch.Tensor        # int8 [2*f, d]     rows interleaved: 2c gate c, 2c+1 up c (local)
+    sgu: torch.Tensor        # fp16 [2*f]        same order
     wd: torch.Tensor         # int8 [d, f]       (local K slice)
     sd: torch.Tensor         # fp16 [d]
     g1: torch.Tensor         # fp16 [d]
@@ -159,7 +159,7 @@ def make_layer(cfg: LlamaConfig, seed: int, device, tp: TP = TP(), std: float = 
     q, so = quantize_linear(rnd(cfg.q_dim, d))                           # O, row parallel
     wo = q[:, rg["o"][0].start:rg["o"][0].stop].contiguous()
     q, s = quantize_linear(rnd(d, 2 * cfg.ffn))                          # gate | up, column parallel
-    wgu, sgu = _shard_rows(q, s, rg["gu"])
+    wgu, sgu = npu.interleave_gate_up(*_shard_rows(q, s, rg["gu"]))
     q, sd = quantize_linear(rnd(cfg.ffn, d))                             # down, row parallel
     wd = q[:, rg["d"][0].start:rg["d"][0].stop].contiguous()
     del q
@@ -177,7 +177,7 @@ def layer_from_float(cfg: LlamaConfig, W: Dict[str, torch.Tensor], device) -> La
                      + [f32(W[f"Wv{k}"]) for k in range(KV)], dim=1)
     wqkv, sqkv = quantize_linear(Wqkv)
     wo, so = quantize_linear(torch.cat([f32(W[f"Wo{h}"]) for h in range(H)], dim=0))
-    wgu, sgu = quantize_linear(torch.cat([f32(W["Wg"]), f32(W["Wu"])], dim=1))
+    wgu, sgu = npu.interleave_gate_up(*quantize_linear(torch.cat([f32(W["Wg"]), f32(W["Wu"])], dim=1)))
     wd, sd = quantize_linear(f32(W["Wd"]))
     g1 = f32(W["Wn1"]).reshape(-1).half()
     g2 = f32(W["Wn2"]).reshape(-1).half()
@@ -220,11 +220,17 @@ class _Marks:
 def layer_prefill(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, *, batch: int = 1, tp: TP = TP(),
                   positions: Optional[torch.Tensor] = None, kv_out: Optional[tuple] = None,
                   scratch: Optional[Scratch] = None, out: Optional[torch.Tensor] = None,
-                  events: Optional[list] = None) -> torch.Tensor:
+                  events: Optional[list] = None, residual: Optional[torch.Tensor] = None,
+                  defer_residual: bool = False):
     """One decoder layer over `batch` prompts of equal length stacked in x [batch*T, d].
 
     kv_out: optional (k_cache, v_cache) [batch, kv_heads_local, cap, hd] that
     receive the prompt's (RoPE'd) K and V for later decode steps.
+    residual / defer_residual: a stack of layers passes the previous layer's
+    (ffn, h) pair unsummed -- the layer input is then fp16(x + residual), formed
+    inside the first RMSNorm -- and defer_residual=True returns this layer's
+    (ffn, h) instead of fp16(ffn + h); the same bits, one launch and one pass
+    over the activations fewer per layer.
     """
     sc = scratch or Scratch()
     dev = x.device
@@ -238,7 +244,11 @@ def layer_prefill(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, *, batch: 
     mk = _Marks(events)
     # attention block
     mk("rmsnorm")
-    xn = npu.rmsnorm(x, w.g1, cfg.eps, out=sc.get("xn", (BT, d), device=dev))
+    if residual is None:
+        xn = npu.rmsnorm(x, w.g1, cfg.eps, out=sc.get("xn", (BT, d), device=dev))
+    else:
+        xn, x = npu.rmsnorm(x, w.g1, cfg.eps, residual=residual, residual_out=sc.get("xres", (BT, d), device=dev),
+                            out=sc.get("xn", (BT, d), device=dev))
     mk("qkv_gemm")
     qkv = npu.matmul(xn, w.wqkv, w.sqkv, out=sc.get("qkv", (BT, qkv_n), device=dev))
     q = qkv[:, : hq * hd]
@@ -261,14 +271,15 @@ def layer_prefill(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, *, batch: 
     mk("rmsnorm")
     h = sc.get("h", (BT, d), device=dev)
     hn, _ = npu.rmsnorm(attn, w.g2, cfg.eps, residual=x, residual_out=h, out=sc.get("hn", (BT, d), device=dev))
-    mk("gate_up_gemm")
-    gu = npu.matmul(hn, w.wgu, w.sgu, out=sc.get("gu", (BT, 2 * w.ffn), device=dev))
-    mk("swiglu")
-    a = npu.swiglu(gu, out=sc.get("act", (BT, w.ffn), device=dev))
+    mk("gate_up_gemm")  # SwiGLU in the GEMM epilogue (interleaved gate/up rows)
+    a = npu.matmul_swiglu(hn, w.wgu, w.sgu, out=sc.get("act", (BT, w.ffn), device=dev))
     mk("down_gemm")
     ffn = npu.matmul(a, w.wd, w.sd, out=sc.get("ffn", (BT, d), device=dev))
     mk("all_reduce")
     tp.all_reduce(ffn)
+    if defer_residual:
+        mk.end()
+        return ffn, h
     mk("residual")
     y = out if out is not None else torch.empty((BT, d), dtype=torch.float16, device=dev)
     npu.add(ffn, h, out=y)
@@ -278,10 +289,11 @@ def layer_prefill(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, *, batch: 
 
 def layer_decode(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, k_cache: torch.Tensor, v_cache: torch.Tensor,
                  pos: torch.Tensor, *, ctx_max: int, tp: TP = TP(), scratch: Optional[Scratch] = None,
-                 out: Optional[torch.Tensor] = None, events: Optional[list] = None) -> torch.Tensor:
+                 out: Optional[torch.Tensor] = None, events: Optional[list] = None,
+                 residual: Optional[torch.Tensor] = None, defer_residual: bool = False):
     """One decode step: x [B, d] holds one new token per sequence at positions
     pos [B] (int32); its K/V are appended to the caches, attention covers
-    positions 0..pos[b]."""
+    positions 0..pos[b].  residual / defer_residual as in layer_prefill."""
     sc = scratch or Scratch()
     dev = x.device
     B, d = x.shape
@@ -289,7 +301,11 @@ def layer_decode(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, k_cache: to
     hq, hk = w.heads, w.kv_heads
     mk = _Marks(events)
     mk("rmsnorm")
-    xn = npu.rmsnorm(x, w.g1, cfg.eps, out=sc.get("dxn", (B, d), device=dev))
+    if residual is None:
+        xn = npu.rmsnorm(x, w.g1, cfg.eps, out=sc.get("dxn", (B, d), device=dev))
+    else:
+        xn, x = npu.rmsnorm(x, w.g1, cfg.eps, residual=residual, residual_out=sc.get("dxres", (B, d), device=dev),
+                            out=sc.get("dxn", (B, d), device=dev))
     mk("qkv_gemm")
     qkv = npu.matmul(xn, w.wqkv, w.sqkv, out=sc.get("dqkv", (B, (hq + 2 * hk) * hd), device=dev))
     q = qkv[:, : hq * hd]
@@ -304,12 +320,13 @@ def layer_decode(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, k_cache: to
     mk("rmsnorm")
     h = sc.get("dh", (B, d), device=dev)
     hn, _ = npu.rmsnorm(attn, w.g2, cfg.eps, residual=x, residual_out=h, out=sc.get("dhn", (B, d), device=dev))
-    mk("gate_up_gemm")
-    gu = npu.matmul(hn, w.wgu, w.sgu, out=sc.get("dgu", (B, 2 * w.ffn), device=dev))
-    mk("swiglu")
-    a = npu.swiglu(gu, out=sc.get("dact", (B, w.ffn), device=dev))
+    mk("gate_up_gemm")  # SwiGLU in the GEMM epilogue (interleaved gate/up rows)
+    a = npu.matmul_swiglu(hn, w.wgu, w.sgu, out=sc.get("dact", (B, w.ffn), device=dev))
     mk("down_gemm")
     ffn = _row_parallel(a, w.wd, w.sd, tp, sc.get("dffn", (B, d), device=dev), mk)
+    if defer_residual:
+        mk.end()
+        return ffn, h
     mk("residual")
     y = out if out is not None else torch.empty((B, d), dtype=torch.float16, device=dev)
     npu.add(ffn, h, out=y)
@@ -417,10 +434,15 @@ class LlamaStack:
                 tp.peer = comm.PeerAllReduce(tp.group, device)
 
     # -- greedy selection over the (possibly vocab-sharded) lm_head
-    def _next_ids(self, xl: torch.Tensor) -> None:
+    def _next_ids(self, xl: torch.Tensor, residual: Optional[torch.Tensor] = None) -> None:
         cfg, w, tp, sc = self.cfg, self.w, self.tp, self.sc
         B = xl.shape[0]
-        hn = npu.rmsnorm(xl, w.norm, cfg.eps, out=sc.get("fn", (B, cfg.d), device=self.dev))
+        if residual is None:
+            hn = npu.rmsnorm(xl, w.norm, cfg.eps, out=sc.get("fn", (B, cfg.d), device=self.dev))
+        else:  # the last layer's residual add, inside the final RMSNorm
+            hn, _ = npu.rmsnorm(xl, w.norm, cfg.eps, residual=residual,
+                                residual_out=sc.get("fres", (B, cfg.d), device=self.dev),
+                                out=sc.get("fn", (B, cfg.d), device=self.dev))
         logits = npu.matmul(hn, w.lm_head, out=sc.get("logits", (B, w.lm_head.shape[0]), device=self.dev))
         idx, val = npu.argmax(logits, idx=sc.get("amax_i", (B,), torch.int32, self.dev),
                               val=sc.get("amax_v", (B,), torch.float32, self.dev))
@@ -441,14 +463,15 @@ class LlamaStack:
     def prefill(self, prompts: torch.Tensor) -> torch.Tensor:
         cfg, B, T = self.cfg, self.B, self.T
         x = npu.embed(prompts.reshape(-1), self.w.embed, out=self.sc.get("px0", (B * T, cfg.d), device=self.dev))
-        bufs = (x, self.sc.get("px1", (B * T, cfg.d), device=self.dev))
+        res = None
         for i, lw in enumerate(self.w.layers):
-            y = bufs[(i + 1) % 2]
-            layer_prefill(bufs[i % 2], lw, cfg, batch=B, tp=self.tp, positions=self.positions,
-                          kv_out=(self.kc[i], self.vc[i]), scratch=self.sc, out=y)
-        last = bufs[len(self.w.layers) % 2].view(B, T, cfg.d)[:, T - 1]
+            # each layer's residual add is folded into the next layer's first RMSNorm
+            x, res = layer_prefill(x, lw, cfg, batch=B, tp=self.tp, positions=self.positions,
+                                   kv_out=(self.kc[i], self.vc[i]), scratch=self.sc, residual=res,
+                                   defer_residual=True)
+        # the last layer's residual add, for the last prompt rows only
         xl = self.sc.get("xlast", (B, cfg.d), device=self.dev)
-        xl.copy_(last)
+        npu.add(x.view(B, T, cfg.d)[:, T - 1], res.view(B, T, cfg.d)[:, T - 1], out=xl)
         self._next_ids(xl)
         self.pos.fill_(T)
         self.tokens = [self.ids.clone()]
@@ -457,11 +480,11 @@ class LlamaStack:
     def _decode_step(self) -> None:
         cfg, B = self.cfg, self.B
         x = npu.embed(self.ids, self.w.embed, out=self.sc.get("dx0", (B, cfg.d), device=self.dev))
-        bufs = (x, self.sc.get("dx1", (B, cfg.d), device=self.dev))
+        res = None
         for i, lw in enumerate(self.w.layers):
-            layer_decode(bufs[i % 2], lw, cfg, self.kc[i], self.vc[i], self.pos, ctx_max=self.cap, tp=self.tp,
-                         scratch=self.sc, out=bufs[(i + 1) % 2])
-        self._next_ids(bufs[len(self.w.layers) % 2])
+            x, res = layer_decode(x, lw, cfg, self.kc[i], self.vc[i], self.pos, ctx_max=self.cap, tp=self.tp,
+                                  scratch=self.sc, residual=res, defer_residual=True)
+        self._next_ids(x, res)
         self.pos.add_(1)
 
     def _capture(self) -> None:

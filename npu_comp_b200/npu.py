@@ -25,7 +25,7 @@ from ._lib import NpubError  # noqa: F401  (re-exported)
 
 __all__ = [
     "fp16", "quantize_w8", "matmul", "rmsnorm", "add", "swiglu", "softmax", "rope", "attention",
-    "attention_decode", "kv_append", "rope_kv_append", "rope_kv_store", "embed", "argmax", "isa_vector", "f32_to_f16_bits", "f16_bits_to_f32", "NpubError",
+    "attention_decode", "kv_append", "rope_kv_append", "rope_kv_store", "matmul_swiglu", "interleave_gate_up", "embed", "argmax", "isa_vector", "f32_to_f16_bits", "f16_bits_to_f32", "NpubError",
 ]
 
 
@@ -154,6 +154,47 @@ def matmul(A: torch.Tensor, W: torch.Tensor, scale: Optional[torch.Tensor] = Non
     if ev is not None:
         e1.record()
         ev.append((e0, e1, 2.0 * M * N * K, int8))
+    return out
+
+
+def interleave_gate_up(wq: torch.Tensor, scale: torch.Tensor):
+    """[gate rows (F) | up rows (F)] -> rows 2c = gate c, 2c + 1 = up c, the
+    layout matmul_swiglu takes (int8 [2F, K] and fp16 [2F])."""
+    F2, K = wq.shape
+    _need(F2 % 2 == 0 and scale.numel() == F2, "gate|up weights need an even row count and one scale per row")
+    F = F2 // 2
+    w = wq.view(2, F, K).transpose(0, 1).reshape(F2, K).contiguous()
+    s = scale.view(2, F).t().reshape(F2).contiguous()
+    return w, s
+
+
+def matmul_swiglu(A: torch.Tensor, Wgu: torch.Tensor, scale: torch.Tensor, *,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[M, F] = fp16(silu(g) * u) with g, u the fp16 W8A16 projections of A
+    on the gate and up rows of Wgu (int8 [2F, K], interleaved by
+    interleave_gate_up; scale fp16 [2F]): matmul() then swiglu(), fused."""
+    lda = _mat(A, "A", torch.float16)
+    ldw = _mat(Wgu, "Wgu", torch.int8)
+    M, K = A.shape
+    F2, K2 = Wgu.shape
+    _need(K == K2 and F2 % 2 == 0, f"shape mismatch: A {tuple(A.shape)} vs Wgu {tuple(Wgu.shape)}")
+    _need(scale.is_cuda and scale.dtype == torch.float16 and scale.numel() == F2 and scale.is_contiguous(),
+          "scale must be a contiguous fp16 CUDA tensor of 2F elements")
+    F = F2 // 2
+    if out is None:
+        out = torch.empty((M, F), dtype=torch.float16, device=A.device)
+    ldo = _mat(out, "out", torch.float16)
+    _need(tuple(out.shape) == (M, F), "out must be [M, F]")
+    ws, wsb = _zeroed_workspace(_lib.query("npub_w8a16_gemm_workspace", M, F2, K), A.device)
+    ev = gemm_events
+    if ev is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+    _lib.call("npub_w8a16_gemm_swiglu", A.data_ptr(), lda, Wgu.data_ptr(), ldw, scale.data_ptr(), out.data_ptr(),
+              ldo, M, F, K, _ptr(ws), wsb, _stream())
+    if ev is not None:
+        e1.record()
+        ev.append((e0, e1, 2.0 * M * F2 * K, True))
     return out
 
 

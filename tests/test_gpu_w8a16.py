@@ -249,3 +249,41 @@ def test_w8a16_pair_ts_kernel_opt_in(cuda_device):
     r = subprocess.run([sys.executable, "-c", _PAIR_TS_CHECK, root], env=env, cwd=root, capture_output=True,
                        text=True, timeout=600)
     assert r.returncode == 0 and "PAIR_TS_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+@pytest.mark.parametrize("M,F,K", [(32, 11008, 4096), (64, 2752, 4096), (32, 1376, 4096), (2048, 1376, 4096),
+                                   (300, 500, 272), (5, 64, 64), (17, 4100, 1024)])
+def test_matmul_swiglu_equals_matmul_then_swiglu(cuda_device, M, F, K):
+    """The fused gate|up + SwiGLU gives the bits of the two separate ops on the
+    same interleaved weights (matmul, then swiglu on its even / odd columns):
+    stream-K (M <= 64, 2F >= 8192), the pair kernel with and without split-K,
+    ragged shapes.  (Against the [gate | up] layout the stream-K kernel cuts a
+    row's K range at other places, so only the pair kernel matches bit for bit
+    there; the oracle test below bounds both.)"""
+    g = torch.Generator(device=cuda_device).manual_seed(M + F + K)
+    W = torch.randn((K, 2 * F), generator=g, device=cuda_device) * 0.02
+    q, s = nb.quantize_w8(W)
+    del W
+    A = torch.randn((M, K), generator=g, device=cuda_device).half()
+    qi, si = nb.interleave_gate_up(q, s)
+    gu = nb.matmul(A, qi, si)
+    ref_out = nb.swiglu(gu[:, 0::2].contiguous(), gu[:, 1::2].contiguous())
+    if M > 64:  # pair kernel: per-row sums independent of the row order
+        assert torch.equal(ref_out, nb.swiglu(nb.matmul(A, q, s)))
+    out = torch.full((M, F + 8), 7.0, dtype=torch.float16, device=cuda_device)
+    nb.matmul_swiglu(A, qi, si, out=out[:, :F])
+    assert torch.equal(out[:, :F], ref_out)
+    assert bool((out[:, F:] == 7.0).all())  # nothing written past the F columns
+
+
+def test_matmul_swiglu_against_oracle(cuda_device, rng):
+    """Against the float64 oracle of the FFN's first half (llama_layer.py:143-150)."""
+    M, F, K = 40, 300, 512
+    A = rng.standard_normal((M, K)).astype(np.float16)
+    W = (rng.standard_normal((K, 2 * F)) * 0.05).astype(np.float32)
+    q, s = ref.quantize_w8(W)
+    gu = ref.w8a16_ref(A, q, s).astype(np.float16).astype(np.float64)
+    want = ref.silu_mul_ref(gu[:, :F], gu[:, F:])
+    qi, si = nb.interleave_gate_up(to_dev(q, cuda_device), to_dev(s, cuda_device))
+    got = nb.matmul_swiglu(to_dev(A, cuda_device), qi, si).float().cpu().numpy()
+    assert ref.rel_err(got, want) <= TOL
