@@ -449,6 +449,20 @@ def run_stack(args):
         if world > 1:
             dist.barrier()
 
+    if args.ncu_region:
+        st.prefill(prompts)
+        st.decode(64)  # graph captured; KV length ~T + 64
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        if args.ncu_region == "prefill":
+            st.prefill(prompts)
+        else:
+            st.decode(1)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"ncu_region": args.ncu_region, "workload": "llama7b_stack_w8a16"}))
+        st.release()
+        return
     for _ in range(args.warmup):
         st.prefill(prompts)
         st.decode(S)
@@ -588,6 +602,10 @@ def main():
     ap.add_argument("--shape", default=None, help="gemm workload: M,N,K instead of the gate|up projection")
     ap.add_argument("--batch", type=int, default=None, help="decode workload: sequences (default 64)")
     ap.add_argument("--ctx", type=int, default=None, help="decode workload: KV length (default 4096)")
+    ap.add_argument("--ncu-region", choices=["prefill", "decode"], default=None,
+                    help="stack workload, 1 GPU: after warm-up, bracket one prefill or one graph-replayed decode "
+                         "step (64 steps in) with cudaProfilerStart/Stop for ncu --profile-from-start off, "
+                         "then exit without a bench line")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.steps is None:
