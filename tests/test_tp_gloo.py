@@ -126,3 +126,25 @@ def test_flop_and_byte_counts():
     assert c.linear_flops_per_token() == 2 * 4096 * (12288 + 4096 + 22016 + 11008)
     assert abs(llama.layer_flops(c, 2048, 2048) - 863.3e9) / 863.3e9 < 1e-3
     assert abs(llama.decode_bytes(c, 64, 4096) - 4.5e9) / 4.5e9 < 0.01
+
+
+@pytest.mark.parametrize("size", [1, 2])
+def test_gate_up_interleave_after_sharding(size):
+    """The layer's gate|up weights: each rank slices its F/TP gate and up rows
+    (tp_ranges) and interleaves them, row 2c = gate channel c, 2c + 1 = up
+    channel c of that rank, scales alike (the layout the SwiGLU epilogue reads
+    from adjacent lanes)."""
+    from npu_comp_b200 import npu
+    F = CFG.ffn
+    rows = torch.arange(2 * F, dtype=torch.int32)  # row r of the full [gate | up] matrix
+    q = rows[:, None].repeat(1, 16).to(torch.int8 if 2 * F < 128 else torch.int32)
+    s = rows.to(torch.float16)
+    for rank in range(size):
+        rg = llama.tp_ranges(CFG, rank, size)["gu"]
+        idx = torch.cat([torch.arange(r.start, r.stop) for r in rg])
+        qi, si = npu.interleave_gate_up(q.index_select(0, idx).contiguous(), s.index_select(0, idx).contiguous())
+        f = F // size
+        for c in range(f):
+            assert int(qi[2 * c, 0]) == rank * f + c and int(qi[2 * c + 1, 0]) == F + rank * f + c
+            assert float(si[2 * c]) == rank * f + c and float(si[2 * c + 1]) == F + rank * f + c
+        assert bool((qi == qi[:, :1]).all())  # whole rows moved
