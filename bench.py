@@ -590,6 +590,13 @@ def _scale_rate(flop_rate, workload):
     return flop_rate / per_tok, "tokens/s"
 
 
+def _scale_note(workload):
+    return {"gemm": "GEMM FLOP rate reported as TFLOP/s",
+            "stack": "GEMM FLOP rate divided by the stack's FLOPs per token (32 layers + lm_head, prefill and decode)",
+            "decode": "GEMM FLOP rate divided by one decode layer's FLOPs per token (KV 4097)",
+            "layer": "GEMM FLOP rate divided by the prefill layer's FLOPs per token (T 2048)"}[workload]
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -634,7 +641,7 @@ def main():
         line = {"impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": world,
                 "steps": len(rates), "warmup": warm, "higher_is_better": True, "vs_baseline": None,
                 "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": kind,
-                                 "sample": sample + " ; GEMM FLOP rate scaled by the layer's FLOPs per token"},
+                                 "sample": sample + " ; " + _scale_note(args.workload)},
                 "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
                 "config": {"workload": {"layer": "llama7b_layer_prefill_w8a16", "decode": "llama7b_layer_decode_w8a16",
                                         "gemm": "w8a16_gemm", "stack": "llama7b_stack_w8a16"}[args.workload]}}
@@ -647,7 +654,7 @@ def main():
             rate, cores, kind, sample = cpu_reference_rate(all_cores=False)
             v, u = _scale_rate(rate, args.workload)
             out["cpu_baseline"] = {"value": v, "unit": u, "cores": cores, "kind": kind,
-                                   "sample": sample + " ; GEMM FLOP rate scaled by the layer's FLOPs per token"}
+                                   "sample": sample + " ; " + _scale_note(args.workload)}
         print(json.dumps(out), flush=True)
     return 0
 
