@@ -70,12 +70,30 @@ struct TileCoord {
     int a0, b0, split, kt0, nk;
 };
 
+// Without split-K the tiles go in bands of up to kBand token tiles: within a
+// band the weight pairs in turn, each against every token tile of the band.
+// The ~74 tiles in flight then share a few weight pairs and one band of
+// tokens (16 MB at K = 4096), so at 32768 tokens the weights come from HBM
+// once per band instead of once per token tile.
+constexpr int kBand = 8;
+
 __device__ __forceinline__ TileCoord tile_coord(const PairParams& p, int tile, int BT) {
     TileCoord c;
-    const int ap = tile % p.n_apairs;
-    const int rest = tile / p.n_apairs;
-    const int bi = rest % p.n_btiles;
-    c.split = rest / p.n_btiles;
+    int ap, bi;
+    if (p.splits == 1) {
+        const int per_band = kBand * p.n_apairs;
+        const int band = tile / per_band;
+        const int r = tile - band * per_band;
+        const int nb = min(kBand, p.n_btiles - band * kBand);  // token tiles in this band
+        ap = r / nb;
+        bi = band * kBand + r % nb;
+        c.split = 0;
+    } else {
+        ap = tile % p.n_apairs;
+        const int rest = tile / p.n_apairs;
+        bi = rest % p.n_btiles;
+        c.split = rest / p.n_btiles;
+    }
     c.a0 = ap * 2 * kRowsPerCta;
     c.b0 = bi * BT;
     c.kt0 = c.split * p.k_tiles_per_split;
