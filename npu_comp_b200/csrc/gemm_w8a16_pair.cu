@@ -70,23 +70,21 @@ struct TileCoord {
     int a0, b0, split, kt0, nk;
 };
 
-// Without split-K the tiles go in bands of up to kBand token tiles: within a
-// band the weight pairs in turn, each against every token tile of the band.
-// The ~74 tiles in flight then share a few weight pairs and one band of
-// tokens (16 MB at K = 4096), so at 32768 tokens the weights come from HBM
-// once per band instead of once per token tile.
-constexpr int kBand = 8;
-
+// Without split-K the tiles go in bands of p.band token tiles: within a band
+// the weight pairs in turn, each against every token tile of the band.  The
+// ~74 tiles in flight then share a few weight pairs and one band of tokens
+// (at most ~24 MB, sized on the host from K), so at 32768 tokens the weights
+// come from HBM once per band instead of once per token tile.
 __device__ __forceinline__ TileCoord tile_coord(const PairParams& p, int tile, int BT) {
     TileCoord c;
     int ap, bi;
     if (p.splits == 1) {
-        const int per_band = kBand * p.n_apairs;
+        const int per_band = p.band * p.n_apairs;
         const int band = tile / per_band;
         const int r = tile - band * per_band;
-        const int nb = min(kBand, p.n_btiles - band * kBand);  // token tiles in this band
+        const int nb = min(p.band, p.n_btiles - band * p.band);  // token tiles in this band
         ap = r / nb;
-        bi = band * kBand + r % nb;
+        bi = band * p.band + r % nb;
         c.split = 0;
     } else {
         ap = tile % p.n_apairs;
@@ -474,6 +472,10 @@ int w8a16_pair_run(PairParams& p, int M, int N, int K, cudaStream_t st) {
     p.k_tiles_per_split = (p.k_tiles + splits - 1) / splits;
     p.splits = (p.k_tiles + p.k_tiles_per_split - 1) / p.k_tiles_per_split;
     p.n_tiles = p.n_apairs * p.n_btiles * p.splits;
+    // token tiles per band: ~24 MB of tokens (8 tiles of 256 at K = 4096, 4 at K = 11008)
+    const int64_t tile_bytes = (int64_t)bt * K * 2;
+    const int64_t band = (int64_t)(24 << 20) / (tile_bytes > 0 ? tile_bytes : 1);
+    p.band = (int)(band < 1 ? 1 : (band > 8 ? 8 : band));
     p.err = npub_internal_device_error_word();
     switch (bt) {
         case 64: return pair::launch<64, kPairStages64, kPairCStages64, kPairGroups64>(p, clusters, st);

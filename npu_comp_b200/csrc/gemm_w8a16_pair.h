@@ -69,6 +69,7 @@ struct PairParams {
     float* part;
     int* err;
     int swiglu;             // 1: rows 2c / 2c+1 are gate / up; C [M, N/2] = fp16(silu(g) * u)
+    int band;               // token tiles per band of the tile order (set by w8a16_pair_run)
 };
 
 int pair_bt(int M);
