@@ -65,3 +65,21 @@ def test_python_wrappers_fail_loudly_without_the_library(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "_lib", None)
     with pytest.raises(ImportError):
         _lib.load(str(tmp_path / "missing.so"))
+
+
+def test_fused_entry_points_validate_before_any_device_work(libnpub_path):
+    """The gate|up + SwiGLU GEMM and the prompt RoPE + KV-store reject bad
+    shapes with NPUB_ERR_INVALID_ARG and treat empty work as a no-op."""
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    # npub_w8a16_gemm_swiglu(A, lda, Wq, ldw, scale, C, ldc, M, F, K, ws, ws_bytes, stream)
+    assert lib.npub_w8a16_gemm_swiglu(p, 24, p, 32, None, p, 8, 4, 8, 24, None, 0, None) == -1  # K % 16
+    assert lib.npub_w8a16_gemm_swiglu(p, 16, p, 16, None, p, 4, 4, 8, 16, None, 0, None) == -1  # ldc < F
+    assert lib.npub_w8a16_gemm_swiglu(p, 16, ctypes.c_void_p(24), 16, None, p, 8, 4, 8, 16, None, 0,
+                                      None) == -1  # misaligned weights
+    assert lib.npub_w8a16_gemm_swiglu(None, 0, None, 0, None, None, 0, 0, 8, 16, None, 0, None) == 0  # M == 0
+    # npub_rope_kv_store(qkv, ldx, tokens, tokens_per_seq, hq, hk, hd, positions, theta, kc, vc, cap, stream)
+    assert lib.npub_rope_kv_store(p, 512, 10, 3, 2, 1, 128, p, 1e4, p, p, 16, None) == -1  # ragged sequences
+    assert lib.npub_rope_kv_store(p, 512, 8, 4, 2, 1, 120, p, 1e4, p, p, 16, None) == -1  # head_dim % 16
+    assert lib.npub_rope_kv_store(p, 256, 8, 4, 2, 1, 128, p, 1e4, p, p, 16, None) == -1  # ldx too small
+    assert lib.npub_rope_kv_store(None, 0, 0, 1, 2, 1, 128, None, 1e4, None, None, 0, None) == 0  # no rows
