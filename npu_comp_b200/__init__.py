@@ -8,4 +8,6 @@ from .npu import (  # noqa: F401
     quantize_w8, rmsnorm, rope, rope_kv_append, rope_kv_store, softmax, swiglu, matmul_swiglu, interleave_gate_up,
 )
 
+from .llama import llama_layer  # noqa: F401,E402
+
 __version__ = "1.0.0"

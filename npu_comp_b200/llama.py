@@ -287,6 +287,24 @@ def layer_prefill(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, *, batch: 
     return y
 
 
+def llama_layer(x: torch.Tensor, weights, cfg: LlamaConfig, *, batch: int = 1, tp: TP = TP(),
+                positions: Optional[torch.Tensor] = None, kv_out: Optional[tuple] = None,
+                scratch: Optional[Scratch] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The Llama decoder layer under the reference's name (llama_layer.py:114-152:
+    h = x + Attn(RMSNorm(x)); y = h + FFN(RMSNorm(h))) over `batch` prompts
+    stacked in x [batch*T, d] fp16.
+
+    weights: LayerWeights (make_layer / layer_from_float), or the reference's
+    float weight dict (Wq{h}, Wk{k}, Wv{k}, Wo{h}, Wg, Wu, Wd, Wn1, Wn2 in the
+    layout of llama_layer.py:24-31), which is quantised per output channel
+    here (one rank).  Same computation and bits as layer_prefill.
+    """
+    if not isinstance(weights, LayerWeights):
+        weights = layer_from_float(cfg, weights, x.device)
+    return layer_prefill(x, weights, cfg, batch=batch, tp=tp, positions=positions, kv_out=kv_out, scratch=scratch,
+                         out=out)
+
+
 def layer_decode(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, k_cache: torch.Tensor, v_cache: torch.Tensor,
                  pos: torch.Tensor, *, ctx_max: int, tp: TP = TP(), scratch: Optional[Scratch] = None,
                  out: Optional[torch.Tensor] = None, events: Optional[list] = None,

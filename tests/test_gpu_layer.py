@@ -4,6 +4,7 @@ import numpy as np
 import pytest
 import torch
 
+import npu_comp_b200 as nb
 from npu_comp_b200 import llama
 from oracle import ref
 
@@ -39,6 +40,20 @@ def test_reference_llama_layer(cuda_device, examples):
     cos, sin = ref.rope_tables(SEQ, HD)
     yq = ref.ref_layer(ref.quantized_weights(W, H, KV), examples["layer_X"], H, KV, HD, 0.0, cos, sin)
     assert ref.rel_err(y, yq) <= 5e-3                                # same weights the GPU applies
+
+
+def test_llama_layer_entry_point(cuda_device, examples):
+    """npu_comp_b200.llama_layer, the reference's name for the layer, takes the
+    reference's float weight dict directly and gives layer_prefill's bits."""
+    W, (SEQ, D, H, KV, HD, F) = layer_weights_from_fixture(examples)
+    cfg = llama.LlamaConfig(d=D, heads=H, kv_heads=KV, head_dim=HD, ffn=F, eps=0.0, theta=10000.0, vocab=64,
+                            layers=1)
+    x = torch.from_numpy(examples["layer_X"]).half().to(cuda_device)
+    y = nb.llama_layer(x, W, cfg)
+    w = llama.layer_from_float(cfg, W, cuda_device)
+    assert torch.equal(y, llama.layer_prefill(x, w, cfg))
+    assert torch.equal(y, nb.llama_layer(x, w, cfg))
+    assert ref.rel_err(y.float().cpu().numpy(), examples["layer_ref"]) <= TOL
 
 
 def random_float_layer(cfg, rng, std=0.02):
