@@ -145,7 +145,9 @@ int npub_add(const void* a, int64_t lda, const void* b, int64_t ldb, void* out, 
              void* stream);
 
 /* SwiGLU, legalize.py:130-149, llama_layer.py:143-151:
- *   h = fp16( g / (1 + exp(-g)) * u )   (fp32 math), g, u, h fp16 [rows, cols]. */
+ *   h = fp16( g / (1 + exp(-g)) * u )   (fp32 math with CUDA's fast exp and
+ *   divide, a few fp32 ulps; the same expression as the SwiGLU epilogue of
+ *   npub_w8a16_gemm_swiglu), g, u, h fp16 [rows, cols]. */
 int npub_swiglu(const void* g, int64_t ldg, const void* u, int64_t ldu, void* h, int64_t ldh, int rows, int cols,
                 void* stream);
 
