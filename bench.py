@@ -119,7 +119,21 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-# ---------------------------------------------------------------- CPU baseline
+# ---------------------------------------------------------------- CPU baselines
+#
+# Two CPU paths are timed on this host, as the reference's own numbers would be:
+#  * mysim, the reference's cmodel (built from its _poc/mysim.cpp into
+#    oracle/_ref/mysim; the C restatement of it when absent), driven like the
+#    reference's run() (npu.py:62-71) on the programs the reference emits for
+#    each op: the 64-tiled W8A16 matmul (codegen.py:59-108) and the RMSNorm,
+#    SwiGLU, masked-softmax and RoPE recipes (test_rmsnorm.py, test_swiglu.py,
+#    test_attention.py, llama_layer.py:96-104).  Each program is run on a
+#    bounded sample; the workload's time is projected from the measured rate
+#    of each op kind (FLOPs or elements per second) times the workload's
+#    count of that kind.  mysim is single-threaded: `cores` processes run
+#    concurrently for the multi-core figure.
+#  * PyTorch on the CPU: fp32 compute on the same fp16 / int8 synthetic
+#    tensors (weights dequantised to fp32 once), all host threads.
 
 def _cpu_cores():
     try:
@@ -128,56 +142,260 @@ def _cpu_cores():
         return os.cpu_count() or 1
 
 
-def cpu_reference_rate(seconds_target: float = 12.0, all_cores: bool = False):
-    """FLOP/s of the reference's CPU path on the W8A16 GEMM: the 64-tiled
-    program (d_compiler/npu_compiler/codegen.py:59-108) over dequantised
-    weights, executed by mysim (or the C restatement when mysim is absent).
-    Sample: 64 tokens x 512 output channels x K 4096 of the layer's QKV
-    projection.  With all_cores, one process per core runs concurrently."""
+def _mysim_program(kind):
+    """(words, G-buffer image, gn, work units of one run, unit) for one op kind."""
     import numpy as np
     sys.path.insert(0, HERE)
-    from oracle import cmodel, emit
-    M, N, K = 64, 512, 4096
+    from oracle import emit, ref
     rng = np.random.default_rng(0)
-    A = rng.standard_normal((M, K)).astype(np.float16)
-    W = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
-    s = (np.abs(W).max(axis=0) / np.float32(127)).astype(np.float16)
-    q = np.clip(np.rint(W / s.astype(np.float32)), -127, 127)
-    Wd = (q * s.astype(np.float32)).astype(np.float16)
-    words, gimg, c_addr, gn = emit.w8a16_program(A, Wd)
-    flops = 2.0 * M * N * K
+    if kind == "gemm":  # 64 tokens x 512 output channels x K 4096 of the QKV projection
+        M, N, K = 64, 512, 4096
+        A = rng.standard_normal((M, K)).astype(np.float16)
+        q, s = ref.quantize_w8((rng.standard_normal((K, N)) * 0.02).astype(np.float32))
+        words, g, _, gn = emit.w8a16_program(A, ref.dequant_f16(q, s))
+        return words, g, gn, 2.0 * M * N * K, "FLOP"
+    if kind == "rmsnorm":
+        X = rng.standard_normal((512, 248)).astype(np.float16)
+        words, g, _, gn = emit.rmsnorm_program(X, np.ones(248))
+        return words, g, gn, float(X.size), "elements"
+    if kind == "swiglu":
+        n = 1 << 18
+        words, g, _, gn = emit.swiglu_program(rng.standard_normal(n).astype(np.float16),
+                                              rng.standard_normal(n).astype(np.float16))
+        return words, g, gn, float(n), "elements"
+    if kind == "softmax":
+        S = rng.standard_normal((255, 255)).astype(np.float16)
+        words, g, _, gn = emit.softmax_program(S)
+        return words, g, gn, float(S.size), "elements"
+    if kind == "rope":
+        Q = rng.standard_normal((256, 128)).astype(np.float16)
+        c, s_ = ref.rope_tables(256, 128)
+        words, g, _, gn = emit.rope_program(Q, ref.f16(c), ref.f16(s_))
+        return words, g, gn, float(Q.size), "elements"
+    raise ValueError(kind)
+
+
+MYSIM_KINDS = ("gemm", "rmsnorm", "swiglu", "softmax", "rope")
+
+
+def mysim_rates(kinds=MYSIM_KINDS, all_cores=False, reps=None):
+    """Measured mysim rate of each op kind (units per second over all processes
+    that ran at once).  Returns (rates, processes, kind, per-kind sample text)."""
+    import tempfile
+    import numpy as np
+    sys.path.insert(0, HERE)
+    from oracle import cmodel
     nproc = _cpu_cores() if all_cores else 1
-    kind = "reference" if cmodel.have_mysim() else "port"
-    if kind == "reference":
-        import tempfile
-        d = tempfile.mkdtemp()
-        with open(os.path.join(d, "program_memory.bin"), "wb") as f:
-            f.write(np.asarray(words, dtype="<u4").tobytes() + b"\n")
-        with open(os.path.join(d, "G_buffer_data.bin"), "wb") as f:
-            f.write(np.asarray(gimg).astype("<f2").tobytes() + b"\n")
-        cmd = [cmodel.MYSIM, "--run", str(len(words) + 1)]
-        t0 = time.time()
-        procs = [subprocess.Popen(cmd, cwd=d, stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
-                 for _ in range(nproc)]
-        for p in procs:
-            p.wait()
-        dt = time.time() - t0
-    else:
-        from concurrent.futures import ProcessPoolExecutor
-        import multiprocessing as mp
-        t0 = time.time()
-        with ProcessPoolExecutor(max_workers=nproc, mp_context=mp.get_context("spawn")) as ex:
-            list(ex.map(_run_port, [(words, gimg, gn)] * nproc))
-        dt = time.time() - t0
-    return flops * nproc / dt, nproc, kind, f"W8A16 {M}x{N}x{K} tiled program ({len(words)} instr) x {nproc} process(es)"
+    use_ref = cmodel.have_mysim()
+    reps = reps or {"gemm": 1, "rmsnorm": 2, "swiglu": 2, "softmax": 8, "rope": 8}
+    rates, notes = {}, []
+    for kind in kinds:
+        words, gimg, gn, units, uname = _mysim_program(kind)
+        r = reps.get(kind, 1)
+        if use_ref:
+            d = tempfile.mkdtemp()
+            with open(os.path.join(d, "program_memory.bin"), "wb") as f:
+                f.write(np.asarray(words, dtype="<u4").tobytes() + b"\n")
+            with open(os.path.join(d, "G_buffer_data.bin"), "wb") as f:
+                f.write(np.asarray(gimg).astype("<f2").tobytes() + b"\n")
+            cmd = " ; ".join([f"{cmodel.MYSIM} --run {len(words) + 1}"] * r)
+            t0 = time.time()
+            procs = [subprocess.Popen(["/bin/sh", "-c", cmd], cwd=d, stdout=subprocess.DEVNULL,
+                                      stderr=subprocess.DEVNULL) for _ in range(nproc)]
+            for p in procs:
+                p.wait()
+            dt = time.time() - t0
+        else:
+            from concurrent.futures import ProcessPoolExecutor
+            import multiprocessing as mp
+            t0 = time.time()
+            with ProcessPoolExecutor(max_workers=nproc, mp_context=mp.get_context("spawn")) as ex:
+                list(ex.map(_run_port, [(words, gimg, gn, r)] * nproc))
+            dt = time.time() - t0
+        rates[kind] = units * r * nproc / dt
+        notes.append(f"{kind} {units * r:.3g} {uname} x {nproc} proc in {dt:.2f} s")
+    return rates, nproc, "reference" if use_ref else "port", "; ".join(notes)
 
 
 def _run_port(args):
     sys.path.insert(0, HERE)
     from oracle import cmodel
-    words, gimg, gn = args
-    cmodel.run_oracle(words, gimg, gn, maxrun=len(words) + 1)
+    words, gimg, gn, reps = args
+    for _ in range(reps):
+        cmodel.run_oracle(words, gimg, gn, maxrun=len(words) + 1)
     return 0
+
+
+def workload_ops(workload, shape=None):
+    """What one unit of the workload asks of the NPU program path, per op kind
+    (FLOPs for the matmuls -- linears and the attention products, full T x T as
+    the NPU computes them before masking -- and elements for the vector
+    recipes), and the unit's name.  Units: a token (layer, decode, stack), a
+    TFLOP (gemm) or a GB of the vector ops' algorithmic traffic (vector)."""
+    sys.path.insert(0, HERE)
+    from npu_comp_b200.llama import LLAMA_7B as c
+    H, KV, hd, d, F = c.heads, c.kv_heads, c.head_dim, c.d, c.ffn
+    lin = c.linear_flops_per_token()
+
+    def per_token(T_q, ctx):  # one layer, one query token attending to ctx keys
+        return {"gemm": lin + 4.0 * H * hd * ctx, "rmsnorm": 2.0 * d, "swiglu": float(F),
+                "softmax": float(H * ctx), "rope": float((H + KV) * hd)}
+
+    if workload == "gemm":
+        return {"gemm": 1e12}, "TFLOP/s"
+    if workload == "vector":
+        b = vector_bytes()
+        tot = sum(b.values()) / 1e9
+        return {"rmsnorm": 2048 * 4096 / tot, "swiglu": 2048 * 11008 / tot, "softmax": 32 * 2048 * 2048 / tot}, "GB/s"
+    if workload == "layer":
+        return per_token(1, 2048), "tokens/s"      # every query row sees the full (masked) 2048-key row
+    if workload == "decode":
+        return per_token(1, 4097), "tokens/s"
+    # stack: 32 prompts x 1024 prefill + 128 greedy steps, 32 layers + lm_head per generated token
+    B, T, S, L = 32, 1024, 128, c.layers
+    tot = {k: 0.0 for k in MYSIM_KINDS}
+    for k, v in per_token(1, T).items():
+        tot[k] += v * B * T * L
+    for s in range(S):
+        for k, v in per_token(1, T + s + 1).items():
+            tot[k] += v * B * L
+    tot["gemm"] += 2.0 * d * c.vocab * B * (S + 1)
+    return {k: v / (B * (T + S)) for k, v in tot.items()}, "tokens/s"
+
+
+def vector_bytes():
+    """Algorithmic HBM bytes of the vector-op workload (2048 tokens): RMSNorm
+    x read + y written (+ gamma), SwiGLU g, u read + h written, causal softmax
+    of 32 x 2048 x 2048 scores: the unmasked entries read, every entry written
+    (masked ones as zeros)."""
+    T, d, F, H = 2048, 4096, 11008, 32
+    return {"rmsnorm": 2 * T * d * 2 + d * 2, "swiglu": 3 * T * F * 2,
+            "softmax": H * (T * (T + 1) // 2) * 2 + H * T * T * 2}
+
+
+def reference_value(workload, rates):
+    """Projected units/s of the NPU program path from the measured mysim rates."""
+    ops, unit = workload_ops(workload)
+    sec = sum(ops[k] / rates[k] for k in ops)
+    return 1.0 / sec, unit
+
+
+def torch_cpu_baseline(workload, shape=None):
+    """PyTorch on all host threads, fp32 compute on the workload's fp16/int8
+    tensors (weights dequantised once, outside the timed region).  Returns
+    {value, unit, cores, kind, sample}."""
+    import torch
+    import torch.nn.functional as Fn
+    sys.path.insert(0, HERE)
+    from npu_comp_b200.llama import LLAMA_7B as c
+    cores = _cpu_cores()
+    torch.set_num_threads(cores)
+    g = torch.Generator().manual_seed(0)
+    f16 = lambda *sh: torch.randn(*sh, generator=g).half().float()  # noqa: E731
+
+    def deq(n, k):  # per-channel int8 weights dequantised to fp32, [n, k]
+        w = torch.randn(n, k, generator=g) * 0.02
+        s = (w.abs().amax(1) / 127).half().float()
+        return (torch.clamp(torch.round(w / s[:, None]), -127, 127) * s[:, None]).contiguous()
+
+    def timed(fn, reps=2):
+        fn()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        return (time.perf_counter() - t0) / reps
+
+    def rms(x, gm):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + c.eps) * gm
+
+    def rope(x, heads, pos):
+        half = c.head_dim // 2
+        inv = c.theta ** (-2.0 * torch.arange(half, dtype=torch.float64) / c.head_dim)
+        ang = (pos.double()[:, None] * inv[None, :]).float()
+        cs, sn = ang.cos(), ang.sin()
+        x = x.view(x.shape[0], heads, c.head_dim)
+        a, b = x[..., :half], x[..., half:]
+        return torch.cat([a * cs[:, None] - b * sn[:, None], b * cs[:, None] + a * sn[:, None]], -1).flatten(1)
+
+    W = None
+
+    def layer_weights():
+        nonlocal W
+        if W is None:
+            W = {"qkv": deq(c.q_dim + 2 * c.kv_dim, c.d), "o": deq(c.d, c.q_dim), "gu": deq(2 * c.ffn, c.d),
+                 "d": deq(c.d, c.ffn), "g": torch.ones(c.d)}
+        return W
+
+    def prefill_layer(x):  # one sequence x [T, d]
+        w = layer_weights()
+        T = x.shape[0]
+        pos = torch.arange(T)
+        qkv = rms(x, w["g"]) @ w["qkv"].T
+        q = rope(qkv[:, :c.q_dim], c.heads, pos).view(T, c.heads, c.head_dim).transpose(0, 1)
+        k = rope(qkv[:, c.q_dim:c.q_dim + c.kv_dim], c.kv_heads, pos).view(T, c.kv_heads, c.head_dim).transpose(0, 1)
+        v = qkv[:, c.q_dim + c.kv_dim:].reshape(T, c.kv_heads, c.head_dim).transpose(0, 1)
+        o = Fn.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(0, 1).reshape(T, c.q_dim)
+        h = x + o @ w["o"].T
+        gu = rms(h, w["g"]) @ w["gu"].T
+        return h + (Fn.silu(gu[:, :c.ffn]) * gu[:, c.ffn:]) @ w["d"].T
+
+    def decode_layer(x, kc, vc, ctx):  # x [B, d]; caches [B, KV, ctx + 1, hd], position ctx is the new token
+        w = layer_weights()
+        B = x.shape[0]
+        pos = torch.full((B,), ctx)
+        qkv = rms(x, w["g"]) @ w["qkv"].T
+        q = rope(qkv[:, :c.q_dim], c.heads, pos).view(B, c.heads, 1, c.head_dim)
+        kc[:, :, ctx] = rope(qkv[:, c.q_dim:c.q_dim + c.kv_dim], c.kv_heads, pos).view(B, c.kv_heads, c.head_dim)
+        vc[:, :, ctx] = qkv[:, c.q_dim + c.kv_dim:].view(B, c.kv_heads, c.head_dim)
+        o = Fn.scaled_dot_product_attention(q, kc[:, :, :ctx + 1], vc[:, :, :ctx + 1]).reshape(B, c.q_dim)
+        h = x + o @ w["o"].T
+        gu = rms(h, w["g"]) @ w["gu"].T
+        return h + (Fn.silu(gu[:, :c.ffn]) * gu[:, c.ffn:]) @ w["d"].T
+
+    if workload == "gemm":
+        M, N, K = shape or (2048, 2 * c.ffn, c.d)
+        A, Wd = f16(M, K), deq(N, K)
+        t = timed(lambda: A @ Wd.T, reps=3)
+        return {"value": 2.0 * M * N * K / t / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "pytorch-cpu",
+                "sample": f"fp32 {M}x{N}x{K} matmul on dequantised int8 weights, full size"}
+    if workload == "vector":
+        x, gm = f16(2048, 4096), f16(4096) * 0.02 + 1
+        gt, ut = f16(2048, 11008), f16(2048, 11008)
+        sc = f16(32, 2048, 2048)
+        mask = torch.ones(2048, 2048, dtype=torch.bool).triu(1)
+        ts = {"rmsnorm": timed(lambda: rms(x, gm)), "swiglu": timed(lambda: Fn.silu(gt) * ut),
+              "softmax": timed(lambda: torch.softmax(sc.masked_fill(mask, float("-inf")), -1))}
+        b = vector_bytes()
+        return {"value": sum(b.values()) / sum(ts.values()) / 1e9, "unit": "GB/s", "cores": cores,
+                "kind": "pytorch-cpu", "per_op_gbs": {k: b[k] / ts[k] / 1e9 for k in ts},
+                "sample": "fp32 RMSNorm [2048,4096], SwiGLU [2048,11008], causal softmax [32,2048,2048], full size"}
+    if workload == "layer":
+        x = f16(2048, c.d)
+        t = timed(lambda: prefill_layer(x), reps=1)
+        return {"value": 2048 / t, "unit": "tokens/s", "cores": cores, "kind": "pytorch-cpu",
+                "sample": "fp32 Llama-7B layer, one 2048-token prompt, full size"}
+    if workload == "decode":
+        B, ctx = 16, 4096
+        kc, vc = f16(B, c.kv_heads, ctx + 1, c.head_dim), f16(B, c.kv_heads, ctx + 1, c.head_dim)
+        x = f16(B, c.d)
+        t = timed(lambda: decode_layer(x, kc, vc, ctx), reps=2)
+        return {"value": B / t, "unit": "tokens/s", "cores": cores, "kind": "pytorch-cpu",
+                "sample": f"fp32 Llama-7B decode layer, {B} of the 64 sequences, KV 4096"}
+    # stack: one layer of one prompt's prefill and of one batch-32 decode step,
+    # projected over 32 layers x (32 prompts + 128 steps) plus the lm_head
+    x = f16(1024, c.d)
+    t_pre = timed(lambda: prefill_layer(x), reps=1)
+    B, ctx = 32, 1024 + 64
+    kc, vc = f16(B, c.kv_heads, ctx + 1, c.head_dim), f16(B, c.kv_heads, ctx + 1, c.head_dim)
+    xd = f16(B, c.d)
+    t_dec = timed(lambda: decode_layer(xd, kc, vc, ctx), reps=2)
+    lm, hl = deq(c.vocab, c.d), f16(B, c.d)
+    t_lm = timed(lambda: hl @ lm.T, reps=2)
+    total = c.layers * (32 * t_pre + 128 * t_dec) + 129 * t_lm
+    return {"value": 32 * (1024 + 128) / total, "unit": "tokens/s", "cores": cores, "kind": "pytorch-cpu",
+            "sample": f"fp32; measured one layer of a 1024-token prompt ({t_pre:.3f} s), one batch-32 decode layer "
+                      f"at KV {ctx} ({t_dec:.3f} s) and the lm_head ({t_lm:.4f} s); projected over 32 layers x "
+                      "(32 prompts + 128 steps)"}
 
 
 # ---------------------------------------------------------------- our arm
@@ -243,6 +461,31 @@ def run_ours(args):
         config = {"workload": "llama7b_layer_decode_w8a16", "batch": B, "kv_len": ctx, "parallelism": f"tp{world}",
                   "l2": "inputs larger than L2 (4.3 GB KV cache per step)"}
         h_in, d_out = x, y
+    elif wl == "vector":
+        # RMSNorm [2048, 4096], SwiGLU [2048, 11008], causal row softmax [32, 2048, 2048]
+        x = torch.randn((2048, cfg.d), generator=gen, device=dev).half()
+        gam = (1 + 0.02 * torch.randn((cfg.d,), generator=gen, device=dev)).half()
+        gt = torch.randn((2048, cfg.ffn), generator=gen, device=dev).half()
+        ut = torch.randn((2048, cfg.ffn), generator=gen, device=dev).half()
+        sc_in = torch.randn((32, 2048, 2048), generator=gen, device=dev).half()
+        y = torch.empty_like(x)
+        h = torch.empty_like(gt)
+        pr = torch.empty_like(sc_in)
+        vb = vector_bytes()
+
+        def step(ev=None):
+            mk = llama._Marks(ev)
+            mk("rmsnorm")
+            npu.rmsnorm(x, gam, 1e-5, out=y)
+            mk("swiglu")
+            npu.swiglu(gt, ut, out=h)
+            mk("softmax")
+            npu.softmax(sc_in, causal=True, out=pr)
+            mk.end()
+        units = sum(vb.values()) / 1e9
+        unit = "GB/s"
+        config = {"workload": "llama_vector_ops_prefill"}
+        h_in, d_out = [x, gt, ut, sc_in], [y, h, pr]
     else:  # gemm: the layer's gate|up projection alone (or --shape M,N,K)
         M, N, K = (2048, 2 * cfg.ffn // world, cfg.d) if not args.shape else map(int, args.shape.split(","))
         Wf = torch.randn((K, N), generator=gen, device=dev) * 0.02
@@ -321,14 +564,15 @@ def run_ours(args):
     step_ms = float(t.item())
     ms_per_step = step_ms / args.steps
     per_rank_units = units  # TP: every rank processes the same tokens (strong scaling)
-    value = per_rank_units / (ms_per_step / 1e3) if wl != "gemm" else units * world / (ms_per_step / 1e3)
+    replicas = wl in ("gemm", "vector")  # independent copies per GPU: weak scaling
+    value = per_rank_units / (ms_per_step / 1e3) if not replicas else units * world / (ms_per_step / 1e3)
 
     # Dominant kernel roofline and per-op breakdown: eager steps with CUDA events
     # around each op on its stream, each enqueued behind a graph replay so that the
     # host is ahead of the device and the events bracket device time only.
     reps = max(1, min(args.steps, 10))
     npu.gemm_events = []
-    evs = [] if wl in ("layer", "decode") else None
+    evs = [] if wl in ("layer", "decode", "vector") else None
     for _ in range(reps):
         if flush is not None:
             flush.fill_(1.0)
@@ -360,9 +604,10 @@ def run_ours(args):
             "traffic": _traffic(wl), "share_of_step": (g_ms / ms_per_step) if ms_per_step else None}
 
     # e2e: same step through the public API with host buffers, copies inside the timed region
-    h_host = torch.empty(h_in.shape, dtype=h_in.dtype, pin_memory=True)
-    h_host.copy_(h_in)
-    o_host = torch.empty(d_out.shape, dtype=d_out.dtype, pin_memory=True)
+    h_ins = h_in if isinstance(h_in, list) else [h_in]
+    d_outs = d_out if isinstance(d_out, list) else [d_out]
+    h_hosts = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t) for t in h_ins]
+    o_hosts = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in d_outs]
     e2e_ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
     torch.cuda.synchronize()
     barrier()
@@ -370,9 +615,11 @@ def run_ours(args):
     for i in range(args.steps):
         if flush is not None:
             flush.fill_(1.0)
-        h_in.copy_(h_host, non_blocking=True)
+        for dst, src in zip(h_ins, h_hosts):
+            dst.copy_(src, non_blocking=True)
         step()
-        o_host.copy_(d_out, non_blocking=True)
+        for dst, src in zip(o_hosts, d_outs):
+            dst.copy_(src, non_blocking=True)
     e2e_ev[1].record()
     torch.cuda.synchronize()
     barrier()
@@ -381,17 +628,19 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item()) / args.steps
-    e2e_val = units / (e2e_ms / 1e3) if wl != "gemm" else units * world / (e2e_ms / 1e3)
+    e2e_val = units / (e2e_ms / 1e3) if not replicas else units * world / (e2e_ms / 1e3)
+    h2d = sum(t.numel() * t.element_size() for t in h_ins)
+    d2h = sum(t.numel() * t.element_size() for t in d_outs)
 
     out = None
     if rank == 0:
         out = {"metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-               "scaling": "strong" if wl != "gemm" else "weak", "vs_baseline": None, "dtype": "int8 x fp16 -> fp32 acc",
+               "scaling": "weak" if replicas else "strong", "vs_baseline": None,
+               "dtype": "fp16 (fp32 math)" if wl == "vector" else "int8 x fp16 -> fp32 acc",
                "data": "synthetic (seeded; random-init weights)", "config": config,
                "roofline": roof,
-               "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": h_in.numel() * h_in.element_size(),
-                       "d2h_bytes_per_step": d_out.numel() * d_out.element_size()},
+               "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
                "gpu_launches": int(launches), "clocks": clk.summary(),
                "launch": "cuda_graph" if graph is not None else "eager"}
         if wl == "layer":
@@ -399,6 +648,17 @@ def run_ours(args):
             flops = llama.layer_flops(cfg, 2048, 2048)
             out["layer_tflops"] = flops / (ms_per_step / 1e3) / 1e12
             out["layer_tensor_frac"] = out["layer_tflops"] * world / peak
+        if wl == "vector":
+            out["breakdown_us"] = breakdown
+            per = {k: {"bytes": vb[k], "us": breakdown[k], "gbs": vb[k] / (breakdown[k] * 1e-6) / 1e9,
+                       "frac": vb[k] / (breakdown[k] * 1e-6) / 1e9 / hbm} for k in vb}
+            out["per_kernel"] = per
+            out.pop("roofline_gemm", None)
+            out["roofline"] = {"kernel": "softmax_kernel (causal rows, 16-byte vectors, block reductions)",
+                               "bound": "hbm", "achieved": per["softmax"]["gbs"], "peak": hbm, "unit": "GB/s",
+                               "frac": per["softmax"]["frac"], "peak_source": f"{peak_src} HBM copy bandwidth",
+                               "bytes_per_launch": vb["softmax"], "avg_launch_us": breakdown["softmax"],
+                               "traffic": _traffic("vector")}
         if wl == "decode":
             out["breakdown_us"] = breakdown
             by = llama.decode_bytes(cfg, B, ctx + 1)
@@ -574,27 +834,30 @@ def run_stack(args):
     return out
 
 
-def _scale_rate(flop_rate, workload):
-    """CPU GEMM FLOP/s -> the workload's unit, through its FLOPs per unit."""
+def workload_config(args, world):
+    """The `config` of a bench line: the same dict for both arms."""
     sys.path.insert(0, HERE)
-    from npu_comp_b200.llama import LLAMA_7B, layer_flops
-    if workload == "gemm":
-        return flop_rate / 1e12, "TFLOP/s"
-    if workload == "stack":
-        from npu_comp_b200.llama import stack_flops
-        per_tok = stack_flops(LLAMA_7B, 32, 1024, 128) / (32 * (1024 + 128))
-    elif workload == "decode":
-        per_tok = layer_flops(LLAMA_7B, 1, 4097, causal=False)
-    else:
-        per_tok = layer_flops(LLAMA_7B, 2048, 2048) / 2048.0
-    return flop_rate / per_tok, "tokens/s"
-
-
-def _scale_note(workload):
-    return {"gemm": "GEMM FLOP rate reported as TFLOP/s",
-            "stack": "GEMM FLOP rate divided by the stack's FLOPs per token (32 layers + lm_head, prefill and decode)",
-            "decode": "GEMM FLOP rate divided by one decode layer's FLOPs per token (KV 4097)",
-            "layer": "GEMM FLOP rate divided by the prefill layer's FLOPs per token (T 2048)"}[workload]
+    from npu_comp_b200.llama import LLAMA_7B as c
+    wl = args.workload
+    if wl == "stack":
+        return {"workload": "llama7b_stack_w8a16", "layers": c.layers, "d": c.d, "heads": c.heads,
+                "head_dim": c.head_dim, "ffn": c.ffn, "vocab": c.vocab, "batch": 32, "prompt_len": 1024,
+                "new_tokens": 128, "parallelism": f"tp{world}",
+                "l2": "inputs larger than L2 (6.5 GB int8 weights, 19 GB KV cache per step)"}
+    if wl == "layer":
+        return {"workload": "llama7b_layer_prefill_w8a16", "tokens": 2048, "batch": 1, "d": c.d, "heads": c.heads,
+                "head_dim": c.head_dim, "ffn": c.ffn, "theta": c.theta, "parallelism": f"tp{world}",
+                "l2": "inputs larger than L2 (202 MB int8 weights per step)"}
+    if wl == "decode":
+        return {"workload": "llama7b_layer_decode_w8a16", "batch": args.batch or 64, "kv_len": args.ctx or 4096,
+                "parallelism": f"tp{world}", "l2": "inputs larger than L2 (4.3 GB KV cache per step)"}
+    if wl == "vector":
+        return {"workload": "llama_vector_ops_prefill", "rmsnorm": [2048, 4096], "swiglu": [2048, 11008],
+                "softmax_causal": [32, 2048, 2048], "eps": 1e-5, "parallelism": f"replica{world}",
+                "l2": "inputs larger than L2 (the softmax streams 403 MB between the other ops)"}
+    M, N, K = (2048, 2 * c.ffn, c.d) if not args.shape else tuple(map(int, args.shape.split(",")))
+    return {"workload": "w8a16_gemm", "M": M, "N": N, "K": K, "parallelism": f"replica{world}",
+            "l2": "flushed: 256 MB buffer written between steps"}
 
 
 def main():
@@ -603,7 +866,7 @@ def main():
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default: 5 for the stack, 300 otherwise)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["stack", "layer", "decode", "gemm"], default="stack")
+    ap.add_argument("--workload", choices=["stack", "layer", "decode", "gemm", "vector"], default="stack")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch every op from the host instead of a CUDA graph")
     ap.add_argument("--shape", default=None, help="gemm workload: M,N,K instead of the gate|up projection")
@@ -621,42 +884,51 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", args.gpus))
 
     if args.impl == "reference":
-        # The reference's CPU path (mysim) on this host's cores; rank 0 only.
+        # The reference's CPU path (mysim on the programs it emits) on all of
+        # this host's cores; rank 0 only.  Each step is one bounded sample of
+        # every op kind (~10-20 s); W untimed samples first (at most 3), then K
+        # timed ones (at most 10), so the run stays within minutes.
         if rank != 0:
             return 0
-        sys.path.insert(0, HERE)
-        # each step is one ~10 s sample on all host cores; W untimed samples first
-        # (at most 3), then K timed ones (at most 10) so the run stays within minutes
         warm = min(args.warmup, 3)
         for _ in range(warm):
-            cpu_reference_rate(all_cores=True)
-        rates = []
-        kind = sample = None
-        cores = 1
-        for i in range(max(1, min(args.steps, 10))):
-            r, cores, kind, sample = cpu_reference_rate(all_cores=True)
-            rates.append(r)
-        rate = statistics.median(rates)
-        value, unit = _scale_rate(rate, args.workload)
+            mysim_rates(all_cores=True)
+        samples = []
+        for _ in range(max(1, min(args.steps, 10))):
+            rates, cores, kind, note = mysim_rates(all_cores=True)
+            samples.append(reference_value(args.workload, rates)[0])
+        value = statistics.median(samples)
+        unit = reference_value(args.workload, rates)[1]
+        sample = (f"mysim on the reference's programs, {cores} concurrent processes: {note}; the workload's time "
+                  "projected from the measured rate of each op kind (matmul FLOPs, RMSNorm/SwiGLU/softmax/RoPE "
+                  "elements)")
         line = {"impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": world,
-                "steps": len(rates), "warmup": warm, "higher_is_better": True, "vs_baseline": None,
-                "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": kind,
-                                 "sample": sample + " ; " + _scale_note(args.workload)},
+                "steps": len(samples), "warmup": warm, "higher_is_better": True, "vs_baseline": None,
+                "ms_per_step": None, "dtype": "fp16 NPU datapath (f32 accumulate)",
+                "data": "synthetic (seeded)", "config": workload_config(args, world),
+                "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": kind, "sample": sample},
                 "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-                "config": {"workload": {"layer": "llama7b_layer_prefill_w8a16", "decode": "llama7b_layer_decode_w8a16",
-                                        "gemm": "w8a16_gemm", "stack": "llama7b_stack_w8a16"}[args.workload]}}
+                "rates": {k: v for k, v in rates.items()}}
+        if not args.no_cpu_baseline:
+            line["cpu_baseline_torch"] = torch_cpu_baseline(args.workload, _shape(args))
         print(json.dumps(line), flush=True)
         return 0
 
     out = run_stack(args) if args.workload == "stack" else run_ours(args)
     if rank == 0 and out is not None:
+        out["config"] = workload_config(args, world)
         if not args.no_cpu_baseline and world == 1:
-            rate, cores, kind, sample = cpu_reference_rate(all_cores=False)
-            v, u = _scale_rate(rate, args.workload)
+            rates, cores, kind, note = mysim_rates(all_cores=False)
+            v, u = reference_value(args.workload, rates)
             out["cpu_baseline"] = {"value": v, "unit": u, "cores": cores, "kind": kind,
-                                   "sample": sample + " ; " + _scale_note(args.workload)}
+                                   "sample": f"mysim, 1 process: {note}; projected from the per-op-kind rates"}
+            out["cpu_baseline_torch"] = torch_cpu_baseline(args.workload, _shape(args))
         print(json.dumps(out), flush=True)
     return 0
+
+
+def _shape(args):
+    return tuple(map(int, args.shape.split(","))) if args.shape else None
 
 
 if __name__ == "__main__":

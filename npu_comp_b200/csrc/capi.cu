@@ -31,6 +31,17 @@ int npub_internal_launch_status() {
     return NPUB_OK;
 }
 
+uint64_t npub_internal_wait_limit_ns() {
+    static const uint64_t ns = [] {
+        const char* v = getenv("NPUB_WAIT_LIMIT_MS");
+        long ms = v ? strtol(v, nullptr, 10) : 2000;
+        if (ms < 1) ms = 1;
+        if (ms > 60000) ms = 60000;
+        return (uint64_t)ms * 1000000ull;
+    }();
+    return ns;
+}
+
 int* npub_internal_device_error_word() {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_npub_device_error) != cudaSuccess) {
@@ -81,6 +92,11 @@ extern "C" int npub_device_error(int clear) {
             t_last_cuda_error = (int)e;
             return NPUB_ERR_CUDA;
         }
+        // A stream-K call whose wait gave up may have left counts in its tile
+        // counters; the library's own (allocation-free) scratch is reset
+        // here, a caller's workspace by its owner.
+        const int rc = npub_internal_noalloc_reset();
+        if (rc != NPUB_OK) return rc;
     }
     return v;
 }

@@ -58,7 +58,8 @@ struct Comm {
 
 // n elements (multiple of 8), 16-byte aligned in and out.
 __global__ void __launch_bounds__(kCommThreads) allreduce_oneshot_kernel(const CommDev c, const __half* in,
-                                                                        __half* out, int64_t n, int* err) {
+                                                                        __half* out, int64_t n, int* err,
+                                                                        uint64_t limit_ns) {
     pdl_trigger();
     pdl_wait();
     __shared__ int ok_s;
@@ -88,7 +89,7 @@ __global__ void __launch_bounds__(kCommThreads) allreduce_oneshot_kernel(const C
                     ok = true;
                     break;
                 }
-                if ((it & 1023u) == 0 && globaltimer_ns() - t0 > 2000000000ull) break;
+                if ((it & 1023u) == 0 && globaltimer_ns() - t0 > limit_ns) break;
             }
         }
         if (!ok) {
@@ -210,7 +211,8 @@ extern "C" int npub_allreduce_f16(void* comm, const void* in, void* out, int64_t
     const int64_t blocks = (n + region - 1) / region;
     return launch_pdl(allreduce_oneshot_kernel, dim3((unsigned)blocks), dim3(kCommThreads), 0,
                       reinterpret_cast<cudaStream_t>(stream), c->d, reinterpret_cast<const __half*>(in),
-                      reinterpret_cast<__half*>(out), n, npub_internal_device_error_word());
+                      reinterpret_cast<__half*>(out), n, npub_internal_device_error_word(),
+                      npub_internal_wait_limit_ns());
 }
 
 namespace npub {

@@ -29,6 +29,13 @@ void npub_internal_set_cuda_error(cudaError_t e);
 int npub_internal_launch_status();
 // Device error word used by bounded waits (one per device, zero-initialised).
 int* npub_internal_device_error_word();
+// Limit of the waits on other CTAs' or other ranks' progress (stream-K tile
+// pieces, peer flags of the all-reduces): NPUB_WAIT_LIMIT_MS in the
+// environment when the library loads (1 ms .. 60 s), else 2 s.
+uint64_t npub_internal_wait_limit_ns();
+// Re-zeroes the allocation-free entry point's tile counters on the current
+// device (after a wait gave up, they may hold counts of the aborted call).
+int npub_internal_noalloc_reset();
 
 static inline bool npub_aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 

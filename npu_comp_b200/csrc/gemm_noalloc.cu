@@ -15,10 +15,13 @@
 // first kSkinnyCounterBytes hold the tile counters of the few-token (M <= 64)
 // kernel, which start at zero (the array is zero-initialised when the module
 // loads) and which every completed call leaves at zero; nothing else is ever
-// written there.  The rest holds split-K partials, fully overwritten before
+// written there.  A call in which a bounded wait gave up (the device error
+// word set, NPUB_ERR_DEVICE_TIMEOUT from npub_device_error) may leave counts
+// behind; npub_device_error(1) re-zeroes them along with the error word.  The rest holds split-K partials, fully overwritten before
 // they are read.  Calls that overlap on the GPU (different streams, or
 // different host threads on the same device) race on the array.
 #include "common.cuh"
+#include "gemm_w8a16_skinny.h"
 
 #include <mutex>
 
@@ -30,7 +33,9 @@ static void* g_noalloc_ptr[64];
 
 // Device address of g_noalloc_scratch for the current device.  In host code
 // the array's name is only a host-side stand-in, so the address is looked up
-// once per device, with that device current, and cached.
+// once per device, with that device current, and cached.  The cache assumes
+// the module stays loaded: the library must not be used across a
+// cudaDeviceReset (which unloads the module and frees the array).
 static int noalloc_scratch(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -50,6 +55,30 @@ static int noalloc_scratch(void** out) {
         g_noalloc_ptr[dev] = p;
     }
     *out = g_noalloc_ptr[dev];
+    return NPUB_OK;
+}
+
+int npub_internal_noalloc_reset() {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        npub_internal_set_cuda_error(e);
+        return NPUB_ERR_CUDA;
+    }
+    if (dev < 0 || dev >= 64) return NPUB_OK;
+    void* p = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        p = g_noalloc_ptr[dev];
+    }
+    if (!p) return NPUB_OK;  // never used on this device: the counters are still zero
+    // cudaMemset writes the counters in place; nothing is allocated
+    e = cudaMemset(p, 0, npub::kSkinnyCounterBytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        npub_internal_set_cuda_error(e);
+        return NPUB_ERR_CUDA;
+    }
     return NPUB_OK;
 }
 

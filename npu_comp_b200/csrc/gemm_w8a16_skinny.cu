@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                                 ok = true;
                                 break;
                             }
-                            if ((it & 255u) == 0 && (*abort_flag || globaltimer_ns() - t0 > 2000000000ull)) break;
+                            if ((it & 255u) == 0 && (*abort_flag || globaltimer_ns() - t0 > p.wait_ns)) break;
                         }
                     }
                     if (ok) *cnt = 0u;  // left zero for the next call
@@ -489,7 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                                 ok = true;
                                 break;
                             }
-                            if ((it & 1023u) == 0 && globaltimer_ns() - t0 > 2000000000ull) break;
+                            if ((it & 1023u) == 0 && globaltimer_ns() - t0 > p.wait_ns) break;
                         }
                     }
                 }
@@ -688,6 +688,7 @@ int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, con
     p.cnt = reinterpret_cast<unsigned*>(ws);
     p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kSkinnyCounterBytes);
     p.err = npub_internal_device_error_word();
+    p.wait_ns = npub_internal_wait_limit_ns();
     p.swiglu = swiglu ? 1 : 0;
     const int grid = skinny_grid(N, K);
     if (ar && ar->world > 1) {

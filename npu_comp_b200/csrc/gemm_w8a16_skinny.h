@@ -41,6 +41,7 @@ struct SkinnyParams {
     float* part;    // [grid][128][BT] fp32 partial tiles
     unsigned* cnt;  // [n_tiles][4] pieces arrived per tile and 32-row quarter (zero between calls)
     int* err;
+    uint64_t wait_ns;  // limit of the waits on other CTAs' pieces and other ranks' flags
     SkinnyAR ar;
     int swiglu;     // 1: rows 2c / 2c+1 are gate / up; C [M, N/2] = fp16(silu(g) * u)
 };

@@ -142,11 +142,30 @@ def quantize_linear(W: torch.Tensor):
     return npu.quantize_w8(W.contiguous())
 
 
+def _pack_layer(cfg: LlamaConfig, Wqkv: torch.Tensor, Wo: torch.Tensor, Wgu: torch.Tensor, Wd: torch.Tensor,
+                g1: torch.Tensor, g2: torch.Tensor, tp: TP) -> LayerWeights:
+    """Quantise the fused float linears (x @ W layout: Wqkv [d, (H+2KV)*hd],
+    Wo [H*hd, d], Wgu [d, 2F] = [gate | up], Wd [F, d]) per output channel over
+    the full matrices, then keep this rank's shard: output rows of the
+    column-parallel QKV and gate|up (gate|up interleaved per rank), input
+    columns (K) of the row-parallel O and down."""
+    rg = tp_ranges(cfg, tp.rank, tp.size)
+    hq, hk, f = cfg.heads // tp.size, cfg.kv_heads // tp.size, cfg.ffn // tp.size
+    q, s = quantize_linear(Wqkv)                                         # QKV, column parallel
+    wqkv, sqkv = _shard_rows(q, s, rg["qkv"])
+    q, so = quantize_linear(Wo)                                          # O, row parallel
+    wo = q[:, rg["o"][0].start:rg["o"][0].stop].contiguous()
+    q, s = quantize_linear(Wgu)                                          # gate | up, column parallel
+    wgu, sgu = npu.interleave_gate_up(*_shard_rows(q, s, rg["gu"]))
+    q, sd = quantize_linear(Wd)                                          # down, row parallel
+    wd = q[:, rg["d"][0].start:rg["d"][0].stop].contiguous()
+    del q
+    return LayerWeights(wqkv, sqkv, wo, so, wgu, sgu, wd, sd, g1.contiguous(), g2.contiguous(), hq, hk, f)
+
+
 def make_layer(cfg: LlamaConfig, seed: int, device, tp: TP = TP(), std: float = 0.02) -> LayerWeights:
     """Random-init layer (weights ~N(0, std), RMSNorm gains 1), quantised per
     output channel over the full matrix, then sliced to this rank's shard."""
-    rg = tp_ranges(cfg, tp.rank, tp.size)
-    hq, hk, f = cfg.heads // tp.size, cfg.kv_heads // tp.size, cfg.ffn // tp.size
     d = cfg.d
     gen = torch.Generator(device=device)
     gen.manual_seed(int(seed))
@@ -154,34 +173,30 @@ def make_layer(cfg: LlamaConfig, seed: int, device, tp: TP = TP(), std: float = 
     def rnd(k, m):
         return torch.randn((k, m), generator=gen, device=device, dtype=torch.float32) * std
 
-    q, s = quantize_linear(rnd(d, cfg.q_dim + 2 * cfg.kv_dim))          # QKV, column parallel
-    wqkv, sqkv = _shard_rows(q, s, rg["qkv"])
-    q, so = quantize_linear(rnd(cfg.q_dim, d))                           # O, row parallel
-    wo = q[:, rg["o"][0].start:rg["o"][0].stop].contiguous()
-    q, s = quantize_linear(rnd(d, 2 * cfg.ffn))                          # gate | up, column parallel
-    wgu, sgu = npu.interleave_gate_up(*_shard_rows(q, s, rg["gu"]))
-    q, sd = quantize_linear(rnd(cfg.ffn, d))                             # down, row parallel
-    wd = q[:, rg["d"][0].start:rg["d"][0].stop].contiguous()
-    del q
+    # drawn in this order (QKV, O, gate|up, down) so a seed gives the same layer on every rank
+    Wqkv = rnd(d, cfg.q_dim + 2 * cfg.kv_dim)
+    Wo = rnd(cfg.q_dim, d)
+    Wgu = rnd(d, 2 * cfg.ffn)
+    Wd = rnd(cfg.ffn, d)
     ones = torch.ones(d, dtype=torch.float16, device=device)
-    return LayerWeights(wqkv, sqkv, wo, so, wgu, sgu, wd, sd, ones, ones.clone(), hq, hk, f)
+    return _pack_layer(cfg, Wqkv, Wo, Wgu, Wd, ones, ones.clone(), tp)
 
 
-def layer_from_float(cfg: LlamaConfig, W: Dict[str, torch.Tensor], device) -> LayerWeights:
-    """Build a 1-rank layer from float weights in the reference's layout
+def layer_from_float(cfg: LlamaConfig, W: Dict[str, torch.Tensor], device, tp: TP = TP()) -> LayerWeights:
+    """Build this rank's layer from float weights in the reference's layout
     (model.py:44-61 / llama_layer.py:24-31): Wq{h} [d, hd], Wk{k}, Wv{k} [d, hd],
-    Wo{h} [hd, d], Wg, Wu [d, f], Wd [f, d], Wn1, Wn2 [d]."""
+    Wo{h} [hd, d], Wg, Wu [d, f], Wd [f, d], Wn1, Wn2 [d].  The matrices are
+    fused and quantised over their full size, then sharded for tp (heads, kv
+    heads and FFN columns split evenly; GQA groups stay whole per rank)."""
     H, KV = cfg.heads, cfg.kv_heads
     f32 = lambda t: torch.as_tensor(t, dtype=torch.float32, device=device)  # noqa: E731
     Wqkv = torch.cat([f32(W[f"Wq{h}"]) for h in range(H)] + [f32(W[f"Wk{k}"]) for k in range(KV)]
                      + [f32(W[f"Wv{k}"]) for k in range(KV)], dim=1)
-    wqkv, sqkv = quantize_linear(Wqkv)
-    wo, so = quantize_linear(torch.cat([f32(W[f"Wo{h}"]) for h in range(H)], dim=0))
-    wgu, sgu = npu.interleave_gate_up(*quantize_linear(torch.cat([f32(W["Wg"]), f32(W["Wu"])], dim=1)))
-    wd, sd = quantize_linear(f32(W["Wd"]))
+    Wo = torch.cat([f32(W[f"Wo{h}"]) for h in range(H)], dim=0)
+    Wgu = torch.cat([f32(W["Wg"]), f32(W["Wu"])], dim=1)
     g1 = f32(W["Wn1"]).reshape(-1).half()
     g2 = f32(W["Wn2"]).reshape(-1).half()
-    return LayerWeights(wqkv, sqkv, wo, so, wgu, sgu, wd, sd, g1, g2, H, KV, cfg.ffn)
+    return _pack_layer(cfg, Wqkv, Wo, Wgu, f32(W["Wd"]), g1, g2, tp)
 
 
 @dataclass
@@ -297,10 +312,14 @@ def llama_layer(x: torch.Tensor, weights, cfg: LlamaConfig, *, batch: int = 1, t
     weights: LayerWeights (make_layer / layer_from_float), or the reference's
     float weight dict (Wq{h}, Wk{k}, Wv{k}, Wo{h}, Wg, Wu, Wd, Wn1, Wn2 in the
     layout of llama_layer.py:24-31), which is quantised per output channel
-    here (one rank).  Same computation and bits as layer_prefill.
+    here and sharded for tp (every rank passes the full dict).  Same
+    computation and bits as layer_prefill.
     """
     if not isinstance(weights, LayerWeights):
-        weights = layer_from_float(cfg, weights, x.device)
+        weights = layer_from_float(cfg, weights, x.device, tp)
+    elif tp.size > 1 and (weights.heads * tp.size != cfg.heads or weights.ffn * tp.size != cfg.ffn):
+        raise ValueError(f"weights hold {weights.heads} of {cfg.heads} heads and {weights.ffn} of {cfg.ffn} FFN "
+                         f"columns: not a shard for tp={tp.size}")
     return layer_prefill(x, weights, cfg, batch=batch, tp=tp, positions=positions, kv_out=kv_out, scratch=scratch,
                          out=out)
 

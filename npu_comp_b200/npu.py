@@ -25,7 +25,8 @@ from ._lib import NpubError  # noqa: F401  (re-exported)
 
 __all__ = [
     "fp16", "quantize_w8", "matmul", "rmsnorm", "add", "swiglu", "softmax", "rope", "attention",
-    "attention_decode", "kv_append", "rope_kv_append", "rope_kv_store", "matmul_swiglu", "interleave_gate_up", "embed", "argmax", "isa_vector", "f32_to_f16_bits", "f16_bits_to_f32", "NpubError",
+    "attention_decode", "kv_append", "rope_kv_append", "rope_kv_store", "matmul_swiglu", "interleave_gate_up",
+    "embed", "argmax", "isa_vector", "f32_to_f16_bits", "f16_bits_to_f32", "device_error", "NpubError",
 ]
 
 
@@ -74,6 +75,27 @@ def _workspace(nbytes: int, device) -> Tuple[Optional[torch.Tensor], int]:
 # that captured its address.
 _zeroed_ws = {}
 _retired_ws = []
+
+
+def device_error(clear: bool = False) -> int:
+    """The current device's error word: non-zero when a bounded device-side wait
+    gave up (NPUB_ERR_DEVICE_TIMEOUT cases; synchronises the device).
+
+    With clear=True the word is reset, and so are the tile counters of every
+    W8A16 workspace this module hands out and of the library's allocation-free
+    scratch: a stream-K call whose wait gave up may have left counts there,
+    which the next call would take for pieces already written."""
+    lib = _lib.load()
+    v = int(lib.npub_device_error(1 if clear else 0))
+    if v == _lib.NPUB_ERR_CUDA:
+        raise NpubError("npub_device_error", v, lib.npub_strerror(v).decode())
+    if clear:
+        dev = torch.cuda.current_device()
+        for (d, _), buf in _zeroed_ws.items():
+            if d == dev:
+                buf.zero_()
+        torch.cuda.synchronize()
+    return v
 
 
 def _zeroed_workspace(nbytes: int, device) -> Tuple[Optional[torch.Tensor], int]:

@@ -277,3 +277,146 @@ def quantized_weights(W: Dict[str, np.ndarray], H: int, KV: int) -> Dict[str, np
     out["Wd"] = (q.astype(np.float64) * s.astype(np.float64)[:, None]).T
     assert out["Wd"].shape == (F, D)
     return out
+
+
+# ------------------------------------------ layer on quantised, fused weights
+#
+# The same float64 layer as ref_layer (model.py:115-157), written over the
+# weights in the layout the W8A16 build stores them: int8 q [N, K] with fp16
+# per-output-channel scales s [N] (applied exactly: q * s in float64), QKV
+# fused as [q heads | k heads | v heads] rows, gate|up rows interleaved
+# (row 2c gate channel c, row 2c + 1 up channel c).  Used at full Llama-7B
+# size, where the per-head weight dict of ref_layer is not at hand.
+
+def dequant(q: np.ndarray, s: np.ndarray) -> np.ndarray:
+    """float64 q[n, k] * s[n] (exact: an 8-bit integer times an fp16 value)."""
+    out = q.astype(np.float64)
+    np.multiply(out, s.astype(np.float64)[:, None], out=out)
+    return out
+
+
+def _rms64(X: np.ndarray, g: np.ndarray, eps: float) -> np.ndarray:
+    ms = np.mean(X * X, axis=1, keepdims=True) + eps
+    return X / np.sqrt(ms) * np.asarray(g, dtype=np.float64).reshape(1, -1)
+
+
+def _rope64(M: np.ndarray, heads: int, hd: int, positions: np.ndarray, theta: float,
+            inv_freq: Optional[np.ndarray] = None) -> np.ndarray:
+    """rotate_half RoPE (model.py:125-131) of every head of M [T, heads*hd] at
+    the given positions; inv_freq [hd/2] overrides theta^(-2i/hd)."""
+    half = hd // 2
+    freqs = theta ** (-2.0 * np.arange(half) / hd) if inv_freq is None else np.asarray(inv_freq, np.float64)
+    ang = positions.astype(np.float64)[:, None] * freqs[None, :]
+    c, s = np.cos(ang), np.sin(ang)
+    X = M.reshape(M.shape[0], heads, hd)
+    a, b = X[:, :, :half], X[:, :, half:]
+    out = np.concatenate([a * c[:, None, :] - b * s[:, None, :], b * c[:, None, :] + a * s[:, None, :]], axis=2)
+    return out.reshape(M.shape[0], heads * hd)
+
+
+def prepare_layer(L: Dict[str, np.ndarray]) -> Dict[str, np.ndarray]:
+    """The float64 matrices a quantised layer applies ([N, K] each), computed
+    once; ref_layer_q and ref_decode_layer_q accept either form."""
+    if "qkv" in L:
+        return L
+    return {"qkv": dequant(L["wqkv"], L["sqkv"]), "o": dequant(L["wo"], L["so"]),
+            "gu": dequant(L["wgu"], L["sgu"]), "d": dequant(L["wd"], L["sd"]),
+            "g1": np.asarray(L["g1"], np.float64), "g2": np.asarray(L["g2"], np.float64)}
+
+
+def ref_layer_q(L: Dict[str, np.ndarray], x: np.ndarray, heads: int, kv_heads: int, hd: int, eps: float,
+                theta: float = 10000.0, positions: Optional[np.ndarray] = None,
+                inv_freq: Optional[np.ndarray] = None) -> np.ndarray:
+    """float64 causal Llama layer for one sequence x [T, d] on quantised weights
+    L = {wqkv, sqkv, wo, so, wgu, sgu, wd, sd, g1, g2} (module comment above),
+    or on prepare_layer(L)."""
+    P = prepare_layer(L)
+    T = x.shape[0]
+    pos = np.arange(T) if positions is None else np.asarray(positions)
+    x = x.astype(np.float64)
+    qd, kd = heads * hd, kv_heads * hd
+    xn = _rms64(x, P["g1"], eps)
+    qkv = xn @ P["qkv"].T
+    q = _rope64(qkv[:, :qd], heads, hd, pos, theta, inv_freq)
+    k = _rope64(qkv[:, qd:qd + kd], kv_heads, hd, pos, theta, inv_freq)
+    v = qkv[:, qd + kd:qd + 2 * kd]
+    ctx = np.zeros((T, qd))
+    grp = heads // kv_heads
+    mask = np.triu(np.ones((T, T), dtype=bool), 1)
+    for h in range(heads):
+        kv = h // grp
+        S = (q[:, h * hd:(h + 1) * hd] @ k[:, kv * hd:(kv + 1) * hd].T) / math.sqrt(hd)
+        S[mask] = -np.inf
+        S -= S.max(axis=1, keepdims=True)
+        E = np.exp(S)
+        E /= E.sum(axis=1, keepdims=True)
+        ctx[:, h * hd:(h + 1) * hd] = E @ v[:, kv * hd:(kv + 1) * hd]
+    h_ = x + ctx @ P["o"].T
+    return h_ + _ffn64(P, _rms64(h_, P["g2"], eps))
+
+
+def _ffn64(P: Dict[str, np.ndarray], hn: np.ndarray) -> np.ndarray:
+    gu = hn @ P["gu"].T
+    g, u = gu[:, 0::2], gu[:, 1::2]
+    return (g / (1.0 + np.exp(-g)) * u) @ P["d"].T
+
+
+def ref_decode_layer_q(L: Dict[str, np.ndarray], x: np.ndarray, k_cache, v_cache, pos: np.ndarray, heads: int,
+                       kv_heads: int, hd: int, eps: float, theta: float = 10000.0) -> np.ndarray:
+    """One decode step of the float64 layer: x [B, d] is the token at position
+    pos[b] of sequence b; k_cache / v_cache [B, kv_heads, >= pos[b], hd] hold
+    the (already rotated) keys and the values of positions 0 .. pos[b] - 1.
+    The token's own k and v join them; attention covers pos[b] + 1 keys."""
+    P = prepare_layer(L)
+    B = x.shape[0]
+    x = x.astype(np.float64)
+    qd, kd = heads * hd, kv_heads * hd
+    xn = _rms64(x, P["g1"], eps)
+    qkv = xn @ P["qkv"].T
+    pos = np.asarray(pos)
+    q = _rope64(qkv[:, :qd], heads, hd, pos, theta)
+    k = _rope64(qkv[:, qd:qd + kd], kv_heads, hd, pos, theta)
+    v = qkv[:, qd + kd:qd + 2 * kd]
+    grp = heads // kv_heads
+    ctx = np.zeros((B, qd))
+    for b in range(B):
+        n = int(pos[b])
+        Kb = np.concatenate([np.asarray(k_cache[b, :, :n], dtype=np.float64),
+                             k[b].reshape(kv_heads, 1, hd)], axis=1)          # [KV, n + 1, hd]
+        Vb = np.concatenate([np.asarray(v_cache[b, :, :n], dtype=np.float64),
+                             v[b].reshape(kv_heads, 1, hd)], axis=1)
+        Q = q[b].reshape(kv_heads, grp, hd)
+        S = np.einsum("kgd,ktd->kgt", Q, Kb) / math.sqrt(hd)
+        S -= S.max(axis=2, keepdims=True)
+        E = np.exp(S)
+        E /= E.sum(axis=2, keepdims=True)
+        ctx[b] = np.einsum("kgt,ktd->kgd", E, Vb).reshape(qd)
+    h_ = x + ctx @ P["o"].T
+    return h_ + _ffn64(P, _rms64(h_, P["g2"], eps))
+
+
+def ref_stack_logits(layers, embed: np.ndarray, norm: np.ndarray, lm_head: np.ndarray, tokens: np.ndarray,
+                     heads: int, kv_heads: int, hd: int, eps: float, theta: float = 10000.0,
+                     rows: Optional[np.ndarray] = None) -> np.ndarray:
+    """float64 decoder stack on sequences of token ids tokens [B, T]: embedding
+    rows (fp16 table), the layers (an iterable of ref_layer_q weight dicts,
+    each prepared once and applied to every sequence), final RMSNorm and the
+    lm_head [vocab, d] -> logits [B, len(rows), vocab] of `rows` (default:
+    every position).  Greedy decoding feeds the chosen tokens back as later
+    positions, so the logits of decode step s are row T - 1 + s of one pass
+    over the prompt followed by the generated tokens."""
+    from concurrent.futures import ThreadPoolExecutor
+    tokens = np.atleast_2d(np.asarray(tokens))
+    emb = np.asarray(embed)
+    xs = [emb[t].astype(np.float64) for t in tokens]
+    it = iter(layers)
+    with ThreadPoolExecutor(max_workers=4) as ex:  # dequantise the next layers while one is applied
+        while True:
+            group = [L for _, L in zip(range(4), it)]
+            if not group:
+                break
+            for P in ex.map(prepare_layer, group):
+                xs = [ref_layer_q(P, x, heads, kv_heads, hd, eps, theta) for x in xs]
+    rows = np.arange(tokens.shape[1]) if rows is None else np.asarray(rows)
+    lm = np.asarray(lm_head, dtype=np.float64)
+    return np.stack([_rms64(x[rows], norm, eps) @ lm.T for x in xs])

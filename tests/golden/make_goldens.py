@@ -1,8 +1,10 @@
 """Regenerate the golden fixtures of tests/golden/ from the reference tree.
 
-Run in a container where the reference (KwanyoungCho/NPU_COMP) is mounted:
+Run where a checkout of the reference (KwanyoungCho/NPU_COMP) is available:
 
-    python tests/golden/make_goldens.py [--ref /root/reference]
+    python tests/golden/make_goldens.py --ref <reference root>
+
+(or with NPU_COMP_REF=<reference root> in the environment).
 
 It never copies reference sources into this repository.  It compiles and runs
 the reference's own generators and simulator (outputs under oracle/_ref/ and a
@@ -186,8 +188,11 @@ def config1():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("NPU_COMP_REF"),
+                    help="root of the reference checkout (default: $NPU_COMP_REF)")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("the reference root is required: --ref <dir> or NPU_COMP_REF=<dir>")
     subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={a.ref}"], check=True)
     gold = isa_goldens(a.ref)
     with open(os.path.join(HERE, "isa_goldens.json"), "w") as f:

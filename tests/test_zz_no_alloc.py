@@ -94,3 +94,30 @@ def test_noalloc_rejects_requests_beyond_its_scratch(cuda_device):
     st = noalloc(A, q, s, out)
     assert st == _lib.NPUB_ERR_SCRATCH_LIMIT
     assert b"scratch" in ctypes.string_at(lib.npub_strerror(st))
+
+
+def test_clearing_the_device_error_rezeroes_tile_counters(cuda_device):
+    """A stream-K call whose bounded wait gave up can leave counts in its tile
+    counters (the first 64 KiB of a W8A16 workspace, and of the static array
+    behind npub_w8a16_gemm_noalloc, which no caller can reach).  Clearing the
+    device error word (npub_device_error(1), npu.device_error(clear=True))
+    re-zeroes both.  Here stale counts are written into the cached workspace
+    with a fill; after the clear, both entry points give the right result."""
+    from npu_comp_b200 import npu
+    M, N, K = 32, 12288, 4096                      # a stream-K (decode-sized) shape
+    assert "skinny" in _lib.load().npub_w8a16_kernel_name(M, N, K).decode()
+    A, q, s = inputs(M, N, K, cuda_device, seed=5)
+    nb.matmul(A, q, s)                             # creates the cached workspace of this stream
+    key = (cuda_device.index or 0, torch.cuda.current_stream().cuda_stream)
+    npu._zeroed_ws[key][: 64 << 10].fill_(0x7F)    # stale counts, as an aborted call leaves them
+    assert npu.device_error(clear=True) == 0
+    assert int(npu._zeroed_ws[key][: 64 << 10].count_nonzero()) == 0
+    A2, q2, s2 = inputs(M, N, K, cuda_device, seed=6)
+    expect = (A2.float() @ q2.float().t()) * s2.float()[None, :]
+    got = nb.matmul(A2, q2, s2).float()
+    assert ((got - expect).abs().max() / expect.abs().max()).item() <= TOL
+    out = torch.empty((M, N), dtype=torch.float16, device=cuda_device)
+    for _ in range(2):
+        assert noalloc(A2, q2, s2, out) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(out.float(), got)
