@@ -539,6 +539,21 @@ def run_ours(args):
     eager_step()
     torch.cuda.synchronize()
     launches_per_step = _lib.launch_count() - c0  # kernels of one step (a graph replay bypasses the counter)
+    if args.steps is None:
+        # no --steps: enough steps for ~0.6 s of timed work (the clock sampler
+        # needs a few 50 ms samples), the same count on every rank
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            if flush is not None:
+                flush.fill_(1.0)
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        est = torch.tensor([e0.elapsed_time(e1) / 5], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(est, op=dist.ReduceOp.MAX)
+        args.steps = int(min(20000, max(50, 600.0 / max(float(est.item()), 1e-3))))
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     try:
         smi_id = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
@@ -863,7 +878,8 @@ def workload_config(args, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=None, help="timed steps (default: 5 for the stack, 300 otherwise)")
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: 5 for the stack, else as many as ~0.6 s of device time)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["stack", "layer", "decode", "gemm", "vector"], default="stack")
@@ -878,8 +894,8 @@ def main():
                          "then exit without a bench line")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
-    if args.steps is None:
-        args.steps = 5 if args.workload == "stack" else 300
+    if args.steps is None and args.workload == "stack":
+        args.steps = 5
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", args.gpus))
 
@@ -894,7 +910,7 @@ def main():
         for _ in range(warm):
             mysim_rates(all_cores=True)
         samples = []
-        for _ in range(max(1, min(args.steps, 10))):
+        for _ in range(max(1, min(args.steps or 5, 10))):
             rates, cores, kind, note = mysim_rates(all_cores=True)
             samples.append(reference_value(args.workload, rates)[0])
         value = statistics.median(samples)

@@ -250,6 +250,41 @@ int npub_f32_to_f16(const float* x, uint16_t* y, int64_t n, void* stream);
 /* fp16 -> fp32 (the cmodel's load of the G-buffer). */
 int npub_f16_to_f32(const uint16_t* x, float* y, int64_t n, void* stream);
 
+/* ------------------------------------------------------------ programs --
+ * Whole NPU programs on the GPU: the drop-in for run(asm, gbuf, gn, rundir,
+ * maxrun) of b_program_examples/npu.py:62-71 and run(program, gbuf, gn,
+ * maxrun) of d_compiler/npu_compiler/runtime.py:46-77, which write
+ * program_memory.bin and G_buffer_data.bin and run the cmodel
+ * (_poc/mysim.cpp:42-157) on them.
+ *
+ * npub_program_create decodes words[0 .. nwords) on the host -- at most
+ * maxrun program-counter steps, HALT (0xFF) ends the program, words past the
+ * end are NOPs, g_in is the number of G-buffer words the caller will pass --
+ * into tasks in dependency order.  It returns NPUB_ERR_INVALID_ARG when an
+ * instruction would read past a PE input buffer (undefined behaviour in the
+ * cmodel); npub_program_error_pc() then gives its program counter (this
+ * thread's last failed create).  npub_program_load copies the task tables
+ * into a caller workspace of npub_program_workspace() bytes (256-byte
+ * aligned; synchronises the stream).  npub_program_run executes the program
+ * on the G-buffer g_in [n_in] (fp16, device; n_in <= the g_in given to
+ * create) and writes the first gn words of the final G-buffer to g_out (fp16,
+ * device; words the machine never held read +0), which is the cmodel's
+ * --gout write-back.  A run may follow a load any number of times.
+ * Results are the cmodel's bits (float32 arithmetic without contraction,
+ * the matmul's ascending-k accumulation, x86-64 integer conversions, fp16
+ * store rounding), except exp (0x0F) and the matrix activation x^2 sigmoid(x)
+ * (CUDA's expf: a few float32 ulps from the host libm before the fp16 store).
+ * npub_program_info fills up to 7 counts: steps executed, tasks, levels,
+ * G-buffer words, temporary words, work chunks, CTAs of the run. */
+int npub_program_create(const uint32_t* words, int64_t nwords, int64_t maxrun, int64_t g_in, void** program);
+int npub_program_error_pc(void);
+int npub_program_info(const void* program, int64_t* info, int n);
+size_t npub_program_workspace(const void* program);
+int npub_program_load(const void* program, void* workspace, size_t workspace_bytes, void* stream);
+int npub_program_run(const void* program, const uint16_t* g_in, int64_t n_in, uint16_t* g_out, int64_t gn,
+                     void* workspace, size_t workspace_bytes, void* stream);
+int npub_program_destroy(void* program);
+
 /* ---------------------------------------------- tensor-parallel all-reduce --
  * One-shot fp16 all-reduce over NVLink peer memory for the decode-sized
  * reductions after the row-parallel O and down projections (the TP sharding

@@ -60,6 +60,13 @@ SIGNATURES = {
     "npub_isa_vector": (_i, [_u32, _p, _p, _p, _p, _i64, _p]),
     "npub_f32_to_f16": (_i, [_p, _p, _i64, _p]),
     "npub_f16_to_f32": (_i, [_p, _p, _i64, _p]),
+    "npub_program_create": (_i, [_p, _i64, _i64, _i64, ctypes.POINTER(ctypes.c_void_p)]),
+    "npub_program_error_pc": (_i, []),
+    "npub_program_info": (_i, [_p, ctypes.POINTER(ctypes.c_int64), _i]),
+    "npub_program_workspace": (_sz, [_p]),
+    "npub_program_load": (_i, [_p, _p, _sz, _p]),
+    "npub_program_run": (_i, [_p, _p, _i64, _p, _i64, _p, _sz, _p]),
+    "npub_program_destroy": (_i, [_p]),
     "npub_comm_handle_bytes": (_sz, []),
     "npub_comm_create": (_i, [_i, _i, _sz, ctypes.POINTER(ctypes.c_void_p), _p]),
     "npub_comm_open": (_i, [_p, _p]),

@@ -103,6 +103,80 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const __half* __restrict__ 
     }
 }
 
+// One warp per row, two rows per CTA, for rows of up to 32 x 8 x CPL elements
+// (d = 4096: 16 16-byte chunks per lane).  Every load of the row is issued
+// before the first is used, the sum of squares is a warp-shuffle reduction
+// (no block barrier), and the row stays in registers as packed fp16 between
+// the two passes.  At 2048 x 4096 it measured 10.6 us (one CTA per row with
+// block reductions: 11.1 us; persistent double-buffered CTAs: 10.0-19.6 us).
+template <int CPL>
+__global__ void __launch_bounds__(64) rmsnorm_warp_kernel(const __half* __restrict__ x, int64_t ldx,
+                                                         const __half* __restrict__ r, int64_t ldr, __half* xo,
+                                                         int64_t ldxo, const __half* __restrict__ gamma,
+                                                         __half* __restrict__ y, int64_t ldy, int rows, int d,
+                                                         float eps) {
+    pdl_trigger();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 2 + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const int nch = d / kVec;
+    const __half* xr = x + (int64_t)row * ldx;
+    uint4 v[CPL];
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+        const int ch = lane + 32 * j;
+        if (ch < nch) v[j] = *reinterpret_cast<const uint4*>(xr + ch * kVec);
+    }
+    if (r) {
+        const __half* rr = r + (int64_t)row * ldr;
+        uint4 w[CPL];
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) {
+            const int ch = lane + 32 * j;
+            if (ch < nch) w[j] = *reinterpret_cast<const uint4*>(rr + ch * kVec);
+        }
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) {
+            const int ch = lane + 32 * j;
+            if (ch < nch) {
+                float a[8], b[8];
+                unpack8(v[j], a);
+                unpack8(w[j], b);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) a[i] = a[i] + b[i];
+                v[j] = pack8(a);  // fp16(x + r), the residual stream
+                *reinterpret_cast<uint4*>(xo + (int64_t)row * ldxo + ch * kVec) = v[j];
+            }
+        }
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+        if (lane + 32 * j < nch) {
+            float a[8];
+            unpack8(v[j], a);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ss += a[i] * a[i];
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = 1.0f / sqrtf(ss / (float)d + eps);
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+        const int ch = lane + 32 * j;
+        if (ch < nch) {
+            float a[8], g[8], o[8];
+            unpack8(v[j], a);
+            unpack8(__ldg(reinterpret_cast<const uint4*>(gamma + ch * kVec)), g);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = (a[i] * inv) * g[i];
+            *reinterpret_cast<uint4*>(y + (int64_t)row * ldy + ch * kVec) = pack8(o);
+        }
+    }
+}
+
 // ------------------------------------------------------------ SwiGLU
 __global__ void swiglu_vec_kernel(const __half* __restrict__ g, int64_t ldg, const __half* __restrict__ u,
                                   int64_t ldu, __half* __restrict__ h, int64_t ldh, int rows, int cols) {
@@ -218,6 +292,92 @@ __global__ void __launch_bounds__(NT) softmax_kernel(const __half* s, __half* p,
             for (int i = 0; i < 8; ++i) o[i] = (e0 < valid) ? v[c][i] * inv : 0.0f;
             if (e0 + 8 <= zend) {
                 *reinterpret_cast<uint4*>(pr + e0) = pack8(o);
+            } else {
+                for (int i = 0; i < 8 && e0 + i < zend; ++i) pr[e0 + i] = __float2half_rn(o[i]);
+            }
+        }
+    }
+}
+
+// One warp per row for rows of up to 32 x 8 x CPL columns (2048: 8 16-byte
+// chunks per lane).  Only the unmasked chunks are read (streaming loads); the
+// row is kept packed in registers through the max, sum and scale passes, the
+// exponentials are recomputed in the last pass with the hardware ex2
+// (MUFU.EX2, ~2 ulp of fp32, far below the fp16 output; the fused attention
+// kernel uses the same instruction) rather than held as fp32, and the masked
+// part up to `zend` is written as zeros with streaming stores.  Measured at
+// 32 x 2048 x 2048 causal: 74.6 us (0.83 of the copy bandwidth for the 403 MB
+// moved) against 95 us with exp2f and 134 us for softmax_kernel.
+template <int CPL>
+__global__ void __launch_bounds__(256) softmax_warp_kernel(const __half* s, __half* p, int64_t ld, int64_t bstride,
+                                                         int rows, int nrows_total, int cols, float scale, int off,
+                                                         int zero_full) {
+    const int lane = threadIdx.x & 31;
+    const int gr = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (gr >= nrows_total) return;
+    const int rr = gr % rows, b = gr / rows;
+    const __half* sr = s + (int64_t)b * bstride + (int64_t)rr * ld;
+    __half* pr = p + (int64_t)b * bstride + (int64_t)rr * ld;
+    int valid = cols, zend = cols;
+    if (off >= 0) {
+        valid = min(cols, rr + off + 1);
+        if (!zero_full) {
+            const int a0 = (rr / 128) * 128;
+            zend = min(cols, ((a0 + 128 + off + 63) / 64) * 64);
+        }
+    }
+    const float sc = scale * 1.4426950408889634f;  // exp(x) = exp2(x log2 e)
+    uint4 v[CPL];
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+        const int e0 = (lane + 32 * j) * kVec;
+        if (e0 < valid) v[j] = __ldcs(reinterpret_cast<const uint4*>(sr + e0));
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+        const int e0 = (lane + 32 * j) * kVec;
+        if (e0 < valid) {
+            float a[8];
+            unpack8(v[j], a);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (e0 + i < valid) mx = fmaxf(mx, a[i] * sc);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+        const int e0 = (lane + 32 * j) * kVec;
+        if (e0 < valid) {
+            float a[8];
+            unpack8(v[j], a);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (e0 + i < valid) sum += ex2_approx(a[i] * sc - mx);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float inv = 1.0f / sum;
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+        const int e0 = (lane + 32 * j) * kVec;
+        if (e0 < zend) {
+            float o[8];
+            if (e0 < valid) {
+                float a[8];
+                unpack8(v[j], a);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) o[i] = (e0 + i < valid) ? ex2_approx(a[i] * sc - mx) * inv : 0.0f;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) o[i] = 0.0f;
+            }
+            if (e0 + 8 <= zend) {
+                __stcs(reinterpret_cast<uint4*>(pr + e0), pack8(o));
             } else {
                 for (int i = 0; i < 8 && e0 + i < zend; ++i) pr[e0 + i] = __float2half_rn(o[i]);
             }
@@ -483,6 +643,13 @@ extern "C" int npub_rmsnorm(const void* x, int64_t ldx, const void* residual, in
     const __half* gh = reinterpret_cast<const __half*>(gamma);
     __half* yh = reinterpret_cast<__half*>(y);
     const int nch = d / kVec;
+#define NPUB_RMSW(C) launch_pdl(rmsnorm_warp_kernel<C>, dim3((rows + 1) / 2), dim3(64), 0, st, xh, ldx, rh, ldr, xoh, \
+                                ldxo, gh, yh, ldy, rows, d, eps)
+    if (nch <= 64) return NPUB_RMSW(2);
+    if (nch <= 128) return NPUB_RMSW(4);
+    if (nch <= 256) return NPUB_RMSW(8);
+    if (nch <= 512) return NPUB_RMSW(16);
+#undef NPUB_RMSW
 #define NPUB_RMS(NT, V) launch_pdl(rmsnorm_kernel<NT, V>, dim3(rows), dim3(NT), 0, st, xh, ldx, rh, ldr, xoh, ldxo, gh, \
                                    yh, ldy, d, eps)
     if (nch <= 128) return NPUB_RMS(128, 1);
@@ -529,6 +696,18 @@ extern "C" int npub_softmax_rows(const void* s, void* p, int64_t ld, int64_t bat
     const __half* sh = reinterpret_cast<const __half*>(s);
     __half* ph = reinterpret_cast<__half*>(p);
     const int nch = (cols + kVec - 1) / kVec;
+    if (cols % kVec == 0 && nch <= 512) {
+        const dim3 grid((unsigned)((nb + 7) / 8));
+#define NPUB_SMW(C) softmax_warp_kernel<C><<<grid, 256, 0, st>>>(sh, ph, ld, batch_stride, rows, nb, cols, scale, \
+                                                                  causal_offset, zero_full)
+        if (nch <= 32) NPUB_SMW(1);
+        else if (nch <= 64) NPUB_SMW(2);
+        else if (nch <= 128) NPUB_SMW(4);
+        else if (nch <= 256) NPUB_SMW(8);
+        else NPUB_SMW(16);
+#undef NPUB_SMW
+        return npub_internal_launch_status();
+    }
     if (nch <= 128)
         softmax_kernel<128, 1><<<nb, 128, 0, st>>>(sh, ph, ld, batch_stride, rows, cols, scale, causal_offset, zero_full);
     else if (nch <= 256)

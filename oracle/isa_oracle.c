@@ -85,9 +85,39 @@ static inline int32_t to_i32(float a) {
     return (int32_t)a;
 }
 
-static inline float hw_act(float x) { /* x^2 * sigmoid(x), evaluated as (x*x)*s */
-    float s = 1.0f / (1.0f + expf(-x));
-    return x * x * s;
+/* SSE NaN results, whatever operand order this compiler picks for a
+ * commutative operation: a NaN operand comes back made quiet; an invalid
+ * operation on non-NaN operands gives the indefinite NaN 0xFFC00000.  When
+ * both operands are NaN, the one the reference simulator's compiled code
+ * keeps in the destination register wins (measured against it): the left
+ * operand of a op b, the product in mul-add, the running sum in the matmul,
+ * and in the activation the sigmoid after a matmul, x * x after an
+ * elementwise matrix op. */
+static inline float quietf(float x) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    u |= 0x00400000u;
+    memcpy(&x, &u, 4);
+    return x;
+}
+static inline float sse2(float r, float x, float y) {
+    if (r == r) return r;
+    if (x != x) return quietf(x);
+    if (y != y) return quietf(y);
+    uint32_t u = 0xFFC00000u;
+    memcpy(&r, &u, 4);
+    return r;
+}
+static inline float f_add(float x, float y) { return sse2(x + y, x, y); }
+static inline float f_sub(float x, float y) { return sse2(x - y, x, y); }
+static inline float f_mul(float x, float y) { return sse2(x * y, x, y); }
+static inline float f_div(float x, float y) { return sse2(x / y, x, y); }
+
+static inline float hw_act(float x, int sigmoid_first) { /* x^2 * sigmoid(x) (mysim.cpp:39-40) */
+    float e = expf(-x);
+    float s = f_div(1.0f, f_add(1.0f, e));
+    float xx = f_mul(x, x);
+    return sigmoid_first ? f_mul(s, xx) : f_mul(xx, s);
 }
 
 /* --------------------------------------------------------------- buffers */
@@ -200,11 +230,11 @@ static float elem_op(uint32_t w, float a, float b, float prev) {
     int cst = (int)((w >> 8) & 0xFFFFu);
     float r = a;
     switch (op) {
-        case 0x01: case 0x40: r = a + b; break;
-        case 0x02: case 0x41: r = a - b; break;
-        case 0x0A: case 0x42: r = a * b; break;
-        case 0x0B: r = a / b; break;
-        case 0x0C: { float p = a * b; r = prev + p; } break;
+        case 0x01: case 0x40: r = f_add(a, b); break;
+        case 0x02: case 0x41: r = f_sub(a, b); break;
+        case 0x0A: case 0x42: r = f_mul(a, b); break;
+        case 0x0B: r = f_div(a, b); break;
+        case 0x0C: r = f_add(f_mul(a, b), prev); break;
         case 0x0D: case 0x43: r = b; break;
         case 0x0E: r = sqrtf(a); break;
         case 0x0F: r = expf(a); break;
@@ -214,7 +244,7 @@ static float elem_op(uint32_t w, float a, float b, float prev) {
         case 0x09: {
             int16_t s = (int16_t)cst;
             if (mode == 2) s = (int16_t)to_i32(b);
-            r = a * ldexpf(1.0f, (int)s);
+            r = f_mul(a, ldexpf(1.0f, (int)s));
         } break;
         case 0x08: {
             int64_t ia = to_i64(a), ib = to_i64(b);
@@ -230,7 +260,7 @@ static float elem_op(uint32_t w, float a, float b, float prev) {
         } break;
         default: break;
     }
-    if (actf && matrix) r = hw_act(r);
+    if (actf && matrix) r = hw_act(r, 0);
     return r;
 }
 
@@ -310,8 +340,8 @@ long ora_exec(void* h, const uint32_t* prog, long nprog, long maxrun, int trace,
                 for (long i = 0; i < rA; i++)
                     for (long j = 0; j < cB; j++) {
                         float acc = 0.0f;
-                        for (long k = 0; k < cA; k++) acc += st->in1.v[i * cA + k] * st->in2.v[k * cB + j];
-                        st->out.v[i * cB + j] = actf ? hw_act(acc) : acc;
+                        for (long k = 0; k < cA; k++) acc = f_add(acc, f_mul(st->in1.v[i * cA + k], st->in2.v[k * cB + j]));
+                        st->out.v[i * cB + j] = actf ? hw_act(acc, 1) : acc;
                     }
             } else {
                 long n = matrix ? st->tA[0] * st->tB[0] : st->vlen;

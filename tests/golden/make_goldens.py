@@ -23,6 +23,10 @@ temporary directory) and records only their outputs:
                      and llama_layer.py, run as-is (on a copy, with mysim
                      built from _poc/mysim.cpp): the G-buffer results of the
                      NPU programs and the scripts' own python references.
+  programs.npz       every program the example scripts hand to run(): the
+                     program words and the initial G-buffer exactly as run()
+                     wrote them, its gn / maxrun, and the simulator's
+                     write-back (gout.bin) -- for the GPU program executor.
   w8a16_config1.npz  the single W8A16 matmul configuration (A [64,512] ~N(0,1),
                      W [512,512] ~N(0,0.02), numpy default_rng(0)) run through
                      the compiler-style 64-tiled program on the reference
@@ -104,12 +108,37 @@ def isa_goldens(refdir):
     return out
 
 
-def run_script(refdir, script, workdir):
-    """Run a reference example script as-is in a copy of its directory; return its globals."""
+_CAPTURE = """#!{python}
+# Runs the reference simulator with the arguments run() gave, then keeps the
+# program, the input G-buffer, the write-back and the arguments of the call.
+import json, os, shutil, subprocess, sys
+r = subprocess.run([{mysim!r}] + sys.argv[1:], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+d = os.path.join({cap!r}, "%03d" % len(os.listdir({cap!r})))
+os.makedirs(d)
+for f in ("program_memory.bin", "G_buffer_data.bin"):
+    shutil.copy(f, d)
+a = sys.argv[1:]
+gout = a[a.index("--gout") + 1]
+shutil.copy(gout, os.path.join(d, "gout.bin"))
+json.dump(a, open(os.path.join(d, "args.json"), "w"))
+sys.exit(r.returncode)
+"""
+
+
+def run_script(refdir, script, workdir, capture=None):
+    """Run a reference example script as-is in a copy of its directory; return its
+    globals.  With `capture` (a directory), every run() of the script leaves its
+    program_memory.bin, G_buffer_data.bin, gout.bin and arguments there."""
     sdir = os.path.join(refdir, "b_program_examples")
     for f in ("npu.py", script):
         shutil.copy(os.path.join(sdir, f), workdir)
-    shutil.copy(cmodel.MYSIM, os.path.join(workdir, "mysim"))
+    if capture is None:
+        shutil.copy(cmodel.MYSIM, os.path.join(workdir, "mysim"))
+    else:
+        os.makedirs(capture, exist_ok=True)
+        with open(os.path.join(workdir, "mysim"), "w") as f:
+            f.write(_CAPTURE.format(python=sys.executable, mysim=os.path.abspath(cmodel.MYSIM), cap=capture))
+        os.chmod(os.path.join(workdir, "mysim"), 0o755)
     cwd = os.getcwd()
     sys.path.insert(0, workdir)
     try:
@@ -175,6 +204,33 @@ def examples(refdir):
     return res
 
 
+EXAMPLE_SCRIPTS = ("test_matmul.py", "test_rmsnorm.py", "test_swiglu.py", "test_attention.py", "llama_layer.py")
+
+
+def programs(refdir):
+    """The programs the reference's example scripts build and hand to run(),
+    as run() wrote them (program words, initial G-buffer), with the arguments
+    and the simulator's write-back: arrays <script>_<i>_{words,gin,gout,gn,maxrun}."""
+    res = {}
+    for script in EXAMPLE_SCRIPTS:
+        name = script[:-3]
+        with tempfile.TemporaryDirectory() as d, tempfile.TemporaryDirectory() as cap:
+            run_script(refdir, script, d, capture=cap)
+            for i, sub in enumerate(sorted(os.listdir(cap))):
+                c = os.path.join(cap, sub)
+                args = json.load(open(os.path.join(c, "args.json")))
+                praw = open(os.path.join(c, "program_memory.bin"), "rb").read()
+                graw = open(os.path.join(c, "G_buffer_data.bin"), "rb").read()
+                oraw = open(os.path.join(c, "gout.bin"), "rb").read()
+                k = f"{name}_{i}"
+                res[k + "_words"] = np.frombuffer(praw[: len(praw) // 4 * 4], dtype="<u4").astype(np.uint32)
+                res[k + "_gin"] = np.frombuffer(graw[: len(graw) // 2 * 2], dtype="<f2").astype(np.float16)
+                res[k + "_gout"] = np.frombuffer(oraw[: len(oraw) // 2 * 2], dtype="<f2").astype(np.float16)
+                res[k + "_gn"] = np.int64(args[args.index("--gn") + 1])
+                res[k + "_maxrun"] = np.int64(args[args.index("--run") + 1])
+    return res
+
+
 def config1():
     rng = np.random.default_rng(0)
     A = rng.standard_normal((64, 512)).astype(np.float16)
@@ -190,10 +246,16 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("NPU_COMP_REF"),
                     help="root of the reference checkout (default: $NPU_COMP_REF)")
+    ap.add_argument("--only", choices=["programs"], default=None, help="regenerate one fixture file only")
     a = ap.parse_args()
     if not a.ref:
         ap.error("the reference root is required: --ref <dir> or NPU_COMP_REF=<dir>")
     subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={a.ref}"], check=True)
+    progs = programs(a.ref)
+    np.savez_compressed(os.path.join(HERE, "programs.npz"), **progs)
+    if a.only == "programs":
+        print(f"wrote programs.npz ({len(progs) // 5} program runs)")
+        return
     gold = isa_goldens(a.ref)
     with open(os.path.join(HERE, "isa_goldens.json"), "w") as f:
         json.dump({"gbuf": "ramp G[i] = fp16(i), i < 8192 (c_hex_data/w_support_binary_data_gen.cpp)",
