@@ -234,6 +234,27 @@ int npub_rope_kv_store(void* qkv, int64_t ldx, int tokens, int tokens_per_seq, i
                        int head_dim, const int32_t* positions, float theta, void* k_cache, void* v_cache, int64_t cap,
                        void* stream);
 
+/* RoPE with a frequency table instead of theta (the Llama-3.2 layer of
+ * d_compiler/npu_compiler/model.py:20-21: base 500000 with the frequency
+ * scaling of legalize.py:50-64, rope_tables(..., llama3_scaling=True) at
+ * legalize.py:67-76).  inv_freq: device fp32 [head_dim/2], frequency i of every
+ * head; angle = p * inv_freq[i].  Otherwise as npub_rope, npub_rope_kv_append
+ * and npub_rope_kv_store. */
+int npub_rope_freqs(void* x, int64_t ldx, int tokens, int heads, int head_dim, const int32_t* positions, int pos0,
+                    const float* inv_freq, void* stream);
+int npub_rope_kv_append_freqs(void* qkv, int64_t ldx, int tokens, int q_heads, int kv_heads, int head_dim,
+                              const int32_t* positions, const float* inv_freq, void* k_cache, void* v_cache,
+                              int64_t cap, int32_t* lens, void* stream);
+int npub_rope_kv_store_freqs(void* qkv, int64_t ldx, int tokens, int tokens_per_seq, int q_heads, int kv_heads,
+                             int head_dim, const int32_t* positions, const float* inv_freq, void* k_cache,
+                             void* v_cache, int64_t cap, void* stream);
+/* The table itself, on the host (out: float [head_dim/2]): theta^(-2i/head_dim),
+ * scaled as legalize.py:50-64 (_llama3_scale_freqs: factor, low, high,
+ * old_ctx = 32, 1, 4, 8192 there) when factor > 0; factor <= 0 gives the
+ * unscaled table.  Computed in double precision, rounded to float. */
+int npub_rope_llama3_freqs(float* out, int head_dim, double theta, double factor, double low, double high,
+                           double old_ctx);
+
 /* ------------------------------------------------- NPU ISA semantics ----
  * One compute instruction of the NPU over PE buffers (_poc/mysim.cpp:114-141):
  * `word` is the 32-bit instruction (opcodes 0x01-0x13 vector, 0x40-0x43

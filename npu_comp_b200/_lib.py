@@ -57,6 +57,11 @@ SIGNATURES = {
     "npub_kv_append": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _p, _i, _i, _i, _i, _p]),
     "npub_rope_kv_append": (_i, [_p, _i64, _i, _i, _i, _i, _p, _f, _p, _p, _i64, _p, _p]),
     "npub_rope_kv_store": (_i, [_p, _i64, _i, _i, _i, _i, _i, _p, _f, _p, _p, _i64, _p]),
+    "npub_rope_freqs": (_i, [_p, _i64, _i, _i, _i, _p, _i, _p, _p]),
+    "npub_rope_kv_append_freqs": (_i, [_p, _i64, _i, _i, _i, _i, _p, _p, _p, _p, _i64, _p, _p]),
+    "npub_rope_kv_store_freqs": (_i, [_p, _i64, _i, _i, _i, _i, _i, _p, _p, _p, _p, _i64, _p]),
+    "npub_rope_llama3_freqs": (_i, [_p, _i, ctypes.c_double, ctypes.c_double, ctypes.c_double, ctypes.c_double,
+                                    ctypes.c_double]),
     "npub_isa_vector": (_i, [_u32, _p, _p, _p, _p, _i64, _p]),
     "npub_f32_to_f16": (_i, [_p, _p, _i64, _p]),
     "npub_f16_to_f32": (_i, [_p, _p, _i64, _p]),

@@ -4,6 +4,8 @@
 // with warp-shuffle reductions.
 #include "common.cuh"
 
+#include <cmath>
+
 #include <math.h>
 
 namespace npub {
@@ -386,8 +388,14 @@ __global__ void __launch_bounds__(256) softmax_warp_kernel(const __half* s, __ha
 }
 
 // ------------------------------------------------------------ RoPE
+// Frequency i of a head: theta^(-2i/hd), or inv_freq[i] when a table is given
+// (Llama-3 scaled frequencies, legalize.py:50-64).
+__device__ __forceinline__ float rope_freq(int k, int hd, float log2_theta, const float* __restrict__ inv_freq) {
+    return inv_freq ? __ldg(inv_freq + k) : exp2f(-(2.0f * (float)k / (float)hd) * log2_theta);
+}
+
 __global__ void rope_kernel(__half* x, int64_t ldx, int tokens, int heads, int hd, const int32_t* __restrict__ pos,
-                            int pos0, float log2_theta) {
+                            int pos0, float log2_theta, const float* __restrict__ inv_freq) {
     const int half = hd / 2;
     const int64_t total = (int64_t)tokens * heads * half;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -395,9 +403,8 @@ __global__ void rope_kernel(__half* x, int64_t ldx, int tokens, int heads, int h
         const int64_t th = i / half;
         const int h = (int)(th % heads), t = (int)(th / heads);
         const int p = pos ? pos[t] : pos0 + t;
-        const float inv_freq = exp2f(-(2.0f * (float)k / (float)hd) * log2_theta);
         float sn, cs;
-        sincosf((float)p * inv_freq, &sn, &cs);
+        sincosf((float)p * rope_freq(k, hd, log2_theta, inv_freq), &sn, &cs);
         __half* row = x + (int64_t)t * ldx + (int64_t)h * hd;
         const float x1 = __half2float(row[k]), x2 = __half2float(row[k + half]);
         row[k] = __float2half_rn(x1 * cs - x2 * sn);
@@ -409,7 +416,7 @@ __global__ void rope_kernel(__half* x, int64_t ldx, int tokens, int heads, int h
 // frequencies are computed once into shared memory, then every head's pairs
 // (x[i], x[i + hd/2]) are rotated 8 at a time with 128-bit accesses.
 __global__ void rope_vec_kernel(__half* x, int64_t ldx, int heads, int hd, const int32_t* __restrict__ pos, int pos0,
-                                float log2_theta) {
+                                float log2_theta, const float* __restrict__ inv_freq) {
     pdl_trigger();
     pdl_wait();
     __shared__ float cs[256], sn[256];
@@ -417,9 +424,8 @@ __global__ void rope_vec_kernel(__half* x, int64_t ldx, int heads, int hd, const
     const int half = hd / 2;
     const int p = pos ? pos[t] : pos0 + t;
     for (int k = threadIdx.x; k < half; k += blockDim.x) {
-        const float inv_freq = exp2f(-(2.0f * (float)k / (float)hd) * log2_theta);
         float sv, cv;
-        sincosf((float)p * inv_freq, &sv, &cv);
+        sincosf((float)p * rope_freq(k, hd, log2_theta, inv_freq), &sv, &cv);
         cs[k] = cv;
         sn[k] = sv;
     }
@@ -452,7 +458,8 @@ __global__ void rope_vec_kernel(__half* x, int64_t ldx, int heads, int hd, const
 // takes heads [hpb * y, hpb * y + hpb).  A position outside [0, cap) is
 // rotated but not stored.
 __global__ void rope_kv_append_kernel(__half* x, int64_t ldx, int hq, int hk, int hd, int tps, int hpb,
-                                      const int32_t* __restrict__ pos, float log2_theta, __half* __restrict__ kc,
+                                      const int32_t* __restrict__ pos, float log2_theta,
+                                      const float* __restrict__ inv_freq, __half* __restrict__ kc,
                                       __half* __restrict__ vc, int64_t cap, int32_t* __restrict__ lens) {
     pdl_trigger();
     pdl_wait();
@@ -462,9 +469,8 @@ __global__ void rope_kv_append_kernel(__half* x, int64_t ldx, int hq, int hk, in
     const int p = pos[t];
     if (lens && blockIdx.y == 0 && threadIdx.x == 0) lens[t] = p + 1;
     for (int k = threadIdx.x; k < half; k += blockDim.x) {
-        const float inv_freq = exp2f(-(2.0f * (float)k / (float)hd) * log2_theta);
         float sv, cv;
-        sincosf((float)p * inv_freq, &sv, &cv);
+        sincosf((float)p * rope_freq(k, hd, log2_theta, inv_freq), &sv, &cv);
         cs[k] = cv;
         sn[k] = sv;
     }
@@ -721,28 +727,42 @@ extern "C" int npub_softmax_rows(const void* s, void* p, int64_t ld, int64_t bat
     return npub_internal_launch_status();
 }
 
-extern "C" int npub_rope(void* x, int64_t ldx, int tokens, int heads, int head_dim, const int32_t* positions, int pos0,
-                         float theta, void* stream) {
+static int rope_impl(void* x, int64_t ldx, int tokens, int heads, int head_dim, const int32_t* positions, int pos0,
+                     float theta, const float* inv_freq, void* stream) {
     NPUB_CHECK_ARG(tokens >= 0 && heads >= 0);
     if (tokens == 0 || heads == 0) return NPUB_OK;
-    NPUB_CHECK_ARG(x && head_dim > 0 && head_dim % 2 == 0 && ldx >= (int64_t)heads * head_dim && theta > 0.0f);
+    NPUB_CHECK_ARG(x && head_dim > 0 && head_dim % 2 == 0 && ldx >= (int64_t)heads * head_dim);
+    NPUB_CHECK_ARG(inv_freq ? npub_aligned(inv_freq, 4) : theta > 0.0f);
+    const float l2t = inv_freq ? 0.0f : log2f(theta);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (head_dim % 16 == 0 && head_dim <= 512 && ldx % 8 == 0 && npub_aligned(x, 16)) {
         return launch_pdl(rope_vec_kernel, dim3(tokens), dim3(128), 0, st, reinterpret_cast<__half*>(x), ldx, heads,
-                          head_dim, positions, pos0, log2f(theta));
+                          head_dim, positions, pos0, l2t, inv_freq);
     }
     const int64_t work = (int64_t)tokens * heads * (head_dim / 2);
     rope_kernel<<<grid_for(work, 256), 256, 0, st>>>(reinterpret_cast<__half*>(x), ldx, tokens, heads, head_dim,
-                                                      positions, pos0, log2f(theta));
+                                                      positions, pos0, l2t, inv_freq);
     return npub_internal_launch_status();
 }
 
-extern "C" int npub_rope_kv_append(void* qkv, int64_t ldx, int tokens, int q_heads, int kv_heads, int head_dim,
-                                   const int32_t* positions, float theta, void* k_cache, void* v_cache, int64_t cap,
-                                   int32_t* lens, void* stream) {
+extern "C" int npub_rope(void* x, int64_t ldx, int tokens, int heads, int head_dim, const int32_t* positions, int pos0,
+                         float theta, void* stream) {
+    return rope_impl(x, ldx, tokens, heads, head_dim, positions, pos0, theta, nullptr, stream);
+}
+
+extern "C" int npub_rope_freqs(void* x, int64_t ldx, int tokens, int heads, int head_dim, const int32_t* positions,
+                               int pos0, const float* inv_freq, void* stream) {
+    NPUB_CHECK_ARG(inv_freq);
+    return rope_impl(x, ldx, tokens, heads, head_dim, positions, pos0, 0.0f, inv_freq, stream);
+}
+
+static int rope_kv_append_impl(void* qkv, int64_t ldx, int tokens, int q_heads, int kv_heads, int head_dim,
+                               const int32_t* positions, float theta, const float* inv_freq, void* k_cache,
+                               void* v_cache, int64_t cap, int32_t* lens, void* stream) {
     NPUB_CHECK_ARG(tokens >= 0 && q_heads >= 0 && kv_heads >= 0);
     if (tokens == 0) return NPUB_OK;
-    NPUB_CHECK_ARG(qkv && positions && k_cache && v_cache && theta > 0.0f && cap > 0);
+    NPUB_CHECK_ARG(qkv && positions && k_cache && v_cache && cap > 0);
+    NPUB_CHECK_ARG(inv_freq ? npub_aligned(inv_freq, 4) : theta > 0.0f);
     NPUB_CHECK_ARG(head_dim % 16 == 0 && head_dim > 0 && head_dim <= 512);
     NPUB_CHECK_ARG(ldx >= (int64_t)(q_heads + 2 * kv_heads) * head_dim && ldx % 8 == 0);
     NPUB_CHECK_ARG(npub_aligned(qkv, 16) && npub_aligned(k_cache, 16) && npub_aligned(v_cache, 16));
@@ -750,17 +770,33 @@ extern "C" int npub_rope_kv_append(void* qkv, int64_t ldx, int tokens, int q_hea
     if (groups == 0) return NPUB_OK;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     return launch_pdl(rope_kv_append_kernel, dim3(tokens, groups), dim3(64), 0, st, reinterpret_cast<__half*>(qkv),
-                      ldx, q_heads, kv_heads, head_dim, 1, 8, positions, log2f(theta),
+                      ldx, q_heads, kv_heads, head_dim, 1, 8, positions, inv_freq ? 0.0f : log2f(theta), inv_freq,
                       reinterpret_cast<__half*>(k_cache), reinterpret_cast<__half*>(v_cache), cap, lens);
 }
 
-extern "C" int npub_rope_kv_store(void* qkv, int64_t ldx, int tokens, int tokens_per_seq, int q_heads, int kv_heads,
-                                  int head_dim, const int32_t* positions, float theta, void* k_cache, void* v_cache,
-                                  int64_t cap, void* stream) {
+extern "C" int npub_rope_kv_append(void* qkv, int64_t ldx, int tokens, int q_heads, int kv_heads, int head_dim,
+                                   const int32_t* positions, float theta, void* k_cache, void* v_cache, int64_t cap,
+                                   int32_t* lens, void* stream) {
+    return rope_kv_append_impl(qkv, ldx, tokens, q_heads, kv_heads, head_dim, positions, theta, nullptr, k_cache,
+                               v_cache, cap, lens, stream);
+}
+
+extern "C" int npub_rope_kv_append_freqs(void* qkv, int64_t ldx, int tokens, int q_heads, int kv_heads, int head_dim,
+                                         const int32_t* positions, const float* inv_freq, void* k_cache,
+                                         void* v_cache, int64_t cap, int32_t* lens, void* stream) {
+    NPUB_CHECK_ARG(inv_freq);
+    return rope_kv_append_impl(qkv, ldx, tokens, q_heads, kv_heads, head_dim, positions, 0.0f, inv_freq, k_cache,
+                               v_cache, cap, lens, stream);
+}
+
+static int rope_kv_store_impl(void* qkv, int64_t ldx, int tokens, int tokens_per_seq, int q_heads, int kv_heads,
+                              int head_dim, const int32_t* positions, float theta, const float* inv_freq,
+                              void* k_cache, void* v_cache, int64_t cap, void* stream) {
     NPUB_CHECK_ARG(tokens >= 0 && q_heads >= 0 && kv_heads >= 0);
     if (tokens == 0) return NPUB_OK;
     NPUB_CHECK_ARG(tokens_per_seq > 0 && tokens % tokens_per_seq == 0);
-    NPUB_CHECK_ARG(qkv && positions && k_cache && v_cache && theta > 0.0f && cap > 0);
+    NPUB_CHECK_ARG(qkv && positions && k_cache && v_cache && cap > 0);
+    NPUB_CHECK_ARG(inv_freq ? npub_aligned(inv_freq, 4) : theta > 0.0f);
     NPUB_CHECK_ARG(head_dim % 16 == 0 && head_dim > 0 && head_dim <= 512);
     NPUB_CHECK_ARG(ldx >= (int64_t)(q_heads + 2 * kv_heads) * head_dim && ldx % 8 == 0);
     NPUB_CHECK_ARG(npub_aligned(qkv, 16) && npub_aligned(k_cache, 16) && npub_aligned(v_cache, 16));
@@ -772,8 +808,50 @@ extern "C" int npub_rope_kv_store(void* qkv, int64_t ldx, int tokens, int tokens
     NPUB_CHECK_ARG(groups <= 65535);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     return launch_pdl(rope_kv_append_kernel, dim3(tokens, groups), dim3(256), 0, st, reinterpret_cast<__half*>(qkv),
-                      ldx, q_heads, kv_heads, head_dim, tokens_per_seq, hpb, positions, log2f(theta),
-                      reinterpret_cast<__half*>(k_cache), reinterpret_cast<__half*>(v_cache), cap, nullptr);
+                      ldx, q_heads, kv_heads, head_dim, tokens_per_seq, hpb, positions,
+                      inv_freq ? 0.0f : log2f(theta), inv_freq, reinterpret_cast<__half*>(k_cache),
+                      reinterpret_cast<__half*>(v_cache), cap, nullptr);
+}
+
+extern "C" int npub_rope_kv_store(void* qkv, int64_t ldx, int tokens, int tokens_per_seq, int q_heads, int kv_heads,
+                                  int head_dim, const int32_t* positions, float theta, void* k_cache, void* v_cache,
+                                  int64_t cap, void* stream) {
+    return rope_kv_store_impl(qkv, ldx, tokens, tokens_per_seq, q_heads, kv_heads, head_dim, positions, theta, nullptr,
+                              k_cache, v_cache, cap, stream);
+}
+
+extern "C" int npub_rope_kv_store_freqs(void* qkv, int64_t ldx, int tokens, int tokens_per_seq, int q_heads,
+                                        int kv_heads, int head_dim, const int32_t* positions, const float* inv_freq,
+                                        void* k_cache, void* v_cache, int64_t cap, void* stream) {
+    NPUB_CHECK_ARG(inv_freq);
+    return rope_kv_store_impl(qkv, ldx, tokens, tokens_per_seq, q_heads, kv_heads, head_dim, positions, 0.0f,
+                              inv_freq, k_cache, v_cache, cap, stream);
+}
+
+// Host-side table of the per-frequency rates: theta^(-2i/hd) for i < hd/2,
+// with the Llama-3 scaling of legalize.py:50-64 when factor > 0 (wavelengths
+// above old_ctx/low divided by factor, below old_ctx/high kept, a smooth blend
+// between), computed in double precision like the reference's numpy tables.
+extern "C" int npub_rope_llama3_freqs(float* out, int head_dim, double theta, double factor, double low, double high,
+                                      double old_ctx) {
+    NPUB_CHECK_ARG(out && head_dim > 0 && head_dim % 2 == 0 && theta > 0.0);
+    NPUB_CHECK_ARG(factor <= 0.0 || (high > low && low > 0.0 && old_ctx > 0.0));
+    const double pi = 3.14159265358979323846;
+    for (int i = 0; i < head_dim / 2; ++i) {
+        const double f = std::pow(theta, -2.0 * i / head_dim);
+        double r = f;
+        if (factor > 0.0) {
+            const double wl = 2.0 * pi / f;
+            if (wl > old_ctx / low) {
+                r = f / factor;
+            } else if (wl >= old_ctx / high) {
+                const double sm = (old_ctx / wl - low) / (high - low);
+                r = (1.0 - sm) * f / factor + sm * f;
+            }
+        }
+        out[i] = (float)r;
+    }
+    return NPUB_OK;
 }
 
 extern "C" int npub_quantize_w8(const float* W, int64_t ldw, int K, int N, int8_t* Wq, int64_t ldq, void* scale,

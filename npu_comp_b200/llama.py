@@ -20,7 +20,7 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass, field
-from typing import Dict, List, Optional
+from typing import Dict, List, Optional, Tuple
 
 import torch
 
@@ -38,6 +38,9 @@ class LlamaConfig:
     theta: float = 10000.0
     vocab: int = 32000
     layers: int = 32
+    # Llama-3 RoPE frequency scaling (legalize.py:50-64): (factor, low, high,
+    # original context), or None for theta^(-2i/hd) alone
+    rope_scaling: Optional[Tuple[float, float, float, float]] = None
 
     @property
     def q_dim(self) -> int:
@@ -58,6 +61,31 @@ LLAMA_7B = LlamaConfig()
 # The reference's reduced layer (llama_layer.py:11-17): SEQ 8, D 64, 4 q heads,
 # 2 kv heads, head_dim 16, FFN 128, eps 0.
 REDUCED = LlamaConfig(d=64, heads=4, kv_heads=2, head_dim=16, ffn=128, eps=0.0, theta=10000.0, vocab=256, layers=1)
+# The reference's all-64-multiple layer (model.py:23-25): D 64, one head of 64, FFN 64.
+MEDIUM = LlamaConfig(d=64, heads=1, kv_heads=1, head_dim=64, ffn=64, eps=1e-5, theta=10000.0, vocab=256, layers=1)
+# The real Llama 3.2 3B layer of the reference (model.py:20-21): D 3072, 24 q /
+# 8 kv heads of 128, FFN 8192, RoPE base 500000 with the Llama-3 scaling
+# (legalize.py:50-64: factor 32, low 1, high 4, original context 8192); the
+# 3B model's 28 layers and 128256-token vocabulary for the stack.
+LLAMA_3_2_3B = LlamaConfig(d=3072, heads=24, kv_heads=8, head_dim=128, ffn=8192, eps=1e-5, theta=500000.0,
+                           vocab=128256, layers=28, rope_scaling=(32.0, 1.0, 4.0, 8192.0))
+
+_FREQS: Dict[tuple, torch.Tensor] = {}
+
+
+def rope_inv_freq(cfg: LlamaConfig, device) -> Optional[torch.Tensor]:
+    """The frequency table of a config with Llama-3 RoPE scaling (fp32 CUDA
+    [head_dim/2], cached per device), None for plain theta frequencies.  Made
+    on first use: call it (or run a prefill) before capturing a CUDA graph."""
+    if cfg.rope_scaling is None:
+        return None
+    dev = torch.device(device)
+    key = (cfg.head_dim, cfg.theta, tuple(cfg.rope_scaling), dev.type, dev.index)
+    t = _FREQS.get(key)
+    if t is None:
+        t = npu.rope_freqs(cfg.head_dim, cfg.theta, llama3_scaling=tuple(cfg.rope_scaling), device=dev)
+        _FREQS[key] = t
+    return t
 
 
 @dataclass
@@ -272,9 +300,10 @@ def layer_prefill(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, *, batch: 
     mk("rope")
     if kv_out is not None:
         # q, k rotated in place and the prompt's K, V stored into the caches, one kernel
-        npu.rope_kv_store(qkv, hq, hk, hd, positions, kv_out[0], kv_out[1], tokens_per_seq=T, theta=cfg.theta)
-    else:
-        npu.rope(qkv, hq + hk, hd, positions=positions, theta=cfg.theta)  # q and k heads are adjacent columns
+        npu.rope_kv_store(qkv, hq, hk, hd, positions, kv_out[0], kv_out[1], tokens_per_seq=T, theta=cfg.theta,
+                          inv_freq=rope_inv_freq(cfg, dev))
+    else:  # q and k heads are adjacent columns
+        npu.rope(qkv, hq + hk, hd, positions=positions, theta=cfg.theta, inv_freq=rope_inv_freq(cfg, dev))
     mk("attention")
     ctx = npu.attention(q, k, v, hq, hk, head_dim=hd, batch=batch, causal=True,
                         out=sc.get("ctx", (BT, hq * hd), device=dev))
@@ -348,7 +377,8 @@ def layer_decode(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, k_cache: to
     q = qkv[:, : hq * hd]
     mk("rope_kv_append")
     lens = sc.get("dlens", (B,), dtype=torch.int32, device=dev)
-    npu.rope_kv_append(qkv, hq, hk, hd, pos, k_cache, v_cache, theta=cfg.theta, lens=lens)
+    npu.rope_kv_append(qkv, hq, hk, hd, pos, k_cache, v_cache, theta=cfg.theta, lens=lens,
+                       inv_freq=rope_inv_freq(cfg, dev))
     mk("attention")
     ctx = npu.attention_decode(q, k_cache, v_cache, heads=hq, kv_heads=hk, lens=lens, ctx_len=ctx_max,
                                out=sc.get("dctx", (B, hq * hd), device=dev))
@@ -464,6 +494,7 @@ class LlamaStack:
         self.use_graph = use_graph
         self.graph = None
         self.positions = torch.arange(prompt_len, device=device, dtype=torch.int32).repeat(batch)
+        rope_inv_freq(cfg, device)  # made here, outside any graph capture
         if tp.size > 1 and tp.peer is None:  # set up outside any graph capture
             import torch.distributed as dist
             from . import comm

@@ -296,10 +296,38 @@ def softmax(s: torch.Tensor, *, causal: bool = False, scale: float = 1.0, causal
     return out
 
 
+def _freq_table(inv_freq: Optional[torch.Tensor], head_dim: int, dev) -> Optional[int]:
+    if inv_freq is None:
+        return None
+    _need(inv_freq.is_cuda and inv_freq.device == dev and inv_freq.dtype == torch.float32
+          and inv_freq.is_contiguous() and inv_freq.numel() == head_dim // 2,
+          "inv_freq must be contiguous fp32 CUDA [head_dim/2] on the tensor's device")
+    return inv_freq.data_ptr()
+
+
+def rope_freqs(head_dim: int, theta: float = 10000.0, *, llama3_scaling=None, device=None) -> torch.Tensor:
+    """Per-frequency rates [head_dim/2] (fp32) for the *_freqs RoPE paths:
+    theta^(-2i/head_dim), with the Llama-3 frequency scaling of
+    legalize.py:50-64 when llama3_scaling is True (the reference's factor 32,
+    low 1, high 4, old context 8192) or a tuple (factor, low, high, old_ctx).
+    Built on the host by npub_rope_llama3_freqs, then copied to `device`."""
+    import ctypes
+    if llama3_scaling is True:
+        llama3_scaling = (32.0, 1.0, 4.0, 8192.0)
+    factor, low, high, old = llama3_scaling if llama3_scaling else (0.0, 1.0, 4.0, 8192.0)
+    out = (ctypes.c_float * (head_dim // 2))()
+    _lib.call("npub_rope_llama3_freqs", ctypes.addressof(out), int(head_dim), float(theta), float(factor), float(low),
+              float(high), float(old))
+    t = torch.tensor(list(out), dtype=torch.float32)
+    return t.to(device) if device is not None else t
+
+
 def rope(x: torch.Tensor, heads: int, head_dim: int, *, pos0: int = 0, positions: Optional[torch.Tensor] = None,
-         theta: float = 10000.0) -> torch.Tensor:
+         theta: float = 10000.0, inv_freq: Optional[torch.Tensor] = None) -> torch.Tensor:
     """In-place RoPE on the first heads*head_dim columns of x [tokens, >=heads*head_dim]
-    (rotate_half convention, llama_layer.py:33-40,96-112).  Returns x."""
+    (rotate_half convention, llama_layer.py:33-40,96-112).  inv_freq (fp32
+    CUDA [head_dim/2], from rope_freqs) replaces theta's frequencies, e.g.
+    the Llama-3 scaled ones.  Returns x."""
     ldx = _mat(x, "x", torch.float16)
     tokens = x.shape[0]
     _need(x.shape[1] >= heads * head_dim, "x is narrower than heads*head_dim")
@@ -308,7 +336,12 @@ def rope(x: torch.Tensor, heads: int, head_dim: int, *, pos0: int = 0, positions
         _need(positions.is_cuda and positions.dtype == torch.int32 and positions.numel() == tokens
               and positions.is_contiguous(), "positions must be contiguous int32 CUDA [tokens]")
         pos_ptr = positions.data_ptr()
-    _lib.call("npub_rope", x.data_ptr(), ldx, tokens, heads, head_dim, pos_ptr, int(pos0), float(theta), _stream())
+    fp = _freq_table(inv_freq, head_dim, x.device)
+    if fp is None:
+        _lib.call("npub_rope", x.data_ptr(), ldx, tokens, heads, head_dim, pos_ptr, int(pos0), float(theta),
+                  _stream())
+    else:
+        _lib.call("npub_rope_freqs", x.data_ptr(), ldx, tokens, heads, head_dim, pos_ptr, int(pos0), fp, _stream())
     return x
 
 
@@ -414,7 +447,7 @@ def kv_append(k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor, v
 
 def rope_kv_append(qkv: torch.Tensor, q_heads: int, kv_heads: int, head_dim: int, positions: torch.Tensor,
                    k_cache: torch.Tensor, v_cache: torch.Tensor, *, theta: float = 10000.0,
-                   lens: Optional[torch.Tensor] = None) -> None:
+                   lens: Optional[torch.Tensor] = None, inv_freq: Optional[torch.Tensor] = None) -> None:
     """Decode step: rope() on the q and k heads of the fused QKV rows (in place)
     and kv_append() of the rotated k and the v heads at positions[t], in one
     kernel; lens (int32 [tokens], optional) receives positions + 1."""
@@ -430,13 +463,19 @@ def rope_kv_append(qkv: torch.Tensor, q_heads: int, kv_heads: int, head_dim: int
     if lens is not None:
         _need(lens.is_cuda and lens.dtype == torch.int32 and lens.numel() == T and lens.is_contiguous(),
               "lens must be contiguous int32 CUDA [tokens]")
-    _lib.call("npub_rope_kv_append", qkv.data_ptr(), ldx, T, q_heads, kv_heads, head_dim, positions.data_ptr(),
-              float(theta), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[2], _ptr(lens), _stream())
+    fp = _freq_table(inv_freq, head_dim, qkv.device)
+    if fp is None:
+        _lib.call("npub_rope_kv_append", qkv.data_ptr(), ldx, T, q_heads, kv_heads, head_dim, positions.data_ptr(),
+                  float(theta), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[2], _ptr(lens), _stream())
+    else:
+        _lib.call("npub_rope_kv_append_freqs", qkv.data_ptr(), ldx, T, q_heads, kv_heads, head_dim,
+                  positions.data_ptr(), fp, k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[2], _ptr(lens),
+                  _stream())
 
 
 def rope_kv_store(qkv: torch.Tensor, q_heads: int, kv_heads: int, head_dim: int, positions: torch.Tensor,
                   k_cache: torch.Tensor, v_cache: torch.Tensor, *, tokens_per_seq: int,
-                  theta: float = 10000.0) -> None:
+                  theta: float = 10000.0, inv_freq: Optional[torch.Tensor] = None) -> None:
     """Prefill: rope() on the q and k heads of the fused QKV rows of `batch`
     prompts (rows r = b * tokens_per_seq + i, in place) and the rotated k and the
     v heads written to the caches [batch, kv_heads, cap, head_dim] at
@@ -452,9 +491,14 @@ def rope_kv_store(qkv: torch.Tensor, q_heads: int, kv_heads: int, head_dim: int,
         _need(c.is_cuda and c.dtype == torch.float16 and c.is_contiguous() and c.dim() == 4
               and tuple(c.shape[:2]) == (batch, kv_heads) and c.shape[3] == head_dim,
               f"{nm} must be contiguous fp16 CUDA [batch, kv_heads, cap, head_dim]")
-    _lib.call("npub_rope_kv_store", qkv.data_ptr(), ldx, T, tokens_per_seq, q_heads, kv_heads, head_dim,
-              positions.data_ptr(), float(theta), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[2],
-              _stream())
+    fp = _freq_table(inv_freq, head_dim, qkv.device)
+    if fp is None:
+        _lib.call("npub_rope_kv_store", qkv.data_ptr(), ldx, T, tokens_per_seq, q_heads, kv_heads, head_dim,
+                  positions.data_ptr(), float(theta), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[2],
+                  _stream())
+    else:
+        _lib.call("npub_rope_kv_store_freqs", qkv.data_ptr(), ldx, T, tokens_per_seq, q_heads, kv_heads, head_dim,
+                  positions.data_ptr(), fp, k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[2], _stream())
 
 
 def isa_vector(word: int, in1: torch.Tensor, in2: Optional[torch.Tensor] = None,

@@ -7,7 +7,8 @@ Each function restates a reference computation, citing the file it follows
     test_swiglu.py:41-46, test_attention.py:57-69);
   * tiled_fp16_ref  (d_compiler/tests/test_tiling.py:37-47);
   * float64 ref_layer  (d_compiler/npu_compiler/model.py:115-157) and the RoPE
-    tables (d_compiler/npu_compiler/legalize.py:67-85);
+    tables with the Llama-3 frequency scaling
+    (d_compiler/npu_compiler/legalize.py:50-85);
   * the W8A16 quantisation, which the reference does not have: symmetric per
     output channel, scale = fp16(absmax / 127), q = clip(rint(W / scale), +-127).
     Parity of that part is unpinned by any reference test; it is pinned here by
@@ -141,10 +142,39 @@ def softmax_ref(s: np.ndarray, scale: float = 1.0, causal: bool = False, offset:
     return e / e.sum(axis=-1, keepdims=True)
 
 
-def rope_tables(seq: int, hd: int, base: float = 10000.0, pos0: int = 0):
-    """Host cos/sin tables of legalize.py:67-85 (no llama3 scaling), [seq, hd]."""
-    half = hd // 2
-    freqs = base ** (-2.0 * np.arange(half) / hd)
+def llama3_scale_freqs(freqs: np.ndarray, factor: float = 32.0, low: float = 1.0, high: float = 4.0,
+                       old_ctx: float = 8192.0) -> np.ndarray:
+    """Llama-3 RoPE frequency scaling of legalize.py:50-64, float64: frequencies
+    whose wavelength exceeds old_ctx/low are divided by factor, those below
+    old_ctx/high kept, the band between blended linearly in old_ctx/wavelength."""
+    out = np.empty_like(np.asarray(freqs, dtype=np.float64))
+    for i, f in enumerate(np.asarray(freqs, dtype=np.float64)):
+        wl = 2.0 * np.pi / f
+        if wl > old_ctx / low:
+            out[i] = f / factor
+        elif wl < old_ctx / high:
+            out[i] = f
+        else:
+            sm = (old_ctx / wl - low) / (high - low)
+            out[i] = (1.0 - sm) * f / factor + sm * f
+    return out
+
+
+def rope_freqs(hd: int, base: float = 10000.0, llama3_scaling=False) -> np.ndarray:
+    """base^(-2i/hd) for i < hd/2 (legalize.py:71), Llama-3 scaled when
+    llama3_scaling is True (the reference's constants) or a tuple (factor,
+    low, high, old_ctx) (legalize.py:72-73)."""
+    freqs = base ** (-2.0 * np.arange(hd // 2) / hd)
+    if llama3_scaling is True:
+        freqs = llama3_scale_freqs(freqs)
+    elif llama3_scaling:
+        freqs = llama3_scale_freqs(freqs, *llama3_scaling)
+    return freqs
+
+
+def rope_tables(seq: int, hd: int, base: float = 10000.0, pos0: int = 0, llama3_scaling=False):
+    """Host cos/sin tables of legalize.py:67-85, [seq, hd] (float64)."""
+    freqs = rope_freqs(hd, base, llama3_scaling)
     ang = (np.arange(seq)[:, None] + pos0) * freqs[None, :]
     cos = np.concatenate([np.cos(ang), np.cos(ang)], axis=1)
     sin = np.concatenate([np.sin(ang), np.sin(ang)], axis=1)
@@ -362,7 +392,8 @@ def _ffn64(P: Dict[str, np.ndarray], hn: np.ndarray) -> np.ndarray:
 
 
 def ref_decode_layer_q(L: Dict[str, np.ndarray], x: np.ndarray, k_cache, v_cache, pos: np.ndarray, heads: int,
-                       kv_heads: int, hd: int, eps: float, theta: float = 10000.0) -> np.ndarray:
+                       kv_heads: int, hd: int, eps: float, theta: float = 10000.0,
+                       inv_freq: Optional[np.ndarray] = None) -> np.ndarray:
     """One decode step of the float64 layer: x [B, d] is the token at position
     pos[b] of sequence b; k_cache / v_cache [B, kv_heads, >= pos[b], hd] hold
     the (already rotated) keys and the values of positions 0 .. pos[b] - 1.
@@ -374,8 +405,8 @@ def ref_decode_layer_q(L: Dict[str, np.ndarray], x: np.ndarray, k_cache, v_cache
     xn = _rms64(x, P["g1"], eps)
     qkv = xn @ P["qkv"].T
     pos = np.asarray(pos)
-    q = _rope64(qkv[:, :qd], heads, hd, pos, theta)
-    k = _rope64(qkv[:, qd:qd + kd], kv_heads, hd, pos, theta)
+    q = _rope64(qkv[:, :qd], heads, hd, pos, theta, inv_freq)
+    k = _rope64(qkv[:, qd:qd + kd], kv_heads, hd, pos, theta, inv_freq)
     v = qkv[:, qd + kd:qd + 2 * kd]
     grp = heads // kv_heads
     ctx = np.zeros((B, qd))
@@ -397,7 +428,7 @@ def ref_decode_layer_q(L: Dict[str, np.ndarray], x: np.ndarray, k_cache, v_cache
 
 def ref_stack_logits(layers, embed: np.ndarray, norm: np.ndarray, lm_head: np.ndarray, tokens: np.ndarray,
                      heads: int, kv_heads: int, hd: int, eps: float, theta: float = 10000.0,
-                     rows: Optional[np.ndarray] = None) -> np.ndarray:
+                     rows: Optional[np.ndarray] = None, inv_freq: Optional[np.ndarray] = None) -> np.ndarray:
     """float64 decoder stack on sequences of token ids tokens [B, T]: embedding
     rows (fp16 table), the layers (an iterable of ref_layer_q weight dicts,
     each prepared once and applied to every sequence), final RMSNorm and the
@@ -416,7 +447,7 @@ def ref_stack_logits(layers, embed: np.ndarray, norm: np.ndarray, lm_head: np.nd
             if not group:
                 break
             for P in ex.map(prepare_layer, group):
-                xs = [ref_layer_q(P, x, heads, kv_heads, hd, eps, theta) for x in xs]
+                xs = [ref_layer_q(P, x, heads, kv_heads, hd, eps, theta, inv_freq=inv_freq) for x in xs]
     rows = np.arange(tokens.shape[1]) if rows is None else np.asarray(rows)
     lm = np.asarray(lm_head, dtype=np.float64)
     return np.stack([_rms64(x[rows], norm, eps) @ lm.T for x in xs])

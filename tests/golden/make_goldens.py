@@ -31,6 +31,14 @@ temporary directory) and records only their outputs:
                      W [512,512] ~N(0,0.02), numpy default_rng(0)) run through
                      the compiler-style 64-tiled program on the reference
                      simulator: C as fp16, with sha256 of the inputs.
+  rope_tables.npz    the compiler's host RoPE tables (cos, sin, rotate_half
+                     matrix) from d_compiler/npu_compiler/legalize.py's own
+                     rope_tables(), for the Llama 3.2 3B layer (base 500000,
+                     Llama-3 frequency scaling) and the reduced layer (base
+                     10000); rows sampled over positions 0..4199.  legalize.py imports TVM's relax module at the top
+                     but these functions only use numpy, so it is loaded with a
+                     placeholder `tvm` module.
+  --only rope        regenerates that file alone.
 """
 from __future__ import annotations
 
@@ -242,14 +250,48 @@ def config1():
             "sha_A": hashlib.sha256(A.tobytes()).hexdigest(), "sha_W": hashlib.sha256(W.tobytes()).hexdigest()}
 
 
+def rope_tables(refdir):
+    """cos/sin/rot from the reference compiler's rope_tables (legalize.py:67-85)."""
+    import importlib.util
+    import types
+    tvm = types.ModuleType("tvm")
+    tvm.relax = types.ModuleType("tvm.relax")
+    saved = {k: sys.modules.get(k) for k in ("tvm", "tvm.relax")}
+    sys.modules["tvm"], sys.modules["tvm.relax"] = tvm, tvm.relax
+    try:
+        spec = importlib.util.spec_from_file_location(
+            "ref_legalize", os.path.join(refdir, "d_compiler", "npu_compiler", "legalize.py"))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                sys.modules.pop(k, None)
+            else:
+                sys.modules[k] = v
+    out = {}
+    for name, seq, hd, base, scaled in (("llama3", 4200, 128, 500000.0, True), ("reduced", 8, 16, 10000.0, False),
+                                        ("hd128", 4200, 128, 10000.0, False)):
+        cos, sin, rot = mod.rope_tables(seq, hd, base=base, llama3_scaling=scaled)
+        rows = np.unique(np.concatenate([np.arange(min(seq, 16)), np.arange(0, seq, 131), np.arange(seq - 8, seq)]))
+        out[f"{name}_rows"] = rows
+        out[f"{name}_cos"], out[f"{name}_sin"], out[f"{name}_rot"] = cos[rows], sin[rows], rot
+        out[f"{name}_args"] = np.array([seq, hd, base, float(scaled)])
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("NPU_COMP_REF"),
                     help="root of the reference checkout (default: $NPU_COMP_REF)")
-    ap.add_argument("--only", choices=["programs"], default=None, help="regenerate one fixture file only")
+    ap.add_argument("--only", choices=["programs", "rope"], default=None, help="regenerate one fixture file only")
     a = ap.parse_args()
     if not a.ref:
         ap.error("the reference root is required: --ref <dir> or NPU_COMP_REF=<dir>")
+    if a.only == "rope":
+        np.savez_compressed(os.path.join(HERE, "rope_tables.npz"), **rope_tables(a.ref))
+        print("wrote rope_tables.npz")
+        return
     subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={a.ref}"], check=True)
     progs = programs(a.ref)
     np.savez_compressed(os.path.join(HERE, "programs.npz"), **progs)
@@ -261,6 +303,7 @@ def main():
         json.dump({"gbuf": "ramp G[i] = fp16(i), i < 8192 (c_hex_data/w_support_binary_data_gen.cpp)",
                    "maxrun": 30, "gbytes": 16385, "pbytes": 1025, "programs": gold}, f, indent=0)
     np.savez_compressed(os.path.join(HERE, "examples.npz"), **examples(a.ref))
+    np.savez_compressed(os.path.join(HERE, "rope_tables.npz"), **rope_tables(a.ref))
     c1 = config1()
     np.savez_compressed(os.path.join(HERE, "w8a16_config1.npz"), C_mysim=c1["C_mysim"],
                         instructions=c1["instructions"], sha_A=np.array(c1["sha_A"]), sha_W=np.array(c1["sha_W"]))
