@@ -177,6 +177,15 @@ int npub_rope(void* x, int64_t ldx, int tokens, int heads, int head_dim, const i
 int npub_embed(const int32_t* ids, int n, const void* table, int64_t ldt, int vocab, int d, void* out, int64_t ldo,
                void* stream);
 int npub_argmax_rows(const void* x, int64_t ldx, int rows, int cols, int32_t* idx, float* val, void* stream);
+/* Greedy selection over a vocabulary split across tensor-parallel ranks, in
+ * one exchange: npub_argmax_keys packs each row's (largest logit, its smallest
+ * index + index_offset) into one uint64 key that orders by value, then by
+ * smaller index; after an all-gather of the ranks' keys [ranks, rows],
+ * npub_select_keys writes the winning global index of every row to ids.
+ * The result is npub_argmax_rows over the concatenated vocabulary. */
+int npub_argmax_keys(const void* x, int64_t ldx, int rows, int cols, int32_t index_offset, uint64_t* keys,
+                     void* stream);
+int npub_select_keys(const uint64_t* keys, int ranks, int rows, int32_t* ids, void* stream);
 
 /* -------------------------------------------------------- attention ----
  * Causal prefill attention, llama_layer.py:114-137, legalize.py:117-127 for

@@ -48,6 +48,8 @@ SIGNATURES = {
     "npub_add": (_i, [_p, _i64, _p, _i64, _p, _i64, _i, _i, _p]),
     "npub_embed": (_i, [_p, _i, _p, _i64, _i, _i, _p, _i64, _p]),
     "npub_argmax_rows": (_i, [_p, _i64, _i, _i, _p, _p, _p]),
+    "npub_argmax_keys": (_i, [_p, _i64, _i, _i, _i, _p, _p]),
+    "npub_select_keys": (_i, [_p, _i, _i, _p, _p]),
     "npub_softmax_rows": (_i, [_p, _p, _i64, _i64, _i, _i, _i, _f, _i, _i, _p]),
     "npub_rope": (_i, [_p, _i64, _i, _i, _i, _p, _i, _f, _p]),
     "npub_attention_prefill": (_i, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _i, _i, _i, _i, _f, _i, _p, _sz, _p]),

@@ -527,8 +527,17 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const __half* __re
 }
 
 // Row argmax over fp16 logits: the largest value and its smallest index.
+// Order-preserving 64-bit key of (value, index): the float's bits made
+// unsigned-monotone in the high word, 0xffffffff - index in the low word, so
+// the largest key is the largest value with the smallest index.
+__device__ __forceinline__ uint64_t argmax_key(float v, int32_t i) {
+    const uint32_t u = __float_as_uint(v);
+    const uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((uint64_t)o << 32) | (uint64_t)(0xffffffffu - (uint32_t)i);
+}
+
 __global__ void argmax_kernel(const __half* __restrict__ x, int64_t ldx, int cols, int32_t* __restrict__ idx,
-                              float* __restrict__ val) {
+                              float* __restrict__ val, uint64_t* __restrict__ key, int32_t key_off) {
     pdl_trigger();
     pdl_wait();
     __shared__ float sv[32];
@@ -564,9 +573,24 @@ __global__ void argmax_kernel(const __half* __restrict__ x, int64_t ldx, int col
                 best = sv[i];
                 bi = si[i];
             }
-        idx[blockIdx.x] = bi;
+        if (idx) idx[blockIdx.x] = bi;
         if (val) val[blockIdx.x] = best;
+        if (key) key[blockIdx.x] = argmax_key(best, bi + key_off);
     }
+}
+
+// ids[b] = the index of the largest key[r * rows + b] over r < ranks.
+__global__ void select_keys_kernel(const uint64_t* __restrict__ key, int ranks, int rows, int32_t* __restrict__ ids) {
+    pdl_trigger();
+    pdl_wait();
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= rows) return;
+    uint64_t best = key[b];
+    for (int r = 1; r < ranks; ++r) {
+        const uint64_t k = key[(int64_t)r * rows + b];
+        best = k > best ? k : best;
+    }
+    ids[b] = (int32_t)(0xffffffffu - (uint32_t)(best & 0xffffffffu));
 }
 
 // ------------------------------------------------------------ quantiser
@@ -899,5 +923,24 @@ extern "C" int npub_argmax_rows(const void* x, int64_t ldx, int rows, int cols, 
     if (rows == 0) return NPUB_OK;
     NPUB_CHECK_ARG(x && idx && cols > 0 && ldx >= cols);
     return launch_pdl(argmax_kernel, dim3(rows), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
-                      reinterpret_cast<const __half*>(x), ldx, cols, idx, val);
+                      reinterpret_cast<const __half*>(x), ldx, cols, idx, val, (uint64_t*)nullptr, 0);
+}
+
+extern "C" int npub_argmax_keys(const void* x, int64_t ldx, int rows, int cols, int32_t index_offset, uint64_t* keys,
+                                void* stream) {
+    NPUB_CHECK_ARG(rows >= 0);
+    if (rows == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(x && keys && cols > 0 && ldx >= cols && index_offset >= 0);
+    NPUB_CHECK_ARG((int64_t)index_offset + cols <= 0x7fffffff && npub_aligned(keys, 8));
+    return launch_pdl(argmax_kernel, dim3(rows), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+                      reinterpret_cast<const __half*>(x), ldx, cols, (int32_t*)nullptr, (float*)nullptr, keys,
+                      index_offset);
+}
+
+extern "C" int npub_select_keys(const uint64_t* keys, int ranks, int rows, int32_t* ids, void* stream) {
+    NPUB_CHECK_ARG(rows >= 0 && ranks >= 0);
+    if (rows == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(keys && ids && ranks > 0 && npub_aligned(keys, 8));
+    return launch_pdl(select_keys_kernel, dim3((rows + 127) / 128), dim3(128), 0,
+                      reinterpret_cast<cudaStream_t>(stream), keys, ranks, rows, ids);
 }

@@ -512,21 +512,16 @@ class LlamaStack:
                                 residual_out=sc.get("fres", (B, cfg.d), device=self.dev),
                                 out=sc.get("fn", (B, cfg.d), device=self.dev))
         logits = npu.matmul(hn, w.lm_head, out=sc.get("logits", (B, w.lm_head.shape[0]), device=self.dev))
-        idx, val = npu.argmax(logits, idx=sc.get("amax_i", (B,), torch.int32, self.dev),
-                              val=sc.get("amax_v", (B,), torch.float32, self.dev))
         if tp.size == 1:
-            self.ids.copy_(idx)
+            npu.argmax(logits, idx=self.ids, val=sc.get("amax_v", (B,), torch.float32, self.dev))
             return
+        # one (value, global index) key per row and shard, one all-gather, one
+        # selection kernel: the largest value, the smallest index on ties
         import torch.distributed as dist
-        gidx = sc.get("amax_g", (B,), torch.int32, self.dev)
-        torch.add(idx, w.vocab_off, out=gidx)
-        all_v = sc.get("all_v", (tp.size * B,), torch.float32, self.dev)
-        all_i = sc.get("all_i", (tp.size * B,), torch.int32, self.dev)
-        dist.all_gather_into_tensor(all_v, val, group=tp.group)
-        dist.all_gather_into_tensor(all_i, gidx, group=tp.group)
-        # shards hold ascending vocabulary ranges: the first maximal rank has the smallest index
-        best = torch.argmax(all_v.view(tp.size, B), dim=0)
-        self.ids.copy_(torch.gather(all_i.view(tp.size, B), 0, best.view(1, B)).view(B))
+        keys = npu.argmax_keys(logits, w.vocab_off, keys=sc.get("amax_k", (B,), torch.int64, self.dev))
+        all_k = sc.get("all_k", (tp.size * B,), torch.int64, self.dev)
+        dist.all_gather_into_tensor(all_k, keys, group=tp.group)
+        npu.select_keys(all_k, tp.size, ids=self.ids)
 
     def prefill(self, prompts: torch.Tensor) -> torch.Tensor:
         cfg, B, T = self.cfg, self.B, self.T

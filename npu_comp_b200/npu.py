@@ -372,6 +372,33 @@ def argmax(x: torch.Tensor, *, idx: Optional[torch.Tensor] = None, val: Optional
     return idx, val
 
 
+def argmax_keys(x: torch.Tensor, index_offset: int = 0, *, keys: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Per-row greedy key (int64 [rows]) of fp16 logits x: the largest value and
+    its smallest index + index_offset in one orderable word (npub_argmax_keys);
+    select_keys over the keys of every vocabulary shard gives the global argmax."""
+    ldx = _mat(x, "x", torch.float16)
+    rows, cols = x.shape
+    if keys is None:
+        keys = torch.empty((rows,), dtype=torch.int64, device=x.device)
+    _need(keys.is_cuda and keys.dtype == torch.int64 and keys.numel() == rows and keys.is_contiguous(),
+          "keys must be contiguous int64 CUDA [rows]")
+    _lib.call("npub_argmax_keys", x.data_ptr(), ldx, rows, cols, int(index_offset), keys.data_ptr(), _stream())
+    return keys
+
+
+def select_keys(keys: torch.Tensor, ranks: int, *, ids: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """ids[b] = index of the largest of keys[r * rows + b] over r < ranks (int32)."""
+    _need(keys.is_cuda and keys.dtype == torch.int64 and keys.is_contiguous() and keys.numel() % ranks == 0,
+          "keys must be contiguous int64 CUDA [ranks * rows]")
+    rows = keys.numel() // ranks
+    if ids is None:
+        ids = torch.empty((rows,), dtype=torch.int32, device=keys.device)
+    _need(ids.is_cuda and ids.dtype == torch.int32 and ids.numel() == rows and ids.is_contiguous(),
+          "ids must be contiguous int32 CUDA [rows]")
+    _lib.call("npub_select_keys", keys.data_ptr(), int(ranks), rows, ids.data_ptr(), _stream())
+    return ids
+
+
 # ----------------------------------------------------------------- attention
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, kv_heads: Optional[int] = None, *,

@@ -186,4 +186,5 @@ def test_weight_file_drives_the_stack_to_the_same_tokens(cuda_device, tmp_path):
         st.decode(4, record=True)
         toks.append(torch.stack(st.tokens).cpu())
         st.release()
+    assert npu.device_error() == 0
     assert torch.equal(toks[0], toks[1])

@@ -109,3 +109,23 @@ def test_residual_add(cuda_device, rng, rows, cols):
     b = rng.standard_normal((rows, cols)).astype(np.float16)
     got = nb.add(dev(a, cuda_device), dev(b, cuda_device)).cpu().numpy()
     assert np.array_equal(got, (a.astype(np.float32) + b.astype(np.float32)).astype(np.float16))  # exact
+
+
+@pytest.mark.parametrize("ranks", [1, 2, 4, 8])
+def test_greedy_keys_select_the_global_argmax(cuda_device, rng, ranks):
+    """argmax_keys on each vocabulary shard + select_keys over the gathered keys
+    == the argmax of the whole row (largest value, smallest index on ties),
+    including ties placed across shards and all-negative rows."""
+    B, V = 9, 4096
+    x = rng.standard_normal((B, V)).astype(np.float16)
+    x[1, 100] = x[1, 3000] = 7.0        # tie across shards: the smaller index wins
+    x[2, 5] = x[2, 6] = 9.0             # tie inside a shard
+    x[3] = -np.abs(x[3]) - 1.0          # no positive logit
+    x[4, V - 1] = 11.0                  # the last index
+    xt = dev(x, cuda_device)
+    vs = V // ranks
+    keys = torch.cat([nb.npu.argmax_keys(xt[:, r * vs:(r + 1) * vs].contiguous(), r * vs) for r in range(ranks)])
+    ids = nb.npu.select_keys(keys, ranks).cpu().numpy()
+    assert np.array_equal(ids, np.argmax(x.astype(np.float32), axis=1))
+    idx, _ = nb.argmax(xt)
+    assert np.array_equal(idx.cpu().numpy(), ids)
