@@ -111,8 +111,11 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const __half* __restrict__ 
 // (no block barrier), and the row stays in registers as packed fp16 between
 // the two passes.  At 2048 x 4096 it measured 10.6 us (one CTA per row with
 // block reductions: 11.1 us; persistent double-buffered CTAs: 10.0-19.6 us).
-template <int CPL>
-__global__ void __launch_bounds__(64) rmsnorm_warp_kernel(const __half* __restrict__ x, int64_t ldx,
+// HAS_R: the residual-add form (x and r of the row in registers at once);
+// without it the kernel fits ten 64-thread CTAs per SM, so a 2048-row
+// prompt is one wave of 2048 warps with every load of its rows in flight.
+template <int CPL, bool HAS_R>
+__global__ void __launch_bounds__(64, HAS_R ? 1 : 10) rmsnorm_warp_kernel(const __half* __restrict__ x, int64_t ldx,
                                                          const __half* __restrict__ r, int64_t ldr, __half* xo,
                                                          int64_t ldxo, const __half* __restrict__ gamma,
                                                          __half* __restrict__ y, int64_t ldy, int rows, int d,
@@ -130,7 +133,7 @@ __global__ void __launch_bounds__(64) rmsnorm_warp_kernel(const __half* __restri
         const int ch = lane + 32 * j;
         if (ch < nch) v[j] = *reinterpret_cast<const uint4*>(xr + ch * kVec);
     }
-    if (r) {
+    if (HAS_R) {
         const __half* rr = r + (int64_t)row * ldr;
         uint4 w[CPL];
 #pragma unroll
@@ -673,8 +676,11 @@ extern "C" int npub_rmsnorm(const void* x, int64_t ldx, const void* residual, in
     const __half* gh = reinterpret_cast<const __half*>(gamma);
     __half* yh = reinterpret_cast<__half*>(y);
     const int nch = d / kVec;
-#define NPUB_RMSW(C) launch_pdl(rmsnorm_warp_kernel<C>, dim3((rows + 1) / 2), dim3(64), 0, st, xh, ldx, rh, ldr, xoh, \
-                                ldxo, gh, yh, ldy, rows, d, eps)
+#define NPUB_RMSW(C)                                                                                              \
+    (rh ? launch_pdl(rmsnorm_warp_kernel<C, true>, dim3((rows + 1) / 2), dim3(64), 0, st, xh, ldx, rh, ldr, xoh, \
+                     ldxo, gh, yh, ldy, rows, d, eps)                                                           \
+        : launch_pdl(rmsnorm_warp_kernel<C, false>, dim3((rows + 1) / 2), dim3(64), 0, st, xh, ldx, rh, ldr,   \
+                     xoh, ldxo, gh, yh, ldy, rows, d, eps))
     if (nch <= 64) return NPUB_RMSW(2);
     if (nch <= 128) return NPUB_RMSW(4);
     if (nch <= 256) return NPUB_RMSW(8);
