@@ -633,28 +633,19 @@ bool w8a16_skinny_fits(int M, int N) {
 
 // Measured on B200 (decode-layer shapes, weights streamed from HBM, CUDA
 // graph replay): the stream-K kernel wins on every matrix with N >= 8192 and,
-// at M <= 32, on K-long ones (4096 x 11008: 22.1 vs 23.3 us); the 2-CTA pair
-// kernel wins on the small square ones (4096 x 4096: 12.8 vs 14.3 us at
-// M = 32) and on K-long ones at M = 64, where its wider MMAs issue fewer
-// instructions per weight byte.
+// at M <= 32, on K-long ones (4096 x 11008) and, inside a decode layer, on
+// the square 4096 x 4096 projection (215.6 vs 219.0 us per batch-32 layer:
+// its weights stream while the attention kernel finishes, although alone it
+// is slower, 22.9 vs 21.7 us); the 2-CTA pair kernel wins on the square and
+// K-long ones at M = 64 (745 vs 754 us per batch-64 layer), where its wider
+// MMAs issue fewer instructions per weight byte.
 // NPUB_W8A16_KERNEL=pair or =skinny in the environment overrides the choice
 // (where the shape allows it), for measuring both kernels on one shape.
-static int kernel_override() {
-    static const int v = [] {
-        const char* e = getenv("NPUB_W8A16_KERNEL");
-        if (!e) return 0;
-        if (!strcmp(e, "pair")) return 1;
-        if (!strcmp(e, "skinny")) return 2;
-        return 0;
-    }();
-    return v;
-}
-
 bool w8a16_use_skinny(int M, int N, int K) {
     if (!w8a16_skinny_fits(M, N) || K <= 0) return false;
     const int o = kernel_override();
     if (o) return o == 2;
-    return N >= 8192 || (M <= 32 && K >= 8192);
+    return N >= 8192 || (M <= 32 && (K >= 8192 || (N >= 4096 && K >= 4096)));
 }
 
 size_t w8a16_skinny_workspace(int M, int N, int K) {
