@@ -641,6 +641,17 @@ bool w8a16_skinny_fits(int M, int N) {
 // MMAs issue fewer instructions per weight byte.
 // NPUB_W8A16_KERNEL=pair or =skinny in the environment overrides the choice
 // (where the shape allows it), for measuring both kernels on one shape.
+static int kernel_override() {
+    static const int v = [] {
+        const char* e = getenv("NPUB_W8A16_KERNEL");
+        if (!e) return 0;
+        if (!strcmp(e, "pair")) return 1;
+        if (!strcmp(e, "skinny")) return 2;
+        return 0;
+    }();
+    return v;
+}
+
 bool w8a16_use_skinny(int M, int N, int K) {
     if (!w8a16_skinny_fits(M, N) || K <= 0) return false;
     const int o = kernel_override();
