@@ -23,7 +23,6 @@
 #include "common.cuh"
 #include "gemm_tc.h"
 #include "gemm_w8a16_pair.h"
-#include "gemm_w8a16_pair_ts.h"
 #include "gemm_w8a16_skinny.h"
 
 #include <cudaTypedefs.h>
@@ -449,7 +448,6 @@ static size_t linear_workspace(int M, int N, int K, bool w_int8) {
     if (w_int8) {
         // every W8A16 workspace starts with the stream-K kernel's counter region
         if (w8a16_use_skinny(M, N, K)) return w8a16_skinny_workspace(M, N, K);
-        if (w8a16_use_pair_ts(M, N, K)) return 0;
         const size_t pair = w8a16_pair_workspace(M, N, K);
         return pair ? kSkinnyCounterBytes + pair : 0;
     }
@@ -522,8 +520,6 @@ static int linear(bool w_int8, const void* A, int64_t lda, const void* W, int64_
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (w_int8 && w8a16_use_skinny(M, N, K))
         return w8a16_skinny_run(A, lda, W, ldw, scale, C, ldc, R, ldr, M, N, K, alpha, ws, ws_bytes, st);
-    if (w_int8 && w8a16_use_pair_ts(M, N, K))
-        return w8a16_pair_ts_run(A, lda, W, ldw, scale, C, ldc, R, ldr, M, N, K, alpha, st);
     if (w_int8) return linear_w8a16_pair(A, lda, W, ldw, scale, C, ldc, R, ldr, M, N, K, alpha, ws, ws_bytes, st);
 
     GemmParams p;
@@ -613,7 +609,6 @@ extern "C" int npub_w8a16_gemm_swiglu(const void* A, int64_t lda, const int8_t* 
 extern "C" const char* npub_w8a16_kernel_name(int M, int N, int K) {
     if (M <= 0 || N <= 0 || K <= 0) return "none";
     if (npub::w8a16_use_skinny(M, N, K)) return "w8a16_skinny_kernel (stream-K, tcgen05 with A in TMEM)";
-    if (npub::w8a16_use_pair_ts(M, N, K)) return "w8a16_pair_ts_kernel (tcgen05 cta_group::2, A in TMEM)";
     return "w8a16_pair_kernel (tcgen05 cta_group::2 W8A16)";
 }
 

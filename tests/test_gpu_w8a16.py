@@ -218,39 +218,6 @@ def test_invalid_shapes_raise(cuda_device):
         nb.matmul(A, torch.zeros((8, 16), dtype=torch.int8, device=cuda_device))  # K mismatch
 
 
-_PAIR_TS_CHECK = r"""
-import numpy as np, torch, sys
-sys.path.insert(0, sys.argv[1])
-import npu_comp_b200 as nb
-from npu_comp_b200 import _lib
-from oracle import ref
-dev = torch.device("cuda", 0)
-rng = np.random.default_rng(11)
-for M, N, K in [(500, 600, 384), (385, 257, 1376), (2048, 4096, 4096)]:
-    assert _lib.load().npub_w8a16_kernel_name(M, N, K).decode().startswith("w8a16_pair_ts_kernel")
-    A = rng.integers(-3, 4, (M, K)).astype(np.float16)
-    q = rng.integers(-4, 5, (N, K)).astype(np.int8)
-    s = (2.0 ** rng.integers(-12, -6, N)).astype(np.float16)
-    R = rng.integers(-8, 9, (M, N)).astype(np.float16)
-    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
-    C = nb.matmul(t(A), t(q), t(s), residual=t(R)).cpu().numpy()
-    assert np.array_equal(C, ref.w8a16_ref(A, q, s, residual=R).astype(np.float16)), (M, N, K)
-print("PAIR_TS_OK")
-"""
-
-
-def test_w8a16_pair_ts_kernel_opt_in(cuda_device):
-    """The tensor-memory pair kernel is opt-in (NPUB_W8A16_KERNEL=pair_ts, read
-    once per process): run it in a child process on exact known answers."""
-    import subprocess
-    import sys
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, NPUB_W8A16_KERNEL="pair_ts")
-    r = subprocess.run([sys.executable, "-c", _PAIR_TS_CHECK, root], env=env, cwd=root, capture_output=True,
-                       text=True, timeout=600)
-    assert r.returncode == 0 and "PAIR_TS_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
-
-
 @pytest.mark.parametrize("M,F,K", [(32, 11008, 4096), (64, 2752, 4096), (32, 1376, 4096), (2048, 1376, 4096),
                                    (300, 500, 272), (5, 64, 64), (17, 4100, 1024)])
 def test_matmul_swiglu_equals_matmul_then_swiglu(cuda_device, M, F, K):
