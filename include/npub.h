@@ -332,19 +332,6 @@ int npub_comm_create(int world, int rank, size_t max_bytes, void** comm, void* h
 int npub_comm_open(void* comm, const void* all_handles);
 int npub_allreduce_f16(void* comm, const void* in, void* out, int64_t n, void* stream);
 int npub_comm_destroy(void* comm);
-/* Row-parallel W8A16 GEMM fused with that all-reduce (decode-sized M <= 64,
- * N <= 8192): every rank passes its K slice (A [M, K_r], Wq [N, K_r]) and
- * the shared per-channel scale; every rank gets
- *   C = fp16( alpha * scale[n] * sum_r sum_k A_r[m, k] Wq_r[n, k] )  (+ R),
- * the same bits on every rank.  Each finished 32-row quarter of a 128-row
- * output tile is exchanged through peer memory as soon as it is done, so the
- * reduction overlaps the rest of the GEMM.  workspace: as npub_w8a16_gemm,
- * sized by npub_w8a16_gemm_allreduce_workspace. */
-size_t npub_w8a16_gemm_allreduce_workspace(int M, int N, int K);
-int npub_w8a16_gemm_allreduce(void* comm, const void* A, int64_t lda, const int8_t* Wq, int64_t ldw,
-                              const void* scale, void* C, int64_t ldc, const void* R, int64_t ldr, int M, int N,
-                              int K, float alpha, void* workspace, size_t workspace_bytes, void* stream);
-
 #ifdef __cplusplus
 }
 #endif

@@ -79,8 +79,6 @@ SIGNATURES = {
     "npub_comm_open": (_i, [_p, _p]),
     "npub_allreduce_f16": (_i, [_p, _p, _p, _i64, _p]),
     "npub_comm_destroy": (_i, [_p]),
-    "npub_w8a16_gemm_allreduce_workspace": (_sz, [_i, _i, _i]),
-    "npub_w8a16_gemm_allreduce": (_i, [_p, _p, _i64, _p, _i64, _p, _p, _i64, _p, _i64, _i, _i, _i, _f, _p, _sz, _p]),
 }
 
 _lock = threading.Lock()

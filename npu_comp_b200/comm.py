@@ -50,26 +50,6 @@ class PeerAllReduce:
         _lib.call("npub_allreduce_f16", self._comm, t.data_ptr(), t.data_ptr(), t.numel(),
                   torch.cuda.current_stream(t.device).cuda_stream)
 
-    def gemm_fits(self, M: int, N: int) -> bool:
-        """Whether the fused GEMM + all-reduce takes this shape (M <= 64, N <= 8192)."""
-        return fused_enabled() and 0 < M <= 64 and 0 < N <= 8192
-
-    def matmul_allreduce(self, A: torch.Tensor, W: torch.Tensor, scale: torch.Tensor, *,
-                         out: torch.Tensor, residual=None, alpha: float = 1.0) -> torch.Tensor:
-        """out = all-reduce over the ranks of npu.matmul(A, W, scale) (+ residual), in one kernel."""
-        from . import npu
-        lda = npu._mat(A, "A", torch.float16)
-        ldw = npu._mat(W, "W", torch.int8)
-        ldc = npu._mat(out, "out", torch.float16)
-        M, K = A.shape
-        N = W.shape[0]
-        ldr = npu._mat(residual, "residual", torch.float16) if residual is not None else 0
-        ws, wsb = npu._zeroed_workspace(_lib.query("npub_w8a16_gemm_allreduce_workspace", M, N, K), A.device)
-        _lib.call("npub_w8a16_gemm_allreduce", self._comm, A.data_ptr(), lda, W.data_ptr(), ldw, scale.data_ptr(),
-                  out.data_ptr(), ldc, npu._ptr(residual), ldr, M, N, K, float(alpha), npu._ptr(ws), wsb,
-                  torch.cuda.current_stream(A.device).cuda_stream)
-        return out
-
     def close(self) -> None:
         if self._comm:
             _lib.load().npub_comm_destroy(self._comm)
@@ -78,11 +58,3 @@ class PeerAllReduce:
 
 def enabled() -> bool:
     return os.environ.get("NPUB_PEER_ALLREDUCE", "1") != "0"
-
-
-def fused_enabled() -> bool:
-    """The fused row-parallel GEMM + all-reduce is opt-in (NPUB_FUSED_GEMM_ALLREDUCE=1):
-    measured on 2 B200s it loses to the pair-kernel GEMM followed by the peer
-    all-reduce (decode 848 vs 737 ms per 128 steps of the stack), because it
-    needs the stream-K kernel, the slower of the two on N = 4096 projections."""
-    return enabled() and os.environ.get("NPUB_FUSED_GEMM_ALLREDUCE", "0") == "1"

@@ -42,12 +42,6 @@ struct CommDev {
     int64_t half_elems;              // elements per data half
 };
 
-// Offsets inside one rank's allocation of the GEMM all-reduce area.
-static size_t gemm_ar_stage_bytes() { return (size_t)2 * kArSlots * kArSlotFloats * sizeof(float); }
-static size_t gemm_ar_bytes() {
-    return gemm_ar_stage_bytes() + (size_t)kArMaxRanks * kArSlots * sizeof(uint32_t) + kArSlots * sizeof(uint32_t);
-}
-
 struct Comm {
     int world = 0, rank = 0, dev = 0;
     size_t max_bytes = 0, total = 0;
@@ -148,8 +142,7 @@ extern "C" int npub_comm_create(int world, int rank, size_t max_bytes, void** co
     NPUB_CUDA_TRY(cudaGetDevice(&c->dev));
     const size_t flags_bytes = (size_t)kCommMaxRanks * kCommMaxBlocks * sizeof(uint32_t);
     const size_t epoch_bytes = (size_t)kCommMaxBlocks * sizeof(uint32_t);
-    // then the fused GEMM all-reduce area: staging, flags, epochs
-    c->total = 2 * max_bytes + flags_bytes + epoch_bytes + gemm_ar_bytes();
+    c->total = 2 * max_bytes + flags_bytes + epoch_bytes;
     cudaError_t e = cudaMalloc(&c->base, c->total);
     if (e == cudaSuccess) e = cudaMemset(c->base, 0, c->total);
     cudaIpcMemHandle_t h;
@@ -213,50 +206,6 @@ extern "C" int npub_allreduce_f16(void* comm, const void* in, void* out, int64_t
                       reinterpret_cast<cudaStream_t>(stream), c->d, reinterpret_cast<const __half*>(in),
                       reinterpret_cast<__half*>(out), n, npub_internal_device_error_word(),
                       npub_internal_wait_limit_ns());
-}
-
-namespace npub {
-int comm_gemm_view(void* comm, SkinnyAR& ar) {
-    Comm* c = reinterpret_cast<Comm*>(comm);
-    if (!c || !c->d.data[0]) return NPUB_ERR_INVALID_ARG;
-    memset(&ar, 0, sizeof(ar));
-    ar.world = c->world;
-    ar.rank = c->rank;
-    const size_t base_off = 2 * c->max_bytes + (size_t)kCommMaxRanks * kCommMaxBlocks * sizeof(uint32_t) +
-                            (size_t)kCommMaxBlocks * sizeof(uint32_t);
-    for (int r = 0; r < c->world; ++r) {
-        uint8_t* b = reinterpret_cast<uint8_t*>(c->peer_base[r]) + base_off;
-        ar.stage[r] = reinterpret_cast<float*>(b);
-        ar.flags[r] = reinterpret_cast<uint32_t*>(b + gemm_ar_stage_bytes());
-    }
-    ar.epochs = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(c->base) + base_off + gemm_ar_stage_bytes() +
-                                            (size_t)kArMaxRanks * kArSlots * sizeof(uint32_t));
-    return NPUB_OK;
-}
-}  // namespace npub
-
-extern "C" size_t npub_w8a16_gemm_allreduce_workspace(int M, int N, int K) {
-    return npub::w8a16_skinny_workspace(M, N, K);
-}
-
-extern "C" int npub_w8a16_gemm_allreduce(void* comm, const void* A, int64_t lda, const int8_t* Wq, int64_t ldw,
-                                         const void* scale, void* C, int64_t ldc, const void* R, int64_t ldr, int M,
-                                         int N, int K, float alpha, void* workspace, size_t workspace_bytes,
-                                         void* stream) {
-    NPUB_CHECK_ARG(comm && M >= 0 && N >= 0 && K >= 0);
-    if (M == 0 || N == 0) return NPUB_OK;
-    NPUB_CHECK_ARG(A && Wq && C);
-    NPUB_CHECK_ARG(K % 16 == 0 && K > 0);
-    NPUB_CHECK_ARG(lda >= K && lda % 8 == 0 && npub_aligned(A, 16));
-    NPUB_CHECK_ARG(ldw >= K && ldw % 16 == 0 && npub_aligned(Wq, 16));
-    NPUB_CHECK_ARG(ldc >= N);
-    NPUB_CHECK_ARG(!R || ldr >= N);
-    if (!npub::w8a16_skinny_fits(M, N) || (N + 127) / 128 * 4 > npub::kArSlots) return NPUB_ERR_UNSUPPORTED;
-    npub::SkinnyAR ar;
-    const int rc = npub::comm_gemm_view(comm, ar);
-    if (rc) return rc;
-    return npub::w8a16_skinny_run(A, lda, Wq, ldw, scale, C, ldc, R, ldr, M, N, K, alpha, workspace, workspace_bytes,
-                                  reinterpret_cast<cudaStream_t>(stream), &ar);
 }
 
 extern "C" int npub_comm_destroy(void* comm) {

@@ -597,11 +597,9 @@ extern "C" int npub_w8a16_gemm_swiglu(const void* A, int64_t lda, const int8_t* 
     NPUB_CHECK_ARG(F <= (1 << 29));
     const int N = 2 * F;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    // the tensor-memory pair kernel has no SwiGLU epilogue: the shared-memory
-    // pair kernel serves every M > 64 here
     if (npub::w8a16_use_skinny(M, N, K))
         return npub::w8a16_skinny_run(A, lda, Wq, ldw, scale, C, ldc, nullptr, 0, M, N, K, 1.0f, workspace,
-                                      workspace_bytes, st, nullptr, 1);
+                                      workspace_bytes, st, 1);
     return npub::linear_w8a16_pair(A, lda, Wq, ldw, scale, C, ldc, nullptr, 0, M, N, K, 1.0f, workspace,
                                    workspace_bytes, st, 1);
 }

@@ -142,7 +142,7 @@ __device__ __forceinline__ Seg seg_in_order(const Range& r, int i) {
     return s;
 }
 
-template <int BT, bool AR>
+template <int BT>
 __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_constant__ SkinnyParams p) {
     pdl_trigger();
     using L = Smem<BT>;
@@ -435,16 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
             }
             tc_fence_after();
             // The finished fp32 sums of this warp's 32 rows leave through
-            // emit(): stored as fp16 (scale, residual), or, with a fused
-            // all-reduce, staged for the other ranks and stored by ar_finish().
-            constexpr bool ar = AR;
-            const int qs = 4 * sg.tile + q;  // this quarter's all-reduce slot
-            uint32_t ar_e = 0;
-            float* ar_mine = nullptr;
-            if (ar) {
-                ar_e = p.ar.epochs[qs] + 1u;
-                ar_mine = p.ar.stage[p.ar.rank] + ((size_t)(ar_e & 1u) * kArSlots + qs) * kArSlotFloats + lane * 64;
-            }
+            // emit(): scaled (+ residual) and stored as fp16, or SwiGLU pairs.
             auto emit = [&](int c0, const float (&v)[16]) {
                 if (p.swiglu) {
                     // gate row 2c and up row 2c + 1 sit in adjacent lanes: both
@@ -461,13 +452,6 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                         if (c0 + t0 + j < M) p.C[(int64_t)(c0 + t0 + j) * p.ldc + n / 2] = __float2half_rn(o[j]);
                     return;
                 }
-                if (ar) {
-#pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        st_cg_f4(reinterpret_cast<float4*>(ar_mine + c0) + j,
-                                 make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
-                    return;
-                }
                 if (!nrow) return;
                 float rv[16];
 #pragma unroll
@@ -476,68 +460,6 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
                     if (c0 + j < M) p.C[(int64_t)(c0 + j) * p.ldc + n] = __float2half_rn(v[j] * sc + rv[j]);
-            };
-            // Cross-rank step: publish the slot, wait for every rank's, sum in
-            // rank order (the same bits on every rank), scale, add, store.
-            auto ar_finish = [&]() {
-                __threadfence_system();
-                __syncwarp();
-                if (lane < p.ar.world) st_release_sys(p.ar.flags[lane] + p.ar.rank * kArSlots + qs, ar_e);
-                bool ok = true;
-                if (lane < p.ar.world) {
-                    const uint32_t* f = p.ar.flags[p.ar.rank] + lane * kArSlots + qs;
-                    ok = ld_acquire_sys(f) >= ar_e;
-                    if (!ok) {
-                        const uint64_t t0 = globaltimer_ns();
-                        for (uint32_t it = 1;; ++it) {
-                            if (ld_acquire_sys(f) >= ar_e) {
-                                ok = true;
-                                break;
-                            }
-                            if ((it & 1023u) == 0 && globaltimer_ns() - t0 > p.wait_ns) break;
-                        }
-                    }
-                }
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) set_err(p.err, 0x308);
-                const size_t off = ((size_t)(ar_e & 1u) * kArSlots + qs) * kArSlotFloats + lane * 64;
-                for (int c0 = 0; c0 < BT && c0 < M && ok; c0 += 16) {
-                    float v[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = 0.0f;
-#pragma unroll
-                    for (int r0 = 0; r0 < kArMaxRanks; r0 += 2) {
-                        if (r0 >= p.ar.world) break;
-                        uint4 u[2][4];  // two ranks' 16 columns in flight
-#pragma unroll
-                        for (int i = 0; i < 2; ++i)
-                            if (r0 + i < p.ar.world)
-#pragma unroll
-                                for (int j = 0; j < 4; ++j)
-                                    u[i][j] = ld_relaxed_sys_v4(reinterpret_cast<const uint4*>(p.ar.stage[r0 + i] + off +
-                                                                                           c0) + j);
-#pragma unroll
-                        for (int i = 0; i < 2; ++i) {
-                            if (r0 + i >= p.ar.world) break;
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                v[4 * j] += __uint_as_float(u[i][j].x);
-                                v[4 * j + 1] += __uint_as_float(u[i][j].y);
-                                v[4 * j + 2] += __uint_as_float(u[i][j].z);
-                                v[4 * j + 3] += __uint_as_float(u[i][j].w);
-                            }
-                        }
-                    }
-                    if (!nrow) continue;
-                    float rv[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        rv[j] = (p.R && c0 + j < M) ? __half2float(__ldg(p.R + (int64_t)(c0 + j) * p.ldr + n)) : 0.0f;
-#pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        if (c0 + j < M) p.C[(int64_t)(c0 + j) * p.ldc + n] = __float2half_rn(v[j] * sc + rv[j]);
-                }
-                if (lane == 0) p.ar.epochs[qs] = ar_e;
             };
             if (sg.full) {
                 for (int c0 = 0; c0 < BT && c0 < M; c0 += 16) {
@@ -548,7 +470,6 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&acc_empty[b]);
-                if (ar) ar_finish();
                 continue;
             }
             if (!finisher) {
@@ -583,7 +504,6 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[b]);
-            if (ar) ar_finish();
         }
     }
 
@@ -596,11 +516,11 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
     }
 }
 
-template <int BT, bool AR>
+template <int BT>
 static int launch(const SkinnyParams& p, int grid, cudaStream_t st) {
     using L = Smem<BT>;
     static_assert(L::kTotal <= 232448, "shared memory budget");
-    auto kern = w8a16_skinny_kernel<BT, AR>;
+    auto kern = w8a16_skinny_kernel<BT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) {
         npub_internal_set_cuda_error(e);
@@ -666,10 +586,9 @@ size_t w8a16_skinny_workspace(int M, int N, int K) {
 
 int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C, int64_t ldc,
                      const void* R, int64_t ldr, int M, int N, int K, float alpha, void* ws, size_t ws_bytes,
-                     cudaStream_t st, const SkinnyAR* ar, int swiglu) {
+                     cudaStream_t st, int swiglu) {
     if (!w8a16_skinny_fits(M, N)) return NPUB_ERR_INVALID_ARG;
-    if (swiglu && (N % 2 || R || (ar && ar->world > 1))) return NPUB_ERR_INVALID_ARG;
-    if (ar && ar->world > 1 && (N + skinny::kRows - 1) / skinny::kRows * 4 > kArSlots) return NPUB_ERR_UNSUPPORTED;
+    if (swiglu && (N % 2 || R)) return NPUB_ERR_INVALID_ARG;
     const size_t need = w8a16_skinny_workspace(M, N, K);
     if (!ws || ws_bytes < need) return NPUB_ERR_WORKSPACE;
     if (!npub_aligned(ws, 16)) return NPUB_ERR_INVALID_ARG;
@@ -698,11 +617,7 @@ int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, con
     p.wait_ns = npub_internal_wait_limit_ns();
     p.swiglu = swiglu ? 1 : 0;
     const int grid = skinny_grid(N, K);
-    if (ar && ar->world > 1) {
-        p.ar = *ar;
-        return bt == 32 ? skinny::launch<32, true>(p, grid, st) : skinny::launch<64, true>(p, grid, st);
-    }
-    return bt == 32 ? skinny::launch<32, false>(p, grid, st) : skinny::launch<64, false>(p, grid, st);
+    return bt == 32 ? skinny::launch<32>(p, grid, st) : skinny::launch<64>(p, grid, st);
 }
 
 }  // namespace npub

@@ -12,22 +12,6 @@ namespace npub {
 // Token counts up to this use the stream-K kernel (one token tile, BT = 32 or 64).
 constexpr int kSkinnyMaxM = 64;
 
-// Fused all-reduce of the result over tensor-parallel ranks (peer memory of
-// comm.cu): every rank's staging area, flags and this rank's epochs for the
-// (128-row tile, 32-row quarter) slots.  world == 0: no all-reduce.
-constexpr int kArMaxRanks = 8;
-constexpr int kArSlots = 256;                    // tile quarters: N <= 8192
-constexpr int kArSlotFloats = 32 * 64;           // 32 rows x up to 64 token columns, fp32
-struct SkinnyAR {
-    float* stage[kArMaxRanks];      // [2 halves][kArSlots][32][64] fp32 per rank
-    uint32_t* flags[kArMaxRanks];   // [world][kArSlots] per rank
-    uint32_t* epochs;               // [kArSlots], this rank
-    int world, rank;
-};
-
-// Fills `ar` from a communicator made by npub_comm_create/npub_comm_open.
-int comm_gemm_view(void* comm, SkinnyAR& ar);
-
 struct SkinnyParams {
     CUtensorMap tmW;  // int8 weights [N, K]: box {128, 128, 1}, 128-byte swizzle
     CUtensorMap tmX;  // fp16 activations [M, K]: box {64, BT, 1}, 128-byte swizzle
@@ -41,8 +25,7 @@ struct SkinnyParams {
     float* part;    // [grid][128][BT] fp32 partial tiles
     unsigned* cnt;  // [n_tiles][4] pieces arrived per tile and 32-row quarter (zero between calls)
     int* err;
-    uint64_t wait_ns;  // limit of the waits on other CTAs' pieces and other ranks' flags
-    SkinnyAR ar;
+    uint64_t wait_ns;  // limit of the waits on other CTAs' pieces
     int swiglu;     // 1: rows 2c / 2c+1 are gate / up; C [M, N/2] = fp16(silu(g) * u)
 };
 
@@ -56,6 +39,6 @@ bool w8a16_use_skinny(int M, int N, int K);
 size_t w8a16_skinny_workspace(int M, int N, int K);
 int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C, int64_t ldc,
                      const void* R, int64_t ldr, int M, int N, int K, float alpha, void* ws, size_t ws_bytes,
-                     cudaStream_t st, const SkinnyAR* ar = nullptr, int swiglu = 0);
+                     cudaStream_t st, int swiglu = 0);
 
 }  // namespace npub

@@ -402,13 +402,7 @@ def layer_decode(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, k_cache: to
 
 
 def _row_parallel(a: torch.Tensor, wq: torch.Tensor, s: torch.Tensor, tp: TP, out: torch.Tensor, mk) -> torch.Tensor:
-    """Row-parallel projection of a decode step followed by its all-reduce: one
-    fused GEMM + peer-memory reduction kernel when the shape allows, else the
-    GEMM and then TP.all_reduce."""
-    if tp.size > 1 and tp.peer is not None and tp.peer.gemm_fits(a.shape[0], wq.shape[0]):
-        tp.peer.matmul_allreduce(a, wq, s, out=out)
-        mk("all_reduce")  # fused into the GEMM
-        return out
+    """Row-parallel projection of a decode step followed by its all-reduce."""
     npu.matmul(a, wq, s, out=out)
     mk("all_reduce")
     tp.all_reduce(out)

@@ -1,6 +1,6 @@
 """Tensor-parallel Llama layer on 2, 4 and 8 GPUs (NCCL + peer all-reduce)
-against the 1-GPU layer and the float64 oracle, the peer all-reduce and the
-fused GEMM + all-reduce on 2 GPUs, and a bounded wait on a peer that gives up.
+against the 1-GPU layer and the float64 oracle, the peer all-reduce on 2
+GPUs, and a bounded wait on a peer that gives up.
 
 Each rank builds its shard of the same seeded layer (llama.make_layer with
 TP(rank, world)), runs a prefill of 2 prompts and a decode step, and rank 0
@@ -161,73 +161,6 @@ def test_peer_allreduce_2gpu():
     bits on every rank, across message sizes and from a replayed CUDA graph."""
     err, same, graph_ok = _run(_ar_worker, 2, timeout=300)
     assert err <= 1e-3, err
-    assert same
-    assert graph_ok
-
-
-def _gemm_ar_worker(rank, world, port, q):
-    import torch.distributed as dist
-    from npu_comp_b200 import comm
-    dev = _init(rank, world, port, {"NPUB_FUSED_GEMM_ALLREDUCE": "1"})
-    try:
-        peer = comm.PeerAllReduce(dist.group.WORLD, dev)
-        errs, same = [], []
-        shapes = [(32, 4096, 2048), (64, 4096, 5504), (5, 300, 1024), (32, 8192, 512)]
-        for i, (M, N, K) in enumerate(shapes * 2):
-            g = torch.Generator(device=dev).manual_seed(100 * i + rank)          # this rank's K slice
-            gs = torch.Generator(device=dev).manual_seed(100 * i + 77)           # shared by the ranks
-            A = torch.randn((M, K), generator=g, device=dev).half()
-            W = torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8)
-            s = (torch.rand(N, generator=gs, device=dev) * 1e-3 + 1e-3).half()
-            R = torch.randn((M, N), generator=gs, device=dev).half()
-            allA = [torch.empty_like(A) for _ in range(world)]
-            allW = [torch.empty_like(W) for _ in range(world)]
-            dist.all_gather(allA, A)
-            dist.all_gather(allW, W)
-            ref = sum(a.float() @ w.float().t() for a, w in zip(allA, allW)) * s.float()[None, :] * 0.5 + R.float()
-            out = torch.empty((M, N), dtype=torch.float16, device=dev)
-            peer.matmul_allreduce(A, W, s, out=out, residual=R, alpha=0.5)
-            errs.append(((out.float() - ref).abs().max() / ref.abs().max()).item())
-            got = [torch.empty_like(out) for _ in range(world)]
-            dist.all_gather(got, out)
-            same.append(all(torch.equal(got[0], o) for o in got))
-        # from a replayed CUDA graph
-        M, N, K = 32, 4096, 1024
-        g = torch.Generator(device=dev).manual_seed(rank)
-        A = torch.randn((M, K), generator=g, device=dev).half()
-        W = torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8)
-        s = torch.full((N,), 1e-3, dtype=torch.float16, device=dev)
-        out = torch.empty((M, N), dtype=torch.float16, device=dev)
-        peer.matmul_allreduce(A, W, s, out=out)
-        first = out.clone()
-        gr = torch.cuda.CUDAGraph()
-        st = torch.cuda.Stream()
-        st.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(st):
-            with torch.cuda.graph(gr, stream=st):
-                peer.matmul_allreduce(A, W, s, out=out)
-        torch.cuda.synchronize()
-        graph_ok = True
-        for _ in range(4):
-            out.zero_()
-            gr.replay()
-            torch.cuda.synchronize()
-            graph_ok &= torch.equal(out, first)
-        del gr
-        torch.cuda.synchronize()
-        dist.barrier()
-        peer.close()
-        if rank == 0:
-            q.put((max(errs), all(same), graph_ok))
-    finally:
-        dist.destroy_process_group()
-
-
-def test_fused_gemm_allreduce_2gpu():
-    """npub_w8a16_gemm_allreduce on 2 GPUs (each rank a K slice): the fp32
-    reference within TOL, the same bits on every rank, and from a graph."""
-    err, same, graph_ok = _run(_gemm_ar_worker, 2, timeout=300)
-    assert err <= TOL, err
     assert same
     assert graph_ok
 
