@@ -7,8 +7,10 @@
 //   O = P V (tcgen05 GEMM, K loop cut at the diagonal), V transposed once so
 //   both GEMM operands are K-major.
 // Decode: flash-decoding over an fp16 KV cache [batch, kv_heads, cap, 128],
-// HBM-bound; 4 lanes per key with 128-bit loads, online softmax in fp32,
-// split over the context when there are too few (sequence, head) pairs.
+// HBM-bound: a persistent kernel that balances the 64-key stages of all
+// (sequence, kv head) pairs over the resident CTAs (grouped-query groups of
+// 1, 2, 4 or 8 heads, up to 512 sequences); other groups run a split kernel
+// with 4 lanes per key and a combine pass.
 #include "common.cuh"
 #include "gemm_tc.h"
 
@@ -56,9 +58,11 @@ struct DecodeArgs {
     __half* out;
     int64_t ldo;
     int heads, kv_heads, splits, chunk;
+    int batch;
     float scale_log2;  // scale * log2(e)
-    float* part;       // [bh, splits, hd + 2] when splits > 1
+    float* part;       // split kernel: [bh, splits, hd + 2]; persistent kernel: [CTA, group, hd + 2]
     int* err;          // device error word
+    uint64_t wait_ns;  // bound of the finishers' waits
 };
 
 __device__ __forceinline__ void ld8f(const __half* p, float (&f)[8]) {
@@ -190,28 +194,63 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_attn_kernel(const Decod
     }
 }
 
-// Streaming decode attention: one CTA per (sequence, kv head, context split)
-// serves all G = heads / kv_heads query heads of the group, so a K/V row is
-// read from HBM once.  K and V of 64 consecutive keys are contiguous in the
-// cache ([cap, 128] per (sequence, kv head)), so each stage is two 16 KB bulk
-// copies (cp.async.bulk, no tensor map) into a 3-deep shared-memory ring,
-// issued by a producer warp; with two CTAs per SM that keeps ~192 KB of HBM
-// reads in flight per SM.  Each of the eight compute warps owns 8 keys of
-// every stage and keeps its own online softmax (no block barrier per stage):
+// Streaming decode attention.  One CTA serves all G = heads / kv_heads query
+// heads of a (sequence, kv head) item, so a K/V row is read from HBM once.  K
+// and V of 64 consecutive keys are contiguous in the cache ([cap, 128] per
+// (sequence, kv head)), so a stage is two 16 KB bulk copies (cp.async.bulk, no
+// tensor map) into a 3-deep shared-memory ring, issued by a producer warp;
+// with two CTAs per SM ~192 KB of HBM reads are in flight per SM.  Each of the
+// eight compute warps owns 8 keys of every stage and keeps its own online
+// softmax (no block barrier per stage):
 //   scores: a half-warp per key, 16 lanes x 8 dims, four shuffles;
 //   P V:    lane l accumulates dims [4 l, 4 l + 4) of every query head;
-// the warps release a stage through an mbarrier and are merged once at the end.
+// the warps release a stage through an mbarrier and merge through shared
+// memory at the end of an item.  Two schedules share that stage code:
+//  * many items (batch x heads >= 6 x SMs): one CTA per item, the hardware
+//    handing items to SMs as CTAs finish;
+//  * few items: a persistent grid (as many CTAs as are resident at once) over
+//    the list of 64-key stages of all items, sequence-major; CTA c takes
+//    stages [c S / G, (c + 1) S / G) of the S, so every SM streams the same
+//    number of K/V bytes whatever the batch and lengths are, and the producer
+//    runs on across item boundaries (the first stage of an item in a CTA also
+//    brings the item's query rows).  An item cut between CTAs is finished by
+//    the CTA holding its first stage (its last piece); the CTAs holding the
+//    other pieces do them first (each such piece starts their range), publish
+//    (acc, max, sum) per head and set a flag, and the finisher merges them in
+//    CTA order, so the result does not depend on timing.  Only finishers
+//    wait, only on pieces other CTAs do first, and every CTA is resident, so
+//    no wait can close a cycle.  This replaces the split-context kernel and
+//    its combine pass (measured 4-14 % faster where that needed splits).
 constexpr int kStKeys = 64;
 constexpr int kStBytes = kStKeys * kDecHd * 2;  // one of K or V per stage
 constexpr int kStStages = 3;
 constexpr int kStWarps = 8;                     // compute warps; warp 8 is the producer
 constexpr int kStKeysPerWarp = kStKeys / kStWarps;  // 8: four pairs of keys per stage
 constexpr int kStThreads = (kStWarps + 1) * 32;
+constexpr int kPsMaxSeq = 512;   // sequences whose stage prefix sums fit in shared memory
+constexpr int kPsMaxCtas = 1024;
+
+// One flag per CTA slot of the persistent kernel: set when the CTA's first
+// piece (of an item started by an earlier CTA) is published, cleared by the
+// item's finisher, so every completed call leaves them zero.
+__device__ uint32_t g_decode_piece_flag[kPsMaxCtas];
 
 template <int G>
 constexpr int stream_smem() {
     return kStStages * 2 * kStBytes + 16 * kStStages + 128;
 }
+
+template <int G>
+struct PsLayout {
+    static constexpr int kQ = G * kDecHd * 2;  // query rows of one item
+    static constexpr int kQOff = kStStages * 2 * kStBytes;
+    static constexpr int kMergeOff = kQOff + kStStages * kQ;
+    static constexpr int kPreOff = kMergeOff + kStWarps * (kDecHd + 2) * 4;
+    static constexpr int kLenOff = kPreOff + (kPsMaxSeq + 1) * 4;
+    static constexpr int kBarOff = (kLenOff + kPsMaxSeq * 4 + 7) / 8 * 8;
+    static constexpr int kAbortOff = kBarOff + 2 * kStStages * 8;
+    static constexpr int kTotal = kAbortOff + 16 + 128;  // + 128: base alignment
+};
 
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -220,8 +259,97 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                  : "memory");
 }
 
+// Barrier of the eight compute warps (the producer warp has left); the
+// non-.aligned form, since lane 0 of warp 0 may arrive from a finisher's wait.
+__device__ __forceinline__ void compute_bar() { asm volatile("barrier.sync 1, %0;" ::"n"(kStWarps * 32) : "memory"); }
+
+__device__ __forceinline__ void st_cg_f32(float* p, float v) {
+    asm volatile("st.global.cg.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
+// One 64-key stage (n valid keys): the warp's 8 keys scored against its G
+// query heads (q pre-scaled by scale * log2 e), online softmax, P V into the
+// lane's 4 dims.
 template <int G>
-__global__ void __launch_bounds__(kStThreads) decode_attn_stream_kernel(const DecodeArgs a) {
+__device__ __forceinline__ void stream_stage(const uint8_t* Ks, const uint8_t* Vs, int n, int warp, int lane,
+                                             const float (&q)[G][8], float (&m)[G], float (&l)[G],
+                                             float (&acc)[G][4]) {
+    const int hw = lane >> 4, l16 = lane & 15;
+    constexpr int NP = kStKeysPerWarp / 2;
+    // scores of keys kStKeysPerWarp warp + 2 it + hw
+    float sc[G][NP];
+#pragma unroll
+    for (int it = 0; it < NP; ++it) {
+        const int key = kStKeysPerWarp * warp + 2 * it + hw;
+        const uint4 raw = *reinterpret_cast<const uint4*>(Ks + key * (kDecHd * 2) + l16 * 16);
+        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+        float kf[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 t = __half22float2(h2[e]);
+            kf[2 * e] = t.x;
+            kf[2 * e + 1] = t.y;
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float x = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x = fmaf(q[g][e], kf[e], x);
+            x += __shfl_xor_sync(0xffffffffu, x, 8);
+            x += __shfl_xor_sync(0xffffffffu, x, 4);
+            x += __shfl_xor_sync(0xffffffffu, x, 2);
+            x += __shfl_xor_sync(0xffffffffu, x, 1);
+            sc[g][it] = key < n ? x : -INFINITY;
+        }
+    }
+    // online softmax over this warp's keys
+    float p[G][NP];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        float mx = sc[g][0];
+#pragma unroll
+        for (int it = 1; it < NP; ++it) mx = fmaxf(mx, sc[g][it]);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float mn = fmaxf(m[g], mx);
+        const float corr = (m[g] == -INFINITY) ? 0.0f : exp2f(m[g] - mn);
+        float sum = 0.0f;
+#pragma unroll
+        for (int it = 0; it < NP; ++it) {
+            p[g][it] = sc[g][it] == -INFINITY ? 0.0f : exp2f(sc[g][it] - mn);
+            sum += p[g][it];
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+        l[g] = l[g] * corr + sum;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[g][e] *= corr;
+        m[g] = mn == -INFINITY ? m[g] : mn;
+    }
+    // P V: lane owns dims 4 lane .. 4 lane + 3
+#pragma unroll
+    for (int it = 0; it < NP; ++it) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int key = kStKeysPerWarp * warp + 2 * it + hh;
+            if (key < n) {  // warp-uniform; rows past n may hold stale bytes
+                const uint2 raw = *reinterpret_cast<const uint2*>(Vs + key * (kDecHd * 2) + lane * 8);
+                const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+                const float2 v01 = __half22float2(h2[0]), v23 = __half22float2(h2[1]);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float pk = __shfl_sync(0xffffffffu, p[g][it], hh * 16);
+                    acc[g][0] = fmaf(pk, v01.x, acc[g][0]);
+                    acc[g][1] = fmaf(pk, v01.y, acc[g][1]);
+                    acc[g][2] = fmaf(pk, v23.x, acc[g][2]);
+                    acc[g][3] = fmaf(pk, v23.y, acc[g][3]);
+                }
+            }
+        }
+    }
+}
+
+// ------------------------------------------------ one CTA per (sequence, kv head)
+template <int G>
+__global__ void __launch_bounds__(kStThreads, G <= 4 ? 2 : 1) decode_attn_stream_kernel(const DecodeArgs a) {
     pdl_trigger();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
@@ -231,7 +359,7 @@ __global__ void __launch_bounds__(kStThreads) decode_attn_stream_kernel(const De
 
     const int bk = blockIdx.x;  // sequence * kv_heads + kv head
     const int b = bk / a.kv_heads, kvh = bk % a.kv_heads;
-    const int split = blockIdx.y;
+    const int split = blockIdx.y;  // context split (a.splits > 1: partials for decode_combine_kernel)
     pdl_wait();  // lens, q and the caches come from earlier kernels
     const int len = (int)min((int64_t)(a.lens ? a.lens[b] : a.ctx), a.cap);
     const int c0 = split * a.chunk;
@@ -263,8 +391,8 @@ __global__ void __launch_bounds__(kStThreads) decode_attn_stream_kernel(const De
     if (warp == kStWarps) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            const __half* kbase = a.kc + ((int64_t)b * a.kv_heads + kvh) * a.cap * kDecHd;
-            const __half* vbase = a.vc + ((int64_t)b * a.kv_heads + kvh) * a.cap * kDecHd;
+            const __half* kbase = a.kc + (((int64_t)b * a.kv_heads + kvh) * a.cap + c0) * kDecHd;
+            const __half* vbase = a.vc + (((int64_t)b * a.kv_heads + kvh) * a.cap + c0) * kDecHd;
             int i = 0;
             for (; i < nst; ++i) {
                 const int slot = i % kStStages;
@@ -273,8 +401,8 @@ __global__ void __launch_bounds__(kStThreads) decode_attn_stream_kernel(const De
                     if (a.err) atomicCAS(a.err, 0, 0x401);
                     break;
                 }
-                const int k0 = c0 + i * kStKeys;
-                const uint32_t bytes = (uint32_t)min(kStKeys, c1 - k0) * kDecHd * 2;
+                const int k0 = i * kStKeys;
+                const uint32_t bytes = (uint32_t)min(kStKeys, nkeys - k0) * kDecHd * 2;
                 mbar_arrive_expect_tx(&full[slot], 2 * bytes);
                 bulk_load(ring + slot * 2 * kStBytes, kbase + (int64_t)k0 * kDecHd, bytes, &full[slot]);
                 bulk_load(ring + slot * 2 * kStBytes + kStBytes, vbase + (int64_t)k0 * kDecHd, bytes, &full[slot]);
@@ -287,7 +415,7 @@ __global__ void __launch_bounds__(kStThreads) decode_attn_stream_kernel(const De
         }
     } else {
         // ------------------------------------------------------------ compute warps
-        const int hw = lane >> 4, l16 = lane & 15;
+        const int l16 = lane & 15;
         float q[G][8];
 #pragma unroll
         for (int g = 0; g < G; ++g) {
@@ -304,78 +432,7 @@ __global__ void __launch_bounds__(kStThreads) decode_attn_stream_kernel(const De
                 break;
             }
             const uint8_t* Ks = ring + slot * 2 * kStBytes;
-            const uint8_t* Vs = Ks + kStBytes;
-            const int n = min(kStKeys, c1 - (c0 + i * kStKeys));
-            // scores of keys kStKeysPerWarp warp + 2 it + hw
-            constexpr int NP = kStKeysPerWarp / 2;
-            float sc[G][NP];
-#pragma unroll
-            for (int it = 0; it < NP; ++it) {
-                const int key = kStKeysPerWarp * warp + 2 * it + hw;
-                const uint4 raw = *reinterpret_cast<const uint4*>(Ks + key * (kDecHd * 2) + l16 * 16);
-                const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
-                float kf[8];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 t = __half22float2(h2[e]);
-                    kf[2 * e] = t.x;
-                    kf[2 * e + 1] = t.y;
-                }
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    float x = 0.0f;
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) x = fmaf(q[g][e], kf[e], x);
-                    x += __shfl_xor_sync(0xffffffffu, x, 8);
-                    x += __shfl_xor_sync(0xffffffffu, x, 4);
-                    x += __shfl_xor_sync(0xffffffffu, x, 2);
-                    x += __shfl_xor_sync(0xffffffffu, x, 1);
-                    sc[g][it] = key < n ? x : -INFINITY;
-                }
-            }
-            // online softmax over this warp's keys
-            float p[G][NP];
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                float mx = sc[g][0];
-#pragma unroll
-                for (int it = 1; it < NP; ++it) mx = fmaxf(mx, sc[g][it]);
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                const float mn = fmaxf(m[g], mx);
-                const float corr = (m[g] == -INFINITY) ? 0.0f : exp2f(m[g] - mn);
-                float sum = 0.0f;
-#pragma unroll
-                for (int it = 0; it < NP; ++it) {
-                    p[g][it] = sc[g][it] == -INFINITY ? 0.0f : exp2f(sc[g][it] - mn);
-                    sum += p[g][it];
-                }
-                sum += __shfl_xor_sync(0xffffffffu, sum, 16);
-                l[g] = l[g] * corr + sum;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) acc[g][e] *= corr;
-                m[g] = mn == -INFINITY ? m[g] : mn;
-            }
-            // P V: lane owns dims 4 lane .. 4 lane + 3
-#pragma unroll
-            for (int it = 0; it < NP; ++it) {
-#pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    const int key = kStKeysPerWarp * warp + 2 * it + hh;
-                    if (key < n) {  // warp-uniform; rows past n may hold stale bytes
-                        const uint2 raw = *reinterpret_cast<const uint2*>(Vs + key * (kDecHd * 2) + lane * 8);
-                        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
-                        const float2 v01 = __half22float2(h2[0]), v23 = __half22float2(h2[1]);
-#pragma unroll
-                        for (int g = 0; g < G; ++g) {
-                            const float pk = __shfl_sync(0xffffffffu, p[g][it], hh * 16);
-                            acc[g][0] = fmaf(pk, v01.x, acc[g][0]);
-                            acc[g][1] = fmaf(pk, v01.y, acc[g][1]);
-                            acc[g][2] = fmaf(pk, v23.x, acc[g][2]);
-                            acc[g][3] = fmaf(pk, v23.y, acc[g][3]);
-                        }
-                    }
-                }
-            }
+            stream_stage<G>(Ks, Ks + kStBytes, min(kStKeys, nkeys - i * kStKeys), warp, lane, q, m, l, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
@@ -436,6 +493,354 @@ static int launch_stream(const DecodeArgs& a, int batch, int kv_heads, int split
         return NPUB_ERR_CUDA;
     }
     return launch_pdl(kern, dim3(batch * kv_heads, splits), dim3(kStThreads), smem, st, a);
+}
+
+// ------------------------------------------------ persistent grid over the stage list
+// Position in the stage list: sequence b, kv head h, stage s of the item's n.
+struct PsCursor {
+    int b, h, s, n;
+};
+
+// pre[b] = kv_heads * (stages of sequences < b); f < pre[batch].
+__device__ __forceinline__ PsCursor ps_locate(int f, const int* pre, int batch, int kvh) {
+    int lo = 0, hi = batch - 1;  // the last b with pre[b] <= f (its item count is non-zero)
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (pre[mid] <= f) lo = mid;
+        else hi = mid - 1;
+    }
+    PsCursor c;
+    c.b = lo;
+    c.n = (pre[lo + 1] - pre[lo]) / kvh;
+    const int off = f - pre[lo];
+    c.h = off / c.n;
+    c.s = off - c.h * c.n;
+    return c;
+}
+
+__device__ __forceinline__ void ps_advance(PsCursor& c, const int* pre, int batch, int kvh) {
+    if (++c.s < c.n) return;
+    c.s = 0;
+    if (++c.h < kvh) return;
+    c.h = 0;
+    do {
+        ++c.b;
+    } while (c.b < batch && pre[c.b + 1] == pre[c.b]);
+    if (c.b < batch) c.n = (pre[c.b + 1] - pre[c.b]) / kvh;
+}
+
+// CTA cc of nctas has no stages (more CTAs than stages): it publishes nothing.
+__device__ __forceinline__ bool ps_empty(int cc, int S, int nctas) {
+    return (int64_t)cc * S / nctas == (int64_t)(cc + 1) * S / nctas;
+}
+
+template <int G>
+__global__ void __launch_bounds__(kStThreads, G >= 8 ? 1 : 2) decode_attn_persist_kernel(const DecodeArgs a) {
+    using L = PsLayout<G>;
+    pdl_trigger();
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    uint8_t* ring = base;
+    const uint8_t* qarea = base + L::kQOff;
+    float* mg = reinterpret_cast<float*>(base + L::kMergeOff);  // [warp][130]: acc[128], m, l of one head
+    int* pre = reinterpret_cast<int*>(base + L::kPreOff);
+    int* lens = reinterpret_cast<int*>(base + L::kLenOff);
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + L::kBarOff);
+    uint64_t* empty = full + kStStages;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(base + L::kAbortOff);
+    static_assert(L::kTotal <= 227 * 1024, "shared memory budget");
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int batch = a.batch, kvh = a.kv_heads;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kStWarps);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    pdl_wait();  // lens, q and the caches come from earlier kernels
+    if (warp == 0) {
+        int carry = 0;
+        for (int b0 = 0; b0 < batch; b0 += 32) {
+            const int b = b0 + lane;
+            int n = 0;
+            if (b < batch) {
+                int64_t len = a.lens ? (int64_t)a.lens[b] : (int64_t)a.ctx;
+                len = len < 0 ? 0 : (len > a.cap ? a.cap : len);
+                lens[b] = (int)len;
+                n = (int)((len + kStKeys - 1) / kStKeys) * kvh;
+            }
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, n, o);
+                if (lane >= o) n += y;
+            }
+            if (b < batch) pre[b + 1] = carry + n;
+            carry += __shfl_sync(0xffffffffu, n, 31);
+        }
+        if (lane == 0) pre[0] = 0;
+    }
+    __syncthreads();
+    const int S = pre[batch];
+    const int c = blockIdx.x, nctas = gridDim.x;
+    const int f0 = (int)((int64_t)c * S / nctas), f1 = (int)((int64_t)(c + 1) * S / nctas);
+    const bool any_empty = S < nctas;  // else every CTA has at least one stage
+
+    if (warp == kStWarps) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0 && f0 < f1) {
+            PsCursor cu = ps_locate(f0, pre, batch, kvh);
+            int i = 0;
+            for (int f = f0; f < f1; ++f, ++i) {
+                const int slot = i % kStStages;
+                if (i >= kStStages &&
+                    !mbar_wait_bounded(&empty[slot], ((uint32_t)(i / kStStages) & 1u) ^ 1u, abort_flag)) {
+                    if (a.err) atomicCAS(a.err, 0, 0x401);
+                    break;
+                }
+                const bool qload = i == 0 || cu.s == 0;
+                const int k0 = cu.s * kStKeys;
+                const uint32_t bytes = (uint32_t)min(kStKeys, lens[cu.b] - k0) * kDecHd * 2;
+                const int64_t kv = (((int64_t)cu.b * kvh + cu.h) * a.cap + k0) * kDecHd;
+                mbar_arrive_expect_tx(&full[slot], 2 * bytes + (qload ? (uint32_t)L::kQ : 0u));
+                bulk_load(ring + slot * 2 * kStBytes, a.kc + kv, bytes, &full[slot]);
+                bulk_load(ring + slot * 2 * kStBytes + kStBytes, a.vc + kv, bytes, &full[slot]);
+                if (qload)
+                    bulk_load(base + L::kQOff + slot * L::kQ, a.q + (int64_t)cu.b * a.ldq + (int64_t)cu.h * G * kDecHd,
+                              (uint32_t)L::kQ, &full[slot]);
+                ps_advance(cu, pre, batch, kvh);
+            }
+            // every copy issued has landed before the ring is reused or the CTA exits
+            int never = 0;
+            for (int j = i - kStStages < 0 ? 0 : i - kStStages; j < i; ++j)
+                if (!mbar_wait_bounded(&full[j % kStStages], (uint32_t)(j / kStStages) & 1u, &never, 200000000ull) &&
+                    a.err)
+                    atomicCAS(a.err, 0, 0x402);
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------- compute warps
+    const int ct = threadIdx.x;  // 0 .. 255
+    const int l16 = lane & 15;
+    float q[G][8], m[G], l[G], acc[G][4];
+    if (f0 < f1) {
+        PsCursor cu = ps_locate(f0, pre, batch, kvh);
+        for (int f = f0, i = 0; f < f1; ++f, ++i) {
+            const int slot = i % kStStages;
+            const bool good =
+                __all_sync(0xffffffffu, mbar_wait_bounded(&full[slot], (uint32_t)(i / kStStages) & 1u, abort_flag));
+            if (!good && lane == 0) {
+                if (a.err) atomicCAS(a.err, 0, 0x403);
+                *abort_flag = 1;
+            }
+            const uint8_t* Ks = ring + slot * 2 * kStBytes;
+            const uint8_t* Vs = Ks + kStBytes;
+            if (i == 0 || cu.s == 0) {
+                // a new piece: the item's query rows came with this stage
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    m[g] = -INFINITY;
+                    l[g] = 0.0f;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) acc[g][e] = 0.0f;
+                    const uint4 raw =
+                        good ? *reinterpret_cast<const uint4*>(qarea + slot * L::kQ + g * kDecHd * 2 + l16 * 16)
+                             : make_uint4(0, 0, 0, 0);
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 t = __half22float2(h2[e]);
+                        q[g][2 * e] = t.x * a.scale_log2;
+                        q[g][2 * e + 1] = t.y * a.scale_log2;
+                    }
+                }
+            }
+            if (good) stream_stage<G>(Ks, Vs, min(kStKeys, lens[cu.b] - cu.s * kStKeys), warp, lane, q, m, l, acc);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+
+            if (cu.s == cu.n - 1 || f == f1 - 1) {
+                // ---------------------------------------- end of this CTA's piece of the item
+                // (every compute warp takes this branch at the same stage)
+                const int is = pre[cu.b] + cu.h * cu.n, ie = is + cu.n;
+                const bool has_first = is >= f0, has_last = ie <= f1;
+                const int c_last = has_last ? c : (int)(((int64_t)ie * nctas - 1) / S);  // owner of stage ie - 1
+                if (has_first && !has_last) {
+                    // the finisher: the later pieces were each their CTA's first
+                    // work; their flags are polled by all compute threads at once
+                    const uint64_t t0 = globaltimer_ns();
+                    for (int cc = c + 1 + ct; cc <= c_last; cc += kStWarps * 32) {
+                        if (any_empty && ps_empty(cc, S, nctas)) continue;
+                        uint32_t it = 0;
+                        while (ld_acquire_gpu(&g_decode_piece_flag[cc]) == 0u) {
+                            if ((++it & 255u) == 0 && (*abort_flag || globaltimer_ns() - t0 > a.wait_ns)) {
+                                if (a.err) atomicCAS(a.err, 0, 0x405);
+                                *abort_flag = 1;
+                                break;
+                            }
+                        }
+                        if (*abort_flag) break;
+                    }
+                    __threadfence();
+                }
+                // the warps' partial softmax states, merged per head through
+                // shared memory (threads 0..127: one head dimension each)
+                float oM[G], oL[G], oA[G];
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float* row = mg + warp * (kDecHd + 2);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) row[4 * lane + e] = acc[g][e];
+                    if (lane == 0) {
+                        row[kDecHd] = m[g];
+                        row[kDecHd + 1] = l[g];
+                    }
+                    compute_bar();
+                    oM[g] = -INFINITY;
+                    oL[g] = oA[g] = 0.0f;
+                    if (ct < kDecHd) {
+#pragma unroll
+                        for (int w = 0; w < kStWarps; ++w) oM[g] = fmaxf(oM[g], mg[w * (kDecHd + 2) + kDecHd]);
+#pragma unroll
+                        for (int w = 0; w < kStWarps; ++w) {
+                            const float* r = mg + w * (kDecHd + 2);
+                            const float cf = r[kDecHd] == -INFINITY ? 0.0f : exp2f(r[kDecHd] - oM[g]);
+                            oL[g] += r[kDecHd + 1] * cf;
+                            oA[g] += r[ct] * cf;
+                        }
+                    }
+                    compute_bar();
+                }
+                if (!has_first) {
+                    // a later piece: publish (acc, max, sum) per head, then the flag
+                    if (ct < kDecHd) {
+#pragma unroll
+                        for (int g = 0; g < G; ++g) {
+                            float* pp = a.part + ((int64_t)c * G + g) * (kDecHd + 2);
+                            st_cg_f32(pp + ct, oA[g]);
+                            if (ct == 0) {
+                                st_cg_f32(pp + kDecHd, oM[g]);
+                                st_cg_f32(pp + kDecHd + 1, oL[g]);
+                            }
+                        }
+                    }
+                    __threadfence();
+                    compute_bar();
+                    if (ct == 0) atomicExch(&g_decode_piece_flag[c], 1u);
+                } else {
+                    if (!has_last) {
+                        // the finisher (this was the CTA's last stage, so the ring is
+                        // idle): the later pieces are copied into it in chunks by all
+                        // compute threads, then merged in CTA order
+                        float* stg = reinterpret_cast<float*>(ring);
+                        constexpr int kPiece = G * (kDecHd + 2);
+                        constexpr int kChunk = kStStages * 2 * kStBytes / (kPiece * 4);
+                        static_assert(kPiece % 2 == 0, "pieces are copied as float2");
+                        for (int cc0 = c + 1; cc0 <= c_last; cc0 += kChunk) {
+                            const int np = min(kChunk, c_last - cc0 + 1);
+                            // 8-byte loads, eight in flight per thread (kPiece is even and
+                            // the workspace 256-byte aligned)
+                            const float2* src = reinterpret_cast<const float2*>(a.part + (int64_t)cc0 * kPiece);
+                            float2* dst = reinterpret_cast<float2*>(stg);
+                            const int n2 = np * kPiece / 2;
+                            for (int x0 = ct; x0 < n2; x0 += 8 * kStWarps * 32) {
+                                float2 v[8];
+#pragma unroll
+                                for (int u = 0; u < 8; ++u) {
+                                    const int x = x0 + u * kStWarps * 32;
+                                    v[u] = x < n2 ? __ldcg(src + x) : make_float2(0.0f, 0.0f);
+                                }
+#pragma unroll
+                                for (int u = 0; u < 8; ++u) {
+                                    const int x = x0 + u * kStWarps * 32;
+                                    if (x < n2) dst[x] = v[u];
+                                }
+                            }
+                            if (any_empty) {
+                                // CTAs without stages published nothing: neutral pieces
+                                __syncwarp();
+                                compute_bar();
+                                for (int x = ct; x < np * kPiece; x += kStWarps * 32)
+                                    if (ps_empty(cc0 + x / kPiece, S, nctas))
+                                        stg[x] = (x % (kDecHd + 2)) == kDecHd ? -INFINITY : 0.0f;
+                            }
+                            compute_bar();
+                            if (ct < kDecHd) {
+                                for (int pc = 0; pc < np; ++pc) {
+#pragma unroll
+                                    for (int g = 0; g < G; ++g) {
+                                        const float* r = stg + pc * kPiece + g * (kDecHd + 2);
+                                        const float mo = r[kDecHd];
+                                        const float Mn = fmaxf(oM[g], mo);
+                                        if (Mn == -INFINITY) continue;
+                                        const float c0 = oM[g] == -INFINITY ? 0.0f : exp2f(oM[g] - Mn);
+                                        const float c1 = mo == -INFINITY ? 0.0f : exp2f(mo - Mn);
+                                        oL[g] = oL[g] * c0 + r[kDecHd + 1] * c1;
+                                        oA[g] = oA[g] * c0 + r[ct] * c1;
+                                        oM[g] = Mn;
+                                    }
+                                }
+                            }
+                            compute_bar();
+                        }
+                        if (ct == 0)
+                            for (int cc = c + 1; cc <= c_last; ++cc) g_decode_piece_flag[cc] = 0u;  // left zero
+                    }
+                    if (ct < kDecHd) {
+#pragma unroll
+                        for (int g = 0; g < G; ++g)
+                            a.out[(int64_t)cu.b * a.ldo + (int64_t)(cu.h * G + g) * kDecHd + ct] =
+                                __float2half_rn(oL[g] > 0.0f ? oA[g] / oL[g] : 0.0f);
+                    }
+                }
+            }
+            ps_advance(cu, pre, batch, kvh);
+        }
+    }
+    // sequences without keys: rows of zeros
+    for (int b = c; b < batch; b += nctas)
+        if (lens[b] == 0)
+            for (int x = ct; x < a.heads * kDecHd; x += kStWarps * 32)
+                a.out[(int64_t)b * a.ldo + x] = __float2half_rn(0.0f);
+}
+
+template <int G>
+static int ps_occupancy() {
+    static int occ = 0;
+    if (occ == 0) {
+        int o = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, decode_attn_persist_kernel<G>, kStThreads,
+                                                          PsLayout<G>::kTotal) != cudaSuccess ||
+            o <= 0) {
+            cudaGetLastError();
+            o = 1;
+        }
+        occ = o;
+    }
+    return occ;
+}
+
+// Grid: every CTA resident at once (the finishers wait on other CTAs), and at
+// least ~4 stages per CTA.
+static int ps_max_ctas() { return min(kPsMaxCtas, num_sms() * 2); }
+
+template <int G>
+static int launch_persist(DecodeArgs a, int64_t stages_max, size_t workspace_bytes, cudaStream_t st) {
+    auto kern = decode_attn_persist_kernel<G>;
+    constexpr int smem = PsLayout<G>::kTotal;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) {
+        npub_internal_set_cuda_error(e);
+        return NPUB_ERR_CUDA;
+    }
+    int64_t grid = (int64_t)num_sms() * ps_occupancy<G>();
+    grid = min(grid, (int64_t)ps_max_ctas());
+    grid = min(grid, max((int64_t)1, (stages_max + 3) / 4));
+    if ((size_t)grid * G * (kDecHd + 2) * sizeof(float) > workspace_bytes || !a.part) return NPUB_ERR_WORKSPACE;
+    return launch_pdl(kern, dim3((unsigned)grid), dim3(kStThreads), smem, st, a);
 }
 
 __global__ void decode_combine_kernel(const float* __restrict__ part, int splits, int heads, __half* __restrict__ out,
@@ -607,9 +1012,12 @@ extern "C" int npub_attention_prefill(const void* q, int64_t ldq, const void* k,
 }
 
 extern "C" size_t npub_attention_decode_workspace(int batch, int heads, int ctx_len, int head_dim) {
-    if (batch <= 0 || heads <= 0 || ctx_len <= 0 || head_dim != kDecHd) return 0;
-    const int s = decode_splits(batch * heads, ctx_len);
-    return s > 1 ? (size_t)batch * heads * s * (kDecHd + 2) * sizeof(float) : 0;
+    if (batch <= 0 || heads <= 0 || head_dim != kDecHd) return 0;
+    // the persistent kernel's published pieces (group <= 8) or the split kernel's partials
+    const size_t ps = (size_t)ps_max_ctas() * (heads < 8 ? heads : 8) * (kDecHd + 2) * sizeof(float);
+    const int s = ctx_len > 0 ? decode_splits(batch * heads, ctx_len) : 1;
+    const size_t split = s > 1 ? (size_t)batch * heads * s * (kDecHd + 2) * sizeof(float) : 0;
+    return ps > split ? ps : split;
 }
 
 extern "C" int npub_attention_decode(const void* q, int64_t ldq, const void* k_cache, const void* v_cache, int64_t cap,
@@ -642,15 +1050,36 @@ extern "C" int npub_attention_decode(const void* q, int64_t ldq, const void* k_c
     a.chunk = (ctx_max + splits - 1) / splits;
     a.scale_log2 = scale * 1.4426950408889634f;
     a.part = nullptr;
+    a.batch = batch;
+    a.err = npub_internal_device_error_word();
+    a.wait_ns = npub_internal_wait_limit_ns();
+    const int group = heads / kv_heads;
+    const int64_t items = (int64_t)batch * kv_heads;
+    const bool streaming = group == 1 || group == 2 || group == 4 || group == 8;
+    // Schedules, by the number of (sequence, kv head) items (measured on B200):
+    //  * >= 6 per SM: one streaming CTA per item;
+    //  * 32 .. 6 per SM: the persistent grid over the stage list (4-24 % faster
+    //    than context splits and a combine pass there);
+    //  * fewer: one streaming CTA per (item, context split) and a combine pass
+    //    (a persistent finisher would merge ~40 pieces one after another).
+    if (streaming && items < 6LL * num_sms() && items >= 32 && batch <= kPsMaxSeq &&
+        items * ((cap + kStKeys - 1) / kStKeys) < 0x7fffffffLL) {
+        a.part = reinterpret_cast<float*>(workspace);
+        const int64_t stages = items * (((ctx_len > 0 ? (int64_t)ctx_len : cap) + kStKeys - 1) / kStKeys);
+        switch (group) {
+            case 1: return launch_persist<1>(a, stages, workspace_bytes, st);
+            case 2: return launch_persist<2>(a, stages, workspace_bytes, st);
+            case 4: return launch_persist<4>(a, stages, workspace_bytes, st);
+            default: return launch_persist<8>(a, stages, workspace_bytes, st);
+        }
+    }
     if (splits > 1) {
         const size_t need = (size_t)bh * splits * (kDecHd + 2) * sizeof(float);
         if (!workspace || workspace_bytes < need) return NPUB_ERR_WORKSPACE;
         a.part = reinterpret_cast<float*>(workspace);
     }
-    a.err = npub_internal_device_error_word();
-    const int group = heads / kv_heads;
     int rc;
-    if (group == 1 || group == 2 || group == 4 || group == 8) {
+    if (streaming) {
         switch (group) {
             case 1: rc = launch_stream<1>(a, batch, kv_heads, splits, st); break;
             case 2: rc = launch_stream<2>(a, batch, kv_heads, splits, st); break;
@@ -664,6 +1093,19 @@ extern "C" int npub_attention_decode(const void* q, int64_t ldq, const void* k_c
     if (rc || splits == 1) return rc;
     return launch_pdl(decode_combine_kernel, dim3(bh), dim3(kDecHd), 0, st, (const float*)a.part, splits, heads,
                       a.out, ldo);
+}
+
+// Clears the persistent decode kernel's piece flags (a finisher whose wait
+// gave up leaves them set).
+int npub_internal_decode_flags_reset() {
+    const uint32_t zero[kPsMaxCtas] = {};
+    cudaError_t e = cudaMemcpyToSymbol(g_decode_piece_flag, zero, sizeof(zero));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        npub_internal_set_cuda_error(e);
+        return NPUB_ERR_CUDA;
+    }
+    return NPUB_OK;
 }
 
 extern "C" int npub_kv_append(const void* k_new, int64_t ldk, const void* v_new, int64_t ldv, void* k_cache,

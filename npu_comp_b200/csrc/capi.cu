@@ -95,7 +95,9 @@ extern "C" int npub_device_error(int clear) {
         // A stream-K call whose wait gave up may have left counts in its tile
         // counters; the library's own (allocation-free) scratch is reset
         // here, a caller's workspace by its owner.
-        const int rc = npub_internal_noalloc_reset();
+        int rc = npub_internal_noalloc_reset();
+        if (rc != NPUB_OK) return rc;
+        rc = npub_internal_decode_flags_reset();  // the decode attention finishers' piece flags
         if (rc != NPUB_OK) return rc;
     }
     return v;

@@ -36,6 +36,8 @@ uint64_t npub_internal_wait_limit_ns();
 // Re-zeroes the allocation-free entry point's tile counters on the current
 // device (after a wait gave up, they may hold counts of the aborted call).
 int npub_internal_noalloc_reset();
+// Re-zeroes the persistent decode attention's piece flags on the current device.
+int npub_internal_decode_flags_reset();
 
 static inline bool npub_aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 

@@ -74,6 +74,45 @@ def test_decode_attention(cuda_device, rng, B, H, KV, ctx, cap):
     assert ref.rel_err(o, ref.decode_attention_ref(q, kc, vc, lens, H, KV, hd)) <= TOL
 
 
+@pytest.mark.parametrize("B,H,KV,ctx,cap,lens", [
+    (4, 32, 32, 4096, 4096, [1, 1, 1, 1]),          # persistent: far fewer stages than CTAs
+    (5, 8, 8, 300, 320, [0, 300, 0, 64, 65]),       # persistent: sequences without keys give zeros
+    (1, 32, 32, 16384, 16384, [16384]),             # persistent: each item cut into ~9 pieces
+    (8, 64, 8, 4000, 4000, [4000, 1, 64, 65, 3999, 128, 2, 700]),  # persistent, groups of 8
+    (1, 32, 8, 32768, 32768, [32768]),              # few items: context splits + combine
+    (2, 64, 8, 20000, 20000, [20000, 1]),           # the same, groups of 8
+    (520, 8, 8, 70, 72, None),                      # many items: one CTA per (sequence, kv head)
+    (900, 8, 1, 100, 128, "with-empty"),            # the same with groups of 8 and empty sequences
+])
+def test_decode_attention_work_split(cuda_device, rng, B, H, KV, ctx, cap, lens):
+    """The three schedules of the streaming kernel (persistent grid over the
+    stage list with items cut between CTAs, CTAs without stages and sequences
+    without keys; context splits and a combine pass; one CTA per item) match
+    the oracle, and a second call on new data (the piece flags left zero)
+    does too."""
+    hd = 128
+    if lens is None:
+        lens = rng.integers(1, ctx + 1, B)
+    elif lens == "with-empty":
+        lens = rng.integers(1, ctx + 1, B) * (rng.random(B) > 0.1)
+    lens = np.asarray(lens, dtype=np.int32)
+    kc = torch.empty((B, KV, cap, hd), dtype=torch.float16, device=cuda_device)
+    vc = torch.empty_like(kc)
+    for rep in range(2):
+        q = rng.standard_normal((B, H * hd)).astype(np.float16)
+        kh = rng.standard_normal((B, KV, cap, hd)).astype(np.float16)
+        vh = rng.standard_normal((B, KV, cap, hd)).astype(np.float16)
+        kc.copy_(torch.from_numpy(kh))
+        vc.copy_(torch.from_numpy(vh))
+        o = nb.attention_decode(dev(q, cuda_device), kc, vc, heads=H, kv_heads=KV, lens=dev(lens, cuda_device),
+                                ctx_len=ctx).float().cpu().numpy()
+        assert nb.npu.device_error() == 0
+        live = lens > 0
+        assert not o[~live].any()
+        r = ref.decode_attention_ref(q[live], kh[live], vh[live], lens[live], H, KV, hd)
+        assert ref.rel_err(o[live], r) <= TOL
+
+
 def test_decode_matches_last_prefill_row(cuda_device, rng):
     """Decode of token T over a cache of T keys == row T of causal prefill over T+1 tokens."""
     T, H, hd = 97, 4, 128
