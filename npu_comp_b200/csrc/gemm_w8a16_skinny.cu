@@ -202,22 +202,13 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
     const uint32_t tmem = *tmem_slot;
     int never = 0;
     volatile int* no_abort = &never;
-    if (warp == 3 && lane == 0) {
-        // the first weight tiles go to L2 while the previous kernel finishes
-        // (an otherwise idle warp, so the producer's first load is not held up)
-        uint32_t n = 0;
-        for (int i = 0; i < rg.nseg && n < (uint32_t)kS8; ++i) {
-            const Seg sg = seg_in_order(rg, i);
-            for (int j = 0; j < sg.nk && n < (uint32_t)kS8; ++j, ++n)
-                for (int c = 0; c < kBK / kBox8; ++c)
-                    tma_prefetch_3d(&p.tmW, (sg.k0 + j) * kBK + c * kBox8, sg.tile * kRows, 0);
-        }
-    }
     // The weight producer, the converters and the MMA issuer touch only the
     // weights (never written by an earlier kernel), shared and tensor memory:
     // they start while the previous kernel finishes (measured: 1.7 % off a
-    // batch-32 decode layer, 2 % off the stack's decode).  The token producer
-    // and the epilogue (activations, residual, workspace) wait for it.
+    // batch-32 decode layer, 2 % off the stack's decode; holding the ring's
+    // later stages back until the previous kernel is done costs 0.5-1.5 %,
+    // while an extra L2 prefetch of the first tiles cost 0.3 %).  The token
+    // producer and the epilogue (activations, residual, workspace) wait for it.
     if (warp == 0 || warp == 2) {
         // ------------------------------------------------------------ producers
         if (lane == 0) {
