@@ -94,6 +94,26 @@ size_t npub_w8a16_gemm_workspace(int M, int N, int K);
  * as npub_w8a16_gemm for (M, 2F, K). */
 int npub_w8a16_gemm_swiglu(const void* A, int64_t lda, const int8_t* Wq, int64_t ldw, const void* scale, void* C,
                            int64_t ldc, int M, int F, int K, void* workspace, size_t workspace_bytes, void* stream);
+/* W8A16 GEMM of a decode step (M <= 64, the stream-K kernel) with an RMSNorm
+ * folded in, replacing the RMSNorm -> projection pairs of llama_layer.py:79-89
+ * -> 95-113 and :139-141 -> 143-150 (legalize.py:30-47 for the norm):
+ *   consumer (rs_part != NULL): A = fp16(h * gamma) for a residual stream h and
+ *     row t of the result is scaled by 1 / sqrt(sum_{i<rs_n} rs_part[i*rs_ld + t] / rs_d + rs_eps)
+ *     before rounding (and before SwiGLU when swiglu != 0; C is then [M, N/2]);
+ *   producer (G, ss != NULL): C = fp16(A Wq^T * scale + R) as npub_w8a16_gemm,
+ *     plus G = fp16(C * gamma) [M, N] and ss[(n/32)*ss_ld + t] = sum of C[t, n]^2
+ *     over the 32 columns n/32 -- the rs_part (rs_n = N / 32) of the next call.
+ * npub_rmsnorm_parts() makes G and ss for a stream that no GEMM produced.
+ * Returns NPUB_ERR_UNSUPPORTED for M > 64.  Workspace:
+ * npub_w8a16_gemm_rms_workspace(M, N, K) bytes whose first 64 KiB are zero
+ * before the first call (every call leaves them zero). */
+int npub_w8a16_gemm_rms(const void* A, int64_t lda, const int8_t* Wq, int64_t ldw, const void* scale, void* C,
+                        int64_t ldc, const void* R, int64_t ldr, int M, int N, int K, int swiglu,
+                        const float* rs_part, int rs_n, int64_t rs_ld, int rs_d, float rs_eps, const void* gamma,
+                        void* G, int64_t ldg, float* ss, int64_t ss_ld, void* workspace, size_t workspace_bytes,
+                        void* stream);
+size_t npub_w8a16_gemm_rms_workspace(int M, int N, int K);
+
 /* Name of the kernel npub_w8a16_gemm runs for this shape (static storage):
  * the 2-CTA pair kernel, or the stream-K kernel for decode-sized M.  No
  * reference counterpart (diagnostics). */
@@ -138,6 +158,11 @@ int npub_quantize_w8(const float* W, int64_t ldw, int K, int N, int8_t* Wq, int6
  * to `x_out` (fp16, may alias x) -- the residual add of llama_layer.py:139. */
 int npub_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr, void* x_out, int64_t ldxo,
                  const void* gamma, void* y, int64_t ldy, int rows, int d, float eps, void* stream);
+
+/* The inputs npub_w8a16_gemm_rms takes for an RMSNorm of x (fp16 [rows, d],
+ * d % 32 == 0): G = fp16(x * gamma) and ss[c*ss_ld + r] = sum_{j<32} x[r, 32c + j]^2. */
+int npub_rmsnorm_parts(const void* x, int64_t ldx, const void* gamma, void* G, int64_t ldg, float* ss,
+                       int64_t ss_ld, int rows, int d, void* stream);
 
 /* Residual add, the v_add of b_program_examples/llama_layer.py:139,152:
  *   out = fp16(a + b)  (fp32 add), a, b, out fp16 [rows, cols] (out may alias a or b). */

@@ -604,6 +604,52 @@ extern "C" int npub_w8a16_gemm_swiglu(const void* A, int64_t lda, const int8_t* 
                                    workspace_bytes, st, 1);
 }
 
+// W8A16 GEMM of a decode step with an RMSNorm folded in (the stream-K
+// kernel; M <= 64).  Replaces the pair RMSNorm -> GEMM of the decode layer
+// (llama_layer.py:71-152 runs them as separate programs):
+//   consumer: A = fp16(h * gamma) of the residual stream h, and row t of the
+//     result is scaled by rsqrt(sum_{i < rs_n} rs_part[i rs_ld + t] / rs_d + eps);
+//   producer: C = fp16(A Wq^T * scale + R) as npub_w8a16_gemm, plus
+//     G = fp16(C * gamma) and the sums of C^2 over every 32 output columns
+//     (ss[(n / 32) ss_ld + t]) for the next GEMM to consume.
+extern "C" size_t npub_w8a16_gemm_rms_workspace(int M, int N, int K) {
+    return npub::w8a16_skinny_workspace(M, N, K);
+}
+
+extern "C" int npub_w8a16_gemm_rms(const void* A, int64_t lda, const int8_t* Wq, int64_t ldw, const void* scale,
+                                   void* C, int64_t ldc, const void* R, int64_t ldr, int M, int N, int K, int swiglu,
+                                   const float* rs_part, int rs_n, int64_t rs_ld, int rs_d, float rs_eps,
+                                   const void* gamma, void* G, int64_t ldg, float* ss, int64_t ss_ld,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+    NPUB_CHECK_ARG(M >= 0 && N >= 0 && K >= 0);
+    if (M == 0 || N == 0) return NPUB_OK;
+    if (!npub::w8a16_skinny_fits(M, N)) return NPUB_ERR_UNSUPPORTED;
+    NPUB_CHECK_ARG(A && Wq && C);
+    NPUB_CHECK_ARG(K % 16 == 0 && K > 0);
+    NPUB_CHECK_ARG(lda >= K && lda % 8 == 0 && npub_aligned(A, 16));
+    NPUB_CHECK_ARG(ldw >= K && ldw % 16 == 0 && npub_aligned(Wq, 16));
+    NPUB_CHECK_ARG(ldc >= (swiglu ? N / 2 : N));
+    NPUB_CHECK_ARG(!swiglu || (N % 2 == 0 && !R && !G && !ss));
+    NPUB_CHECK_ARG(!R || ldr >= N);
+    NPUB_CHECK_ARG(!rs_part || (rs_n > 0 && rs_ld >= M && rs_d > 0));
+    NPUB_CHECK_ARG(!G || (gamma && ldg >= N));
+    NPUB_CHECK_ARG(!ss || (N % 32 == 0 && ss_ld >= M));
+    npub::SkinnyNorm nrm;
+    memset(&nrm, 0, sizeof(nrm));
+    nrm.rs_part = rs_part;
+    nrm.rs_n = rs_n;
+    nrm.rs_ld = rs_ld;
+    nrm.rs_d = (float)rs_d;
+    nrm.rs_eps = rs_eps;
+    nrm.gamma = reinterpret_cast<const __half*>(gamma);
+    nrm.G = reinterpret_cast<__half*>(G);
+    nrm.ldg = ldg;
+    nrm.ss = ss;
+    nrm.ss_ld = ss_ld;
+    return npub::w8a16_skinny_run(A, lda, Wq, ldw, scale, C, ldc, R, ldr, M, N, K, 1.0f, workspace, workspace_bytes,
+                                  reinterpret_cast<cudaStream_t>(stream), swiglu ? 1 : 0, &nrm);
+}
+
 extern "C" const char* npub_w8a16_kernel_name(int M, int N, int K) {
     if (M <= 0 || N <= 0 || K <= 0) return "none";
     if (npub::w8a16_use_skinny(M, N, K)) return "w8a16_skinny_kernel (stream-K, tcgen05 with A in TMEM)";

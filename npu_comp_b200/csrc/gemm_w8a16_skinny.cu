@@ -78,7 +78,7 @@ struct Smem {
     static constexpr int kTok = (kBK / 64) * kTokChunk;
     static constexpr int kA8Box = kRows * kBox8;
     static constexpr int kA8 = kRows * kBK;
-    static constexpr int kBars = 8 * (2 * kS8 + 2 * kST + 2 * kSA + 4) + 16;
+    static constexpr int kBars = 8 * (2 * kS8 + 2 * kST + 2 * kSA + 4) + 16 + 4 * BT;  // + row scales
     static constexpr int kTotal = kST * kTok + kS8 * kA8 + kBars + 1024;
 };
 
@@ -98,6 +98,33 @@ __device__ __forceinline__ float4 ld_cg_f4(const float4* ptr) {
                  : "memory");
     return v;
 }
+
+// Column sums of a warp's 32 x 16 block (lane = row): a butterfly that halves
+// the columns each lane keeps at every step (16 shuffles).  Lanes 2c and
+// 2c + 1 return the sum of column c' = 8 b4 + 4 b3 + 2 b2 + b1 (b = lane bits).
+__device__ __forceinline__ float warp_colsum16(const float (&a)[16], int lane) {
+    float b[8], c[4], d[2];
+    const bool u4 = lane & 16, u3 = lane & 8, u2 = lane & 4, u1 = lane & 2;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const float send = u4 ? a[k] : a[k + 8];
+        b[k] = (u4 ? a[k + 8] : a[k]) + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float send = u3 ? b[k] : b[k + 4];
+        c[k] = (u3 ? b[k + 4] : b[k]) + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const float send = u2 ? c[k] : c[k + 2];
+        d[k] = (u2 ? c[k + 2] : c[k]) + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    const float e = (u1 ? d[1] : d[0]) + __shfl_xor_sync(0xffffffffu, u1 ? d[0] : d[1], 2);
+    return e + __shfl_xor_sync(0xffffffffu, e, 1);
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("barrier.sync 1, 128;" ::: "memory"); }
 
 __device__ __forceinline__ void set_err(int* err, int code) {
     if (err) atomicCAS(err, 0, code);
@@ -162,6 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
     uint64_t* acc_empty = acc_full + 2;        // [2] epilogue drained the accumulator (4 warps)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* rstd_s = reinterpret_cast<float*>(tmem_slot + 4);  // [BT] row scales of a folded RMSNorm
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KT = p.k_steps;
@@ -336,6 +364,31 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
         const int r = 32 * q + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
         const int M = p.M;
+        const SkinnyNorm& nm = p.nrm;
+        if (nm.rs_part) {
+            // row scales of the folded RMSNorm, while the first MMAs run: 128 / BT
+            // threads per token sum its partials (8 loads in flight each) and
+            // combine in a fixed order
+            constexpr int P = 128 / BT;
+            const int i = 32 * q + lane, tt = i / P, part = i % P;
+            float s = 0.0f;
+            if (tt < M) {
+                const int lo = part * nm.rs_n / P, hi = (part + 1) * nm.rs_n / P;
+                int k = lo;
+                for (; k + 8 <= hi; k += 8) {
+                    float x[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) x[u] = __ldcg(nm.rs_part + (int64_t)(k + u) * nm.rs_ld + tt);
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) s += x[u];
+                }
+                for (; k < hi; ++k) s += __ldcg(nm.rs_part + (int64_t)k * nm.rs_ld + tt);
+            }
+#pragma unroll
+            for (int o = 1; o < P; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            if (part == 0 && tt < BT) rstd_s[tt] = tt < M ? 1.0f / sqrtf(s / nm.rs_d + nm.rs_eps) : 0.0f;
+            epi_bar();
+        }
         for (int t = 0; t < rg.nseg; ++t) {
             const Seg sg = seg_in_order(rg, t);
             const uint32_t b = (uint32_t)t & 1u, bph = ((uint32_t)t >> 1) & 1u;
@@ -428,13 +481,16 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
             // The finished fp32 sums of this warp's 32 rows leave through
             // emit(): scaled (+ residual) and stored as fp16, or SwiGLU pairs.
             auto emit = [&](int c0, const float (&v)[16]) {
+                float rs[16];  // row scales of a folded RMSNorm (1: none)
+#pragma unroll
+                for (int j = 0; j < 16; ++j) rs[j] = nm.rs_part ? rstd_s[c0 + j] : 1.0f;
                 if (p.swiglu) {
                     // gate row 2c and up row 2c + 1 sit in adjacent lanes: both
                     // are rounded to fp16 as a separate GEMM would store them,
                     // and the pair forms fp16(silu(g) * u) for channel c
                     float gu[16], o[8];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) gu[j] = __half2float(__float2half_rn(v[j] * sc));
+                    for (int j = 0; j < 16; ++j) gu[j] = __half2float(__float2half_rn(v[j] * sc * rs[j]));
                     int t0;
                     swiglu_pair16(gu, lane, o, &t0);
                     if (!nrow) return;
@@ -443,14 +499,36 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                         if (c0 + t0 + j < M) p.C[(int64_t)(c0 + t0 + j) * p.ldc + n / 2] = __float2half_rn(o[j]);
                     return;
                 }
-                if (!nrow) return;
                 float rv[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
-                    rv[j] = (p.R && c0 + j < M) ? __half2float(__ldg(p.R + (int64_t)(c0 + j) * p.ldr + n)) : 0.0f;
+                    rv[j] = (p.R && nrow && c0 + j < M) ? __half2float(__ldg(p.R + (int64_t)(c0 + j) * p.ldr + n))
+                                                       : 0.0f;
+                __half o[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    if (c0 + j < M) p.C[(int64_t)(c0 + j) * p.ldc + n] = __float2half_rn(v[j] * sc + rv[j]);
+                for (int j = 0; j < 16; ++j) o[j] = __float2half_rn(v[j] * sc * rs[j] + rv[j]);
+                if (nm.ss) {
+                    // the next RMSNorm's partial sums: this warp's 32 rows of C
+                    float sq[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float f = __half2float(o[j]);
+                        sq[j] = (nrow && c0 + j < M) ? f * f : 0.0f;
+                    }
+                    const float tot = warp_colsum16(sq, lane);
+                    const int col = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+                    if (!(lane & 1) && c0 + col < M)
+                        nm.ss[(int64_t)(sg.tile * 4 + q) * nm.ss_ld + c0 + col] = tot;
+                }
+                if (!nrow) return;
+                const float gm = nm.G ? __half2float(__ldg(nm.gamma + n)) : 0.0f;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    if (c0 + j < M) {
+                        p.C[(int64_t)(c0 + j) * p.ldc + n] = o[j];
+                        if (nm.G) nm.G[(int64_t)(c0 + j) * nm.ldg + n] = __float2half_rn(__half2float(o[j]) * gm);
+                    }
+                }
             };
             if (sg.full) {
                 for (int c0 = 0; c0 < BT && c0 < M; c0 += 16) {
@@ -577,7 +655,7 @@ size_t w8a16_skinny_workspace(int M, int N, int K) {
 
 int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C, int64_t ldc,
                      const void* R, int64_t ldr, int M, int N, int K, float alpha, void* ws, size_t ws_bytes,
-                     cudaStream_t st, int swiglu) {
+                     cudaStream_t st, int swiglu, const SkinnyNorm* nrm) {
     if (!w8a16_skinny_fits(M, N)) return NPUB_ERR_INVALID_ARG;
     if (swiglu && (N % 2 || R)) return NPUB_ERR_INVALID_ARG;
     const size_t need = w8a16_skinny_workspace(M, N, K);
@@ -607,6 +685,7 @@ int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, con
     p.err = npub_internal_device_error_word();
     p.wait_ns = npub_internal_wait_limit_ns();
     p.swiglu = swiglu ? 1 : 0;
+    if (nrm) p.nrm = *nrm;
     const int grid = skinny_grid(N, K);
     return bt == 32 ? skinny::launch<32>(p, grid, st) : skinny::launch<64>(p, grid, st);
 }

@@ -653,6 +653,36 @@ static int grid_for(int64_t work, int threads) {
     return (int)b;
 }
 
+// Inputs of an RMSNorm folded into the next W8A16 GEMM (npub_w8a16_gemm_rms):
+// G = fp16(x * gamma) and, per 32 columns (chunk c), ss[c * ss_ld + row] =
+// sum of x^2.  A lane holds 8 columns, four lanes a chunk.
+__global__ void __launch_bounds__(256) rms_parts_kernel(const __half* __restrict__ x, int64_t ldx,
+                                                        const __half* __restrict__ gamma, __half* __restrict__ G,
+                                                        int64_t ldg, float* __restrict__ ss, int64_t ss_ld, int d) {
+    pdl_trigger();
+    pdl_wait();
+    const int row = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int c0 = warp * 256; c0 < d; c0 += nw * 256) {
+        const int col = c0 + lane * 8;
+        float s = 0.0f;
+        if (col < d) {
+            float v[8], g[8], o[8];
+            unpack8(*reinterpret_cast<const uint4*>(x + (int64_t)row * ldx + col), v);
+            unpack8(*reinterpret_cast<const uint4*>(gamma + col), g);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                s += v[i] * v[i];
+                o[i] = v[i] * g[i];
+            }
+            *reinterpret_cast<uint4*>(G + (int64_t)row * ldg + col) = pack8(o);
+        }
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        if ((lane & 3) == 0 && col < d) ss[(int64_t)(col / 32) * ss_ld + row] = s;
+    }
+}
+
 }  // namespace npub
 
 using namespace npub;
@@ -694,6 +724,18 @@ extern "C" int npub_rmsnorm(const void* x, int64_t ldx, const void* residual, in
     if (nch <= 1024) return NPUB_RMS(256, 4);
     return NPUB_RMS(256, 8);
 #undef NPUB_RMS
+}
+
+extern "C" int npub_rmsnorm_parts(const void* x, int64_t ldx, const void* gamma, void* G, int64_t ldg, float* ss,
+                                  int64_t ss_ld, int rows, int d, void* stream) {
+    NPUB_CHECK_ARG(rows >= 0 && d > 0);
+    if (rows == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(x && gamma && G && ss);
+    NPUB_CHECK_ARG(d % 32 == 0 && ldx % kVec == 0 && ldg % kVec == 0 && ldx >= d && ldg >= d && ss_ld >= rows);
+    NPUB_CHECK_ARG(npub_aligned(x, 16) && npub_aligned(gamma, 16) && npub_aligned(G, 16));
+    return launch_pdl(rms_parts_kernel, dim3(rows), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+                      reinterpret_cast<const __half*>(x), ldx, reinterpret_cast<const __half*>(gamma),
+                      reinterpret_cast<__half*>(G), ldg, ss, ss_ld, d);
 }
 
 extern "C" int npub_swiglu(const void* g, int64_t ldg, const void* u, int64_t ldu, void* h, int64_t ldh, int rows,

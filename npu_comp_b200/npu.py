@@ -26,6 +26,7 @@ from ._lib import NpubError  # noqa: F401  (re-exported)
 __all__ = [
     "fp16", "quantize_w8", "matmul", "rmsnorm", "add", "swiglu", "softmax", "rope", "attention",
     "attention_decode", "kv_append", "rope_kv_append", "rope_kv_store", "matmul_swiglu", "interleave_gate_up",
+    "matmul_rms", "rmsnorm_parts",
     "embed", "argmax", "isa_vector", "f32_to_f16_bits", "f16_bits_to_f32", "device_error", "NpubError",
 ]
 
@@ -218,6 +219,84 @@ def matmul_swiglu(A: torch.Tensor, Wgu: torch.Tensor, scale: torch.Tensor, *,
         e1.record()
         ev.append((e0, e1, 2.0 * M * F2 * K, True))
     return out
+
+
+def matmul_rms(A: torch.Tensor, Wq: torch.Tensor, scale: torch.Tensor, *, out: Optional[torch.Tensor] = None,
+               residual: Optional[torch.Tensor] = None, swiglu: bool = False,
+               rs: Optional[Tuple[torch.Tensor, int]] = None, eps: float = 1e-5,
+               gamma: Optional[torch.Tensor] = None, g_out: Optional[torch.Tensor] = None,
+               ss_out: Optional[torch.Tensor] = None):
+    """W8A16 GEMM of a decode step (M <= 64) with an RMSNorm folded in
+    (npub_w8a16_gemm_rms): the RMSNorm -> projection pairs of a decode layer
+    without the normalised activations' round trip or their own launch.
+
+    rs=(ss, d): A is fp16(h * gamma) of a residual stream h (rmsnorm_parts or a
+    producer call below) and row t of the result is scaled by
+    1 / sqrt(sum(ss[:, t]) / d + eps) before rounding (before SwiGLU with
+    swiglu=True, where Wq holds interleaved gate/up rows and out is [M, N/2]).
+    gamma: also return (out, g_out, ss_out) -- g_out = fp16(out * gamma) and
+    ss_out [N/32, M] fp32, the next call's rs.  Raises NpubError for M > 64."""
+    lda = _mat(A, "A", torch.float16)
+    ldw = _mat(Wq, "Wq", torch.int8)
+    M, K = A.shape
+    N, K2 = Wq.shape
+    _need(K == K2, f"K mismatch: A {tuple(A.shape)} vs Wq {tuple(Wq.shape)}")
+    _need(scale.is_cuda and scale.dtype == torch.float16 and scale.numel() == N and scale.is_contiguous(),
+          "scale must be a contiguous fp16 CUDA tensor of N elements")
+    NC = N // 2 if swiglu else N
+    if out is None:
+        out = torch.empty((M, NC), dtype=torch.float16, device=A.device)
+    ldc = _mat(out, "out", torch.float16)
+    _need(tuple(out.shape) == (M, NC), f"out must be [{M}, {NC}]")
+    ldr = 0
+    if residual is not None:
+        ldr = _mat(residual, "residual", torch.float16)
+        _need(tuple(residual.shape) == (M, N), "residual must be [M, N]")
+    rs_p, rs_n, rs_ld, rs_d = None, 0, 0, 0
+    if rs is not None:
+        ss, rs_d = rs
+        _need(ss.is_cuda and ss.dtype == torch.float32 and ss.dim() == 2 and ss.shape[1] >= M and ss.stride(1) == 1,
+              "rs[0] must be fp32 CUDA [parts, >= M] with unit column stride")
+        rs_p, rs_n, rs_ld = ss, ss.shape[0], ss.stride(0)
+    ldg = ss_ld = 0
+    if gamma is not None:
+        _need(gamma.is_cuda and gamma.dtype == torch.float16 and gamma.numel() == N and gamma.is_contiguous(),
+              "gamma must be a contiguous fp16 CUDA tensor of N elements")
+        if g_out is None:
+            g_out = torch.empty((M, N), dtype=torch.float16, device=A.device)
+        if ss_out is None:
+            ss_out = torch.empty((N // 32, M), dtype=torch.float32, device=A.device)
+        ldg = _mat(g_out, "g_out", torch.float16)
+        _need(ss_out.dtype == torch.float32 and ss_out.dim() == 2 and ss_out.shape[0] == N // 32 and
+              ss_out.shape[1] >= M and ss_out.stride(1) == 1, "ss_out must be fp32 [N/32, >= M]")
+        ss_ld = ss_out.stride(0)
+    ws, wsb = _zeroed_workspace(_lib.query("npub_w8a16_gemm_rms_workspace", M, N, K), A.device)
+    _lib.call("npub_w8a16_gemm_rms", A.data_ptr(), lda, Wq.data_ptr(), ldw, scale.data_ptr(), out.data_ptr(), ldc,
+              _ptr(residual), ldr, M, N, K, 1 if swiglu else 0, _ptr(rs_p), rs_n, rs_ld, int(rs_d), float(eps),
+              _ptr(gamma), _ptr(g_out if gamma is not None else None), ldg,
+              _ptr(ss_out if gamma is not None else None), ss_ld, _ptr(ws), wsb, _stream())
+    return out if gamma is None else (out, g_out, ss_out)
+
+
+def rmsnorm_parts(x: torch.Tensor, gamma: torch.Tensor, *, g_out: Optional[torch.Tensor] = None,
+                  ss_out: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The (g, ss) that matmul_rms(rs=(ss, d)) takes for an RMSNorm of x
+    (fp16 [rows, d], d % 32 == 0): g = fp16(x * gamma), ss [d/32, rows] fp32
+    the sums of x^2 over every 32 columns."""
+    ldx = _mat(x, "x", torch.float16)
+    rows, d = x.shape
+    _need(gamma.is_cuda and gamma.dtype == torch.float16 and gamma.numel() == d and gamma.is_contiguous(),
+          "gamma must be a contiguous fp16 CUDA tensor of d elements")
+    if g_out is None:
+        g_out = torch.empty((rows, d), dtype=torch.float16, device=x.device)
+    if ss_out is None:
+        ss_out = torch.empty((d // 32, rows), dtype=torch.float32, device=x.device)
+    ldg = _mat(g_out, "g_out", torch.float16)
+    _need(ss_out.dtype == torch.float32 and ss_out.dim() == 2 and ss_out.shape[0] == d // 32 and
+          ss_out.shape[1] >= rows and ss_out.stride(1) == 1, "ss_out must be fp32 [d/32, >= rows]")
+    _lib.call("npub_rmsnorm_parts", x.data_ptr(), ldx, gamma.data_ptr(), g_out.data_ptr(), ldg, ss_out.data_ptr(),
+              ss_out.stride(0), rows, d, _stream())
+    return g_out, ss_out
 
 
 # ---------------------------------------------------------------- vector ops

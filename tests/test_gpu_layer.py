@@ -141,3 +141,24 @@ def test_decode_step_matches_reference_and_prefill(cuda_device):
         assert ref.rel_err(yd[b].cpu().numpy(), yr) <= TOL
     e = ((yd - full[:, T]).abs().max() / full[:, T].abs().max()).item()
     assert e <= 2 * TOL
+
+
+def test_decode_folded_norms_match_separate_norms(cuda_device, monkeypatch):
+    """A decode step with the RMSNorms folded into the GEMMs (npu.matmul_rms)
+    and the same step with separate RMSNorm launches (NPUB_FOLD_RMSNORM=0):
+    two fp16 paths of the same layer, batch 32 (the stack's decode batch)."""
+    cfg = llama.LLAMA_7B
+    w = llama.make_layer(cfg, seed=2, device=cuda_device)
+    B, ctx = 32, 300
+    g = torch.Generator(device=cuda_device).manual_seed(4)
+    kc = torch.randn((B, cfg.kv_heads, ctx + 8, cfg.head_dim), generator=g, device=cuda_device).half()
+    vc = torch.randn_like(kc)
+    x = torch.randn((B, cfg.d), generator=g, device=cuda_device).half()
+    pos = torch.full((B,), ctx, dtype=torch.int32, device=cuda_device)
+    assert llama.folded_norm_ok(cfg, B, llama.TP())
+    y1 = llama.layer_decode(x, w, cfg, kc.clone(), vc.clone(), pos, ctx_max=ctx + 1).float()
+    monkeypatch.setenv("NPUB_FOLD_RMSNORM", "0")
+    assert not llama.folded_norm_ok(cfg, B, llama.TP())
+    y0 = llama.layer_decode(x, w, cfg, kc.clone(), vc.clone(), pos, ctx_max=ctx + 1).float()
+    e = ((y1 - y0).abs().max() / y0.abs().max()).item()
+    assert e <= TOL, e

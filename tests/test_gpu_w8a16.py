@@ -254,3 +254,82 @@ def test_matmul_swiglu_against_oracle(cuda_device, rng):
     qi, si = nb.interleave_gate_up(to_dev(q, cuda_device), to_dev(s, cuda_device))
     got = nb.matmul_swiglu(to_dev(A, cuda_device), qi, si).float().cpu().numpy()
     assert ref.rel_err(got, want) <= TOL
+
+
+# ------------------------------------------------ RMSNorm folded into the decode GEMMs
+
+@pytest.mark.parametrize("M,N,K", [(32, 12288, 4096), (7, 1024, 512), (64, 4096, 4096), (1, 512, 1376)])
+def test_matmul_rms_consumer_against_oracle(cuda_device, rng, M, N, K):
+    """matmul_rms(rmsnorm_parts(h)) = RMSNorm(h) then the W8A16 projection
+    (legalize.py:30-47 then npu.py:41-47), against the float64 oracle, and
+    close to the unfused pair of launches."""
+    h = (rng.standard_normal((M, K)) * 3).astype(np.float16)
+    gam = (1 + 0.1 * rng.standard_normal(K)).astype(np.float16)
+    W = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    q, s = ref.quantize_w8(W)
+    hd, gd, qd, sd = (to_dev(a, cuda_device) for a in (h, gam, q, s))
+    g, ss = nb.rmsnorm_parts(hd, gd)
+    got = nb.matmul_rms(g, qd, sd, rs=(ss, K), eps=1e-5).float().cpu().numpy()
+    want = ref.w8a16_ref(ref.rmsnorm_ref(h, gam, 1e-5).astype(np.float16), q, s)
+    assert ref.rel_err(got, want) <= TOL
+    unfused = nb.matmul(nb.rmsnorm(hd, gd, 1e-5), qd, sd).float().cpu().numpy()
+    assert ref.rel_err(got, unfused) <= 2e-3
+
+
+def test_rmsnorm_parts_exact(cuda_device, rng):
+    """g = fp16(x * gamma) bit for bit; ss = the sums of x^2 over every 32 columns."""
+    x = (rng.standard_normal((5, 4096)) * 2).astype(np.float16)
+    gam = rng.standard_normal(4096).astype(np.float16)
+    g, ss = nb.rmsnorm_parts(to_dev(x, cuda_device), to_dev(gam, cuda_device))
+    assert np.array_equal(g.cpu().numpy(), (x.astype(np.float32) * gam.astype(np.float32)).astype(np.float16))
+    want = (x.astype(np.float64) ** 2).reshape(5, 128, 32).sum(-1).T
+    assert np.allclose(ss.cpu().numpy(), want, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("M,N,K", [(32, 4096, 4096), (32, 4096, 11008), (13, 512, 512), (64, 1024, 1376)])
+def test_matmul_rms_producer_outputs(cuda_device, rng, M, N, K):
+    """The producer form: C = fp16(A Wq^T s + R) as matmul(residual=R) on the
+    stream-K kernel, G = fp16(C * gamma) bit for bit from C, and the column
+    sums of C^2 -- which a consumer call turns into the RMSNorm of C."""
+    A = rng.standard_normal((M, K)).astype(np.float16)
+    R = rng.standard_normal((M, N)).astype(np.float16)
+    gam = (1 + 0.1 * rng.standard_normal(N)).astype(np.float16)
+    W = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    q, s = ref.quantize_w8(W)
+    Ad, Rd, gd, qd, sd = (to_dev(a, cuda_device) for a in (A, R, gam, q, s))
+    C, G, ss = nb.matmul_rms(Ad, qd, sd, residual=Rd, gamma=gd)
+    Cn = C.float().cpu().numpy()
+    assert ref.rel_err(Cn, ref.w8a16_ref(A, q, s, residual=R)) <= TOL
+    assert torch.equal(G, (C.float() * gd.float()).half())
+    want = (Cn.astype(np.float64) ** 2).reshape(M, N // 32, 32).sum(-1).T
+    assert np.allclose(ss.cpu().numpy()[:, :M], want, rtol=1e-5, atol=1e-5)
+    # the folded pair equals RMSNorm(C) then the next projection, within tolerance
+    W2 = (rng.standard_normal((N, 256)) * 0.02).astype(np.float32)
+    q2, s2 = ref.quantize_w8(W2)
+    nxt = nb.matmul_rms(G, to_dev(q2, cuda_device), to_dev(s2, cuda_device), rs=(ss, N), eps=1e-6)
+    want2 = ref.w8a16_ref(ref.rmsnorm_ref(Cn.astype(np.float16), gam, 1e-6).astype(np.float16), q2, s2)
+    assert ref.rel_err(nxt.float().cpu().numpy(), want2) <= TOL
+
+
+def test_matmul_rms_swiglu_against_oracle(cuda_device, rng):
+    """Consumer form with SwiGLU: RMSNorm -> gate|up -> silu(g) * u (llama_layer.py:139-150)."""
+    M, F, K = 32, 688, 512
+    h = (rng.standard_normal((M, K)) * 2).astype(np.float16)
+    gam = (1 + 0.1 * rng.standard_normal(K)).astype(np.float16)
+    W = (rng.standard_normal((K, 2 * F)) * 0.05).astype(np.float32)
+    q, s = ref.quantize_w8(W)
+    hn = ref.rmsnorm_ref(h, gam, 1e-5).astype(np.float16)
+    gu = ref.w8a16_ref(hn, q, s).astype(np.float16).astype(np.float64)
+    want = ref.silu_mul_ref(gu[:, :F], gu[:, F:])
+    qi, si = nb.interleave_gate_up(to_dev(q, cuda_device), to_dev(s, cuda_device))
+    g, ss = nb.rmsnorm_parts(to_dev(h, cuda_device), to_dev(gam, cuda_device))
+    got = nb.matmul_rms(g, qi, si, swiglu=True, rs=(ss, K), eps=1e-5).float().cpu().numpy()
+    assert ref.rel_err(got, want) <= TOL
+
+
+def test_matmul_rms_rejects_many_tokens(cuda_device):
+    A = torch.zeros((65, 512), dtype=torch.float16, device=cuda_device)
+    q = torch.zeros((512, 512), dtype=torch.int8, device=cuda_device)
+    s = torch.ones(512, dtype=torch.float16, device=cuda_device)
+    with pytest.raises(nb.NpubError):
+        nb.matmul_rms(A, q, s)
