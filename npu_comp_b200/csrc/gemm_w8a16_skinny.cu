@@ -389,6 +389,17 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
             if (part == 0 && tt < BT) rstd_s[tt] = tt < M ? 1.0f / sqrtf(s / nm.rs_d + nm.rs_eps) : 0.0f;
             epi_bar();
         }
+        if (p.R || nm.G) {
+            // the residual rows (and gamma) the stores will read go to L2 now,
+            // while the MMAs run: read at the end, after the weight stream
+            // has filled HBM's queues, they cost several microseconds
+            for (int t = 0; t < rg.nseg; ++t) {
+                const int n0 = seg_in_order(rg, t).tile * kRows + 32 * q;
+                if (n0 >= p.N) continue;
+                if (p.R && lane < M) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.R + (int64_t)lane * p.ldr + n0));
+                if (nm.G && lane == 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(nm.gamma + n0));
+            }
+        }
         for (int t = 0; t < rg.nseg; ++t) {
             const Seg sg = seg_in_order(rg, t);
             const uint32_t b = (uint32_t)t & 1u, bph = ((uint32_t)t >> 1) & 1u;
