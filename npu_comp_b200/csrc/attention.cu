@@ -7,10 +7,10 @@
 //   O = P V (tcgen05 GEMM, K loop cut at the diagonal), V transposed once so
 //   both GEMM operands are K-major.
 // Decode: flash-decoding over an fp16 KV cache [batch, kv_heads, cap, 128],
-// HBM-bound: a persistent kernel that balances the 64-key stages of all
-// (sequence, kv head) pairs over the resident CTAs (grouped-query groups of
-// 1, 2, 4 or 8 heads, up to 512 sequences); other groups run a split kernel
-// with 4 lanes per key and a combine pass.
+// HBM-bound: streaming kernels (a bulk-copy ring of K/V stages) for
+// grouped-query groups of 1 to 8 heads, scheduled by the number of (sequence,
+// kv head) items; larger groups run a split kernel with 4 lanes per key and a
+// combine pass.
 #include "common.cuh"
 #include "gemm_tc.h"
 
@@ -535,7 +535,7 @@ __device__ __forceinline__ bool ps_empty(int cc, int S, int nctas) {
 }
 
 template <int G>
-__global__ void __launch_bounds__(kStThreads, G >= 8 ? 1 : 2) decode_attn_persist_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kStThreads, G > 4 ? 1 : 2) decode_attn_persist_kernel(const DecodeArgs a) {
     using L = PsLayout<G>;
     pdl_trigger();
     extern __shared__ uint8_t smem_raw[];
@@ -1055,7 +1055,7 @@ extern "C" int npub_attention_decode(const void* q, int64_t ldq, const void* k_c
     a.wait_ns = npub_internal_wait_limit_ns();
     const int group = heads / kv_heads;
     const int64_t items = (int64_t)batch * kv_heads;
-    const bool streaming = group == 1 || group == 2 || group == 4 || group == 8;
+    const bool streaming = group >= 1 && group <= 8;
     // Schedules, by the number of (sequence, kv head) items (measured on B200):
     //  * >= 6 per SM: one streaming CTA per item;
     //  * 32 .. 6 per SM: the persistent grid over the stage list (4-24 % faster
@@ -1069,7 +1069,11 @@ extern "C" int npub_attention_decode(const void* q, int64_t ldq, const void* k_c
         switch (group) {
             case 1: return launch_persist<1>(a, stages, workspace_bytes, st);
             case 2: return launch_persist<2>(a, stages, workspace_bytes, st);
+            case 3: return launch_persist<3>(a, stages, workspace_bytes, st);
             case 4: return launch_persist<4>(a, stages, workspace_bytes, st);
+            case 5: return launch_persist<5>(a, stages, workspace_bytes, st);
+            case 6: return launch_persist<6>(a, stages, workspace_bytes, st);
+            case 7: return launch_persist<7>(a, stages, workspace_bytes, st);
             default: return launch_persist<8>(a, stages, workspace_bytes, st);
         }
     }
@@ -1083,7 +1087,11 @@ extern "C" int npub_attention_decode(const void* q, int64_t ldq, const void* k_c
         switch (group) {
             case 1: rc = launch_stream<1>(a, batch, kv_heads, splits, st); break;
             case 2: rc = launch_stream<2>(a, batch, kv_heads, splits, st); break;
+            case 3: rc = launch_stream<3>(a, batch, kv_heads, splits, st); break;
             case 4: rc = launch_stream<4>(a, batch, kv_heads, splits, st); break;
+            case 5: rc = launch_stream<5>(a, batch, kv_heads, splits, st); break;
+            case 6: rc = launch_stream<6>(a, batch, kv_heads, splits, st); break;
+            case 7: rc = launch_stream<7>(a, batch, kv_heads, splits, st); break;
             default: rc = launch_stream<8>(a, batch, kv_heads, splits, st); break;
         }
     } else {

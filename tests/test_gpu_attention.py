@@ -83,6 +83,10 @@ def test_decode_attention(cuda_device, rng, B, H, KV, ctx, cap):
     (2, 64, 8, 20000, 20000, [20000, 1]),           # the same, groups of 8
     (520, 8, 8, 70, 72, None),                      # many items: one CTA per (sequence, kv head)
     (900, 8, 1, 100, 128, "with-empty"),            # the same with groups of 8 and empty sequences
+    (32, 24, 8, 1100, 1104, None),                  # groups of 3 (Llama-3.2-3B), persistent
+    (6, 48, 8, 900, 904, None),                     # groups of 6, persistent
+    (120, 40, 8, 50, 64, None),                     # groups of 5, one CTA per item
+    (3, 21, 3, 2000, 2000, None),                   # groups of 7, context splits
 ])
 def test_decode_attention_work_split(cuda_device, rng, B, H, KV, ctx, cap, lens):
     """The three schedules of the streaming kernel (persistent grid over the
