@@ -259,6 +259,17 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                  : "memory");
 }
 
+// L2 prefetch of the first stages of a (sequence, kv head)'s keys [k0, k1),
+// issued before griddepcontrol.wait: only the newest key is written by the
+// kernels this one follows, and L2 stays coherent with that write.
+__device__ __forceinline__ void prefetch_kv_l2(const DecodeArgs& a, int b, int kvh, int64_t k0, int64_t k1) {
+    if (k1 <= k0) return;
+    const int64_t off = (((int64_t)b * a.kv_heads + kvh) * a.cap + k0) * kDecHd;
+    const uint32_t bytes = (uint32_t)(k1 - k0) * kDecHd * 2;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.kc + off), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.vc + off), "r"(bytes) : "memory");
+}
+
 // Barrier of the eight compute warps (the producer warp has left); the
 // non-.aligned form, since lane 0 of warp 0 may arrive from a finisher's wait.
 __device__ __forceinline__ void compute_bar() { asm volatile("barrier.sync 1, %0;" ::"n"(kStWarps * 32) : "memory"); }
@@ -360,6 +371,10 @@ __global__ void __launch_bounds__(kStThreads, G <= 4 ? 2 : 1) decode_attn_stream
     const int bk = blockIdx.x;  // sequence * kv_heads + kv head
     const int b = bk / a.kv_heads, kvh = bk % a.kv_heads;
     const int split = blockIdx.y;  // context split (a.splits > 1: partials for decode_combine_kernel)
+    if (threadIdx.x == kStWarps * 32) {
+        const int64_t k0 = (int64_t)split * a.chunk;
+        prefetch_kv_l2(a, b, kvh, k0, min(min(k0 + kStStages * kStKeys, k0 + (int64_t)a.chunk), a.cap));
+    }
     pdl_wait();  // lens, q and the caches come from earlier kernels
     const int len = (int)min((int64_t)(a.lens ? a.lens[b] : a.ctx), a.cap);
     const int c0 = split * a.chunk;
@@ -559,6 +574,21 @@ __global__ void __launch_bounds__(kStThreads, G > 4 ? 1 : 2) decode_attn_persist
         }
         *abort_flag = 0;
         fence_barrier_init();
+    }
+    if (threadIdx.x == kStWarps * 32 && a.ctx > 0) {
+        // the first stages of this CTA's range if every length is the largest
+        // (ctx): the usual case, and only a prefetch when it is not
+        const int64_t n = (min((int64_t)a.ctx, a.cap) + kStKeys - 1) / kStKeys;
+        const int64_t S = (int64_t)batch * kvh * n;
+        int64_t f = (int64_t)blockIdx.x * S / gridDim.x;
+        const int64_t fe = min(f + kStStages, ((int64_t)blockIdx.x + 1) * S / gridDim.x);
+        while (f < fe) {
+            const int64_t item = f / n, st = f % n;
+            const int64_t k0 = st * kStKeys, k1 = min(min((int64_t)a.ctx, a.cap), k0 + (fe - f) * kStKeys);
+            const int64_t kend = min(k1, n * kStKeys);
+            prefetch_kv_l2(a, (int)(item / kvh), (int)(item % kvh), k0, min(kend, min((int64_t)a.ctx, a.cap)));
+            f += (kend - k0 + kStKeys - 1) / kStKeys;
+        }
     }
     pdl_wait();  // lens, q and the caches come from earlier kernels
     if (warp == 0) {

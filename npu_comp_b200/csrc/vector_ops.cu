@@ -548,13 +548,42 @@ __global__ void argmax_kernel(const __half* __restrict__ x, int64_t ldx, int col
     const __half* row = x + (int64_t)blockIdx.x * ldx;
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-        const float v = __half2float(row[c]);
+    auto take = [&](float v, int c) {
         if (v > best || (v == best && c < bi)) {
             best = v;
             bi = c;
         }
+    };
+    int c0 = 0;
+    if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+        // 16-byte loads, four in flight per thread (a row is a few hundred
+        // vectors per warp: one pass of latency-bound rounds)
+        const int nv = cols / 8;
+        const uint4* rv = reinterpret_cast<const uint4*>(row);
+        for (int v0 = threadIdx.x; v0 < nv; v0 += 4 * (int)blockDim.x) {
+            uint4 u[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int v = v0 + k * (int)blockDim.x;
+                u[k] = v < nv ? __ldg(rv + v) : make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int v = v0 + k * (int)blockDim.x;
+                if (v < nv) {
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&u[k]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = __half22float2(h2[e]);
+                        take(f.x, 8 * v + 2 * e);
+                        take(f.y, 8 * v + 2 * e + 1);
+                    }
+                }
+            }
+        }
+        c0 = nv * 8;
     }
+    for (int c = c0 + threadIdx.x; c < cols; c += blockDim.x) take(__half2float(row[c]), c);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, best, o);
@@ -970,7 +999,7 @@ extern "C" int npub_argmax_rows(const void* x, int64_t ldx, int rows, int cols, 
     NPUB_CHECK_ARG(rows >= 0);
     if (rows == 0) return NPUB_OK;
     NPUB_CHECK_ARG(x && idx && cols > 0 && ldx >= cols);
-    return launch_pdl(argmax_kernel, dim3(rows), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+    return launch_pdl(argmax_kernel, dim3(rows), dim3(512), 0, reinterpret_cast<cudaStream_t>(stream),
                       reinterpret_cast<const __half*>(x), ldx, cols, idx, val, (uint64_t*)nullptr, 0);
 }
 
@@ -980,7 +1009,7 @@ extern "C" int npub_argmax_keys(const void* x, int64_t ldx, int rows, int cols, 
     if (rows == 0) return NPUB_OK;
     NPUB_CHECK_ARG(x && keys && cols > 0 && ldx >= cols && index_offset >= 0);
     NPUB_CHECK_ARG((int64_t)index_offset + cols <= 0x7fffffff && npub_aligned(keys, 8));
-    return launch_pdl(argmax_kernel, dim3(rows), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+    return launch_pdl(argmax_kernel, dim3(rows), dim3(512), 0, reinterpret_cast<cudaStream_t>(stream),
                       reinterpret_cast<const __half*>(x), ldx, cols, (int32_t*)nullptr, (float*)nullptr, keys,
                       index_offset);
 }

@@ -129,3 +129,20 @@ def test_greedy_keys_select_the_global_argmax(cuda_device, rng, ranks):
     assert np.array_equal(ids, np.argmax(x.astype(np.float32), axis=1))
     idx, _ = nb.argmax(xt)
     assert np.array_equal(idx.cpu().numpy(), ids)
+
+
+@pytest.mark.parametrize("rows,cols,ld", [(32, 32000, 32000), (5, 32003, 32003), (3, 1001, 1005), (2, 7, 7)])
+def test_argmax_rows_vector_and_scalar_paths(cuda_device, rng, rows, cols, ld):
+    """The per-row argmax against numpy's (first index on ties): 16-byte loads
+    where a row starts 16-byte aligned, scalar elsewhere and for the tail;
+    ties inside one vector, across vectors and at the last column."""
+    x = rng.standard_normal((rows, ld)).astype(np.float16)
+    x[0, 3] = x[0, 5] = 12.0                     # tie inside a vector
+    if cols > 20:
+        x[1 % rows, 9] = x[1 % rows, cols - 1] = 13.0   # tie across vectors / the tail
+    x[rows - 1, cols - 1] = 20.0                 # the last column
+    xt = dev(x, cuda_device)[:, :cols]
+    idx, val = nb.argmax(xt)
+    want = np.argmax(x[:, :cols].astype(np.float32), axis=1)
+    assert np.array_equal(idx.cpu().numpy(), want)
+    assert np.array_equal(val.cpu().numpy(), x[np.arange(rows), want].astype(np.float32))
