@@ -310,6 +310,47 @@ __device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_
         }
     }
 }
+// Arrive on a (possibly remote) mbarrier with release semantics at cluster
+// scope, and the matching acquire wait: stores a thread made (to shared::cluster
+// addresses) before the arrive are visible to the threads that see the phase.
+__device__ __forceinline__ void mbar_arrive_rel_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_acq_cluster(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                      uint64_t limit_ns = 2000000000ull) {
+    if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+    uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+        if ((it & 255u) == 0) {
+            if (*abort) return false;
+            if (globaltimer_ns() - t0 > limit_ns) return false;
+        }
+    }
+}
+// 16-byte store to another CTA's shared memory (distributed shared memory).
+__device__ __forceinline__ void st_cluster_f4(uint32_t cluster_addr, const float* v) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "f"(v[0]), "f"(v[1]),
+                 "f"(v[2]), "f"(v[3])
+                 : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+// The two halves of cluster_sync(), for threads that finish their remote work
+// at different points: arrive when done, wait before leaving.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+
 // 3-D TMA load whose completion is signalled on a barrier that may live in the
 // peer CTA of a 2-CTA pair (cta_group::2 form, no multicast).
 __device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* m, uint32_t bar_cluster_addr, int c0,

@@ -54,6 +54,8 @@
 
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
+#include <mutex>
 
 namespace npub {
 
@@ -78,7 +80,7 @@ struct Smem {
     static constexpr int kTok = (kBK / 64) * kTokChunk;
     static constexpr int kA8Box = kRows * kBox8;
     static constexpr int kA8 = kRows * kBK;
-    static constexpr int kBars = 8 * (2 * kS8 + 2 * kST + 2 * kSA + 4) + 16 + 4 * BT;  // + row scales
+    static constexpr int kBars = 8 * (2 * kS8 + 2 * kST + 2 * kSA + 6) + 16 + 4 * BT;  // + row scales
     static constexpr int kTotal = kST * kTok + kS8 * kA8 + kBars + 1024;
 };
 
@@ -187,14 +189,31 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
     uint64_t* a_empty = a_full + kSA;          // [kSA] MMA done with the TMEM stage
     uint64_t* acc_full = a_empty + kSA;        // [2] accumulator ready
     uint64_t* acc_empty = acc_full + 2;        // [2] epilogue drained the accumulator (4 warps)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    uint64_t* cl_go = acc_empty + 2;           // cluster split: the finisher's ring is free (1)
+    uint64_t* cl_recv = cl_go + 1;             // cluster split: the other pieces are in (4 per piece)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cl_recv + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     float* rstd_s = reinterpret_cast<float*>(tmem_slot + 4);  // [BT] row scales of a folded RMSNorm
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KT = p.k_steps;
     const int64_t U = (int64_t)p.n_tiles * KT, G = gridDim.x;
-    const Range rg = make_range(unit_start(blockIdx.x, U, G), unit_start((int64_t)blockIdx.x + 1, U, G), KT);
+    // Cluster split (p.csplit = C > 1): cluster t computes tile t, its rank r
+    // the K steps [r KT / C, (r + 1) KT / C); rank 0 finishes the tile from the
+    // others' fp32 pieces, written into its idle int8 ring through distributed
+    // shared memory.  Otherwise stream-K over the whole unit list.
+    const int C = p.csplit > 1 ? p.csplit : 1;
+    const uint32_t crank = C > 1 ? cluster_ctarank() : 0u;
+    int64_t u0, u1;
+    if (C > 1) {
+        const int64_t t = blockIdx.x / C;
+        u0 = t * KT + (int64_t)crank * KT / C;
+        u1 = t * KT + (int64_t)(crank + 1) * KT / C;
+    } else {
+        u0 = unit_start(blockIdx.x, U, G);
+        u1 = unit_start((int64_t)blockIdx.x + 1, U, G);
+    }
+    const Range rg = make_range(u0, u1, KT);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kS8; ++s) {
@@ -213,6 +232,8 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], 4);
         }
+        mbar_init(cl_go, 1);
+        mbar_init(cl_recv, 4 * (C - 1));
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -227,6 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
     tc_fence_before();
     cta_sync_divergent();
     tc_fence_after();
+    if (C > 1) cluster_sync();  // every rank's barriers are initialised before any remote arrive
+    bool cl_arrived = false;
     const uint32_t tmem = *tmem_slot;
     int never = 0;
     volatile int* no_abort = &never;
@@ -407,6 +430,122 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
             const bool nrow = n < p.N;
             // the scale load is in flight while the accumulator is waited for
             const float sc = p.alpha * ((p.scale && nrow) ? __half2float(__ldg(p.scale + n)) : 1.0f);
+            // The finished fp32 sums of this warp's 32 rows leave through
+            // emit(): scaled (+ residual) and stored as fp16, or SwiGLU pairs.
+            auto emit = [&](int c0, const float (&v)[16]) {
+                float rs[16];  // row scales of a folded RMSNorm (1: none)
+#pragma unroll
+                for (int j = 0; j < 16; ++j) rs[j] = nm.rs_part ? rstd_s[c0 + j] : 1.0f;
+                if (p.swiglu) {
+                    // gate row 2c and up row 2c + 1 sit in adjacent lanes: both
+                    // are rounded to fp16 as a separate GEMM would store them,
+                    // and the pair forms fp16(silu(g) * u) for channel c
+                    float gu[16], o[8];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) gu[j] = __half2float(__float2half_rn(v[j] * sc * rs[j]));
+                    int t0;
+                    swiglu_pair16(gu, lane, o, &t0);
+                    if (!nrow) return;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (c0 + t0 + j < M) p.C[(int64_t)(c0 + t0 + j) * p.ldc + n / 2] = __float2half_rn(o[j]);
+                    return;
+                }
+                float rv[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    rv[j] = (p.R && nrow && c0 + j < M) ? __half2float(__ldg(p.R + (int64_t)(c0 + j) * p.ldr + n))
+                                                       : 0.0f;
+                __half o[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) o[j] = __float2half_rn(v[j] * sc * rs[j] + rv[j]);
+                if (nm.ss) {
+                    // the next RMSNorm's partial sums: this warp's 32 rows of C
+                    float sq[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float f = __half2float(o[j]);
+                        sq[j] = (nrow && c0 + j < M) ? f * f : 0.0f;
+                    }
+                    const float tot = warp_colsum16(sq, lane);
+                    const int col = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+                    if (!(lane & 1) && c0 + col < M)
+                        nm.ss[(int64_t)(sg.tile * 4 + q) * nm.ss_ld + c0 + col] = tot;
+                }
+                if (!nrow) return;
+                const float gm = nm.G ? __half2float(__ldg(nm.gamma + n)) : 0.0f;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    if (c0 + j < M) {
+                        p.C[(int64_t)(c0 + j) * p.ldc + n] = o[j];
+                        if (nm.G) nm.G[(int64_t)(c0 + j) * nm.ldg + n] = __float2half_rn(__half2float(o[j]) * gm);
+                    }
+                }
+            };
+            if (C > 1) {
+                // ---------------------------------------- cluster split: one segment per CTA
+                bool have = mbar_wait_bounded(&acc_full[b], bph, abort_flag);
+                if (!__all_sync(0xffffffffu, have)) {
+                    if (lane == 0) set_err(p.err, 0x30a);
+                    *abort_flag = 1;
+                }
+                tc_fence_after();
+                float* recv = reinterpret_cast<float*>(sA8);  // [C - 1][kRows][BT] fp32 pieces (rank 0)
+                if (crank != 0) {
+                    // wait until rank 0's MMAs are done (its ring is free), then write this
+                    // piece into it and arrive on its barrier (release at cluster scope)
+                    const bool go = __all_sync(0xffffffffu, mbar_wait_acq_cluster(cl_go, 0, abort_flag));
+                    if (!go) {
+                        if (lane == 0) set_err(p.err, 0x30b);
+                        cluster_arrive();
+                        cl_arrived = true;
+                        continue;
+                    }
+                    const uint32_t dst =
+                        mapa_shared(smem_u32(recv + ((int64_t)(crank - 1) * kRows + r) * BT), 0u);
+                    for (int c0 = 0; c0 < BT && c0 < M; c0 += 16) {
+                        float v[16];
+                        tmem_ld16(lane_base + b * (uint32_t)BT + (uint32_t)c0, v);
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4) st_cluster_f4(dst + 4u * (uint32_t)(c0 + j), v + j);
+                    }
+                    fence_acq_rel_cluster();  // every lane's stores before lane 0's release
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&acc_empty[b]);
+                        mbar_arrive_rel_cluster(mapa_shared(smem_u32(cl_recv), 0u));
+                    }
+                    cluster_arrive();  // this CTA's remote work is done
+                    cl_arrived = true;
+                    continue;
+                }
+                if (warp == 4 && lane == 0)
+                    for (int rr = 1; rr < C; ++rr) mbar_arrive_rel_cluster(mapa_shared(smem_u32(cl_go), (uint32_t)rr));
+                if (!mbar_wait_acq_cluster(cl_recv, 0, abort_flag) && lane == 0) set_err(p.err, 0x30c);
+                cluster_arrive();  // every piece is in: the other ranks may leave
+                cl_arrived = true;
+                for (int c0 = 0; c0 < BT && c0 < M; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(lane_base + b * (uint32_t)BT + (uint32_t)c0, v);
+                    for (int rr = 1; rr < C; ++rr) {  // the pieces in rank order
+                        const float4* pc = reinterpret_cast<const float4*>(recv + ((int64_t)(rr - 1) * kRows + r) * BT + c0);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const float4 x = pc[j];
+                            v[4 * j] += x.x;
+                            v[4 * j + 1] += x.y;
+                            v[4 * j + 2] += x.z;
+                            v[4 * j + 3] += x.w;
+                        }
+                    }
+                    emit(c0, v);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[b]);
+                continue;
+            }
             // A tile cut between CTAs: its finisher is the CTA holding its first
             // K step; every other piece is the first tile of its CTA, whose one
             // partial slot it fills.
@@ -489,58 +628,6 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                 break;
             }
             tc_fence_after();
-            // The finished fp32 sums of this warp's 32 rows leave through
-            // emit(): scaled (+ residual) and stored as fp16, or SwiGLU pairs.
-            auto emit = [&](int c0, const float (&v)[16]) {
-                float rs[16];  // row scales of a folded RMSNorm (1: none)
-#pragma unroll
-                for (int j = 0; j < 16; ++j) rs[j] = nm.rs_part ? rstd_s[c0 + j] : 1.0f;
-                if (p.swiglu) {
-                    // gate row 2c and up row 2c + 1 sit in adjacent lanes: both
-                    // are rounded to fp16 as a separate GEMM would store them,
-                    // and the pair forms fp16(silu(g) * u) for channel c
-                    float gu[16], o[8];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) gu[j] = __half2float(__float2half_rn(v[j] * sc * rs[j]));
-                    int t0;
-                    swiglu_pair16(gu, lane, o, &t0);
-                    if (!nrow) return;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        if (c0 + t0 + j < M) p.C[(int64_t)(c0 + t0 + j) * p.ldc + n / 2] = __float2half_rn(o[j]);
-                    return;
-                }
-                float rv[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    rv[j] = (p.R && nrow && c0 + j < M) ? __half2float(__ldg(p.R + (int64_t)(c0 + j) * p.ldr + n))
-                                                       : 0.0f;
-                __half o[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j) o[j] = __float2half_rn(v[j] * sc * rs[j] + rv[j]);
-                if (nm.ss) {
-                    // the next RMSNorm's partial sums: this warp's 32 rows of C
-                    float sq[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float f = __half2float(o[j]);
-                        sq[j] = (nrow && c0 + j < M) ? f * f : 0.0f;
-                    }
-                    const float tot = warp_colsum16(sq, lane);
-                    const int col = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
-                    if (!(lane & 1) && c0 + col < M)
-                        nm.ss[(int64_t)(sg.tile * 4 + q) * nm.ss_ld + c0 + col] = tot;
-                }
-                if (!nrow) return;
-                const float gm = nm.G ? __half2float(__ldg(nm.gamma + n)) : 0.0f;
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    if (c0 + j < M) {
-                        p.C[(int64_t)(c0 + j) * p.ldc + n] = o[j];
-                        if (nm.G) nm.G[(int64_t)(c0 + j) * nm.ldg + n] = __float2half_rn(__half2float(o[j]) * gm);
-                    }
-                }
-            };
             if (sg.full) {
                 for (int c0 = 0; c0 < BT && c0 < M; c0 += 16) {
                     float v[16];
@@ -588,12 +675,16 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
     }
 
     // Lane 0 alone ran some warps' role loops: a thread-counting barrier.
+    // Cluster split: no CTA leaves before every CTA of its cluster has arrived
+    // (after its last access to another CTA's shared memory).
+    if (C > 1 && !cl_arrived) cluster_arrive();
     tc_fence_before();
     cta_sync_divergent();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
+    if (C > 1) cluster_wait();
 }
 
 template <int BT>
@@ -606,7 +697,55 @@ static int launch(const SkinnyParams& p, int grid, cudaStream_t st) {
         npub_internal_set_cuda_error(e);
         return NPUB_ERR_CUDA;
     }
-    return launch_pdl(kern, dim3(grid), dim3(kThreads), L::kTotal, st, p);
+    if (p.csplit <= 1) return launch_pdl(kern, dim3(grid), dim3(kThreads), L::kTotal, st, p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L::kTotal;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = npub_internal_pdl_enabled() ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)p.csplit;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess) {
+        npub_internal_set_cuda_error(e);
+        return NPUB_ERR_CUDA;
+    }
+    return npub_internal_launch_status();
+}
+
+// Clusters of c stream-K kernels that can be resident at once (0: none).
+template <int BT>
+static int max_clusters(int c) {
+    using L = Smem<BT>;
+    auto kern = w8a16_skinny_kernel<BT>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c * 64);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L::kTotal;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = (unsigned)c;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
 }
 
 }  // namespace skinny
@@ -625,6 +764,35 @@ static int skinny_grid(int N, int K) {
 }
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Cluster split for matrices of few 128-row tiles (the decode step's O and
+// down projections at d = 4096: 32 tiles): C = SMs / tiles CTAs per tile
+// (2..8) when they fill most of the GPU, every cluster can be resident at
+// once and each piece has at least two K steps.  The pieces then meet in the
+// finisher's shared memory instead of global memory (the stream-K partials'
+// store / fence / counter / load chain cost ~5 us per launch behind the
+// weight stream).  NPUB_SKINNY_CLUSTER=0 in the environment keeps stream-K.
+static int skinny_csplit(int bt, int n_tiles, int k_steps) {
+    static const bool off = [] {
+        const char* e = getenv("NPUB_SKINNY_CLUSTER");
+        return e && e[0] == '0';
+    }();
+    const int sms = num_sms();
+    if (off || n_tiles <= 0) return 1;
+    const int c = std::min(8, sms / n_tiles);
+    if (c < 2 || n_tiles * c * 5 < sms * 4 || k_steps < 2 * c) return 1;
+    // the other pieces land in the finisher's int8 ring
+    if ((size_t)(c - 1) * skinny::kRows * bt * sizeof(float) > (size_t)skinny::kS8 * skinny::kRows * skinny::kBK)
+        return 1;
+    static std::mutex mu;
+    static int cache[2][9];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    int& mc = cache[bt == 32 ? 0 : 1][c];
+    if (mc == 0) mc = 1 + (bt == 32 ? skinny::max_clusters<32>(c) : skinny::max_clusters<64>(c));
+    return mc - 1 >= n_tiles ? c : 1;
+}
 
 bool w8a16_skinny_fits(int M, int N) {
     return M > 0 && M <= kSkinnyMaxM && N > 0 &&
@@ -697,7 +865,8 @@ int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, con
     p.wait_ns = npub_internal_wait_limit_ns();
     p.swiglu = swiglu ? 1 : 0;
     if (nrm) p.nrm = *nrm;
-    const int grid = skinny_grid(N, K);
+    p.csplit = skinny_csplit(bt, p.n_tiles, p.k_steps);
+    const int grid = p.csplit > 1 ? p.n_tiles * p.csplit : skinny_grid(N, K);
     return bt == 32 ? skinny::launch<32>(p, grid, st) : skinny::launch<64>(p, grid, st);
 }
 

@@ -48,6 +48,7 @@ struct SkinnyParams {
     uint64_t wait_ns;  // limit of the waits on other CTAs' pieces
     int swiglu;     // 1: rows 2c / 2c+1 are gate / up; C [M, N/2] = fp16(silu(g) * u)
     SkinnyNorm nrm;
+    int csplit;     // > 1: cluster split, grid = n_tiles * csplit (cluster t = tile t)
 };
 
 // Tile counters at the start of every workspace of this kernel: a fixed

@@ -333,3 +333,23 @@ def test_matmul_rms_rejects_many_tokens(cuda_device):
     s = torch.ones(512, dtype=torch.float16, device=cuda_device)
     with pytest.raises(nb.NpubError):
         nb.matmul_rms(A, q, s)
+
+
+@pytest.mark.parametrize("M,N,K", [(32, 4096, 4096), (17, 3072, 3072), (32, 2048, 4096), (5, 4096, 11008),
+                                   (64, 4096, 4096)])
+def test_stream_k_cluster_split_against_oracle(cuda_device, rng, M, N, K):
+    """Matrices of few 128-row tiles run as one cluster per tile (2-8 CTAs
+    splitting K, the pieces summed in the finisher's shared memory): against
+    the oracle, with a residual, and bit-identical from call to call."""
+    A = rng.standard_normal((M, K)).astype(np.float16)
+    R = rng.standard_normal((M, N)).astype(np.float16)
+    W = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    q, s = ref.quantize_w8(W)
+    Ad, Rd, qd, sd = (to_dev(a, cuda_device) for a in (A, R, q, s))
+    got = nb.matmul_rms(Ad, qd, sd, residual=Rd)
+    again = nb.matmul_rms(Ad, qd, sd, residual=Rd)
+    assert torch.equal(got, again)
+    assert ref.rel_err(got.float().cpu().numpy(), ref.w8a16_ref(A, q, s, residual=R)) <= TOL
+    if M <= 32:
+        plain = nb.matmul(Ad, qd, sd).float().cpu().numpy()
+        assert ref.rel_err(plain, ref.w8a16_ref(A, q, s)) <= TOL
