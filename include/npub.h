@@ -356,6 +356,13 @@ size_t npub_comm_handle_bytes(void);
 int npub_comm_create(int world, int rank, size_t max_bytes, void** comm, void* handle_out);
 int npub_comm_open(void* comm, const void* all_handles);
 int npub_allreduce_f16(void* comm, const void* in, void* out, int64_t n, void* stream);
+/* The same sum of a [rows, d] message (d % 32 == 0) with the residual add and
+ * the next RMSNorm's inputs folded in (llama_layer.py:139-141 after the TP
+ * reduction): out = fp16(fp16(sum) + residual), G = fp16(out * gamma) and
+ * ss[(c/32)*ss_ld + r] = sum over the 32 columns c.. of out[r, c]^2 -- the
+ * rs_part of npub_w8a16_gemm_rms. */
+int npub_allreduce_f16_rms(void* comm, const void* in, void* out, int rows, int d, const void* residual,
+                           const void* gamma, void* G, float* ss, int64_t ss_ld, void* stream);
 int npub_comm_destroy(void* comm);
 #ifdef __cplusplus
 }

@@ -82,6 +82,7 @@ SIGNATURES = {
     "npub_comm_create": (_i, [_i, _i, _sz, ctypes.POINTER(ctypes.c_void_p), _p]),
     "npub_comm_open": (_i, [_p, _p]),
     "npub_allreduce_f16": (_i, [_p, _p, _p, _i64, _p]),
+    "npub_allreduce_f16_rms": (_i, [_p, _p, _p, _i, _i, _p, _p, _p, _p, _i64, _p]),
     "npub_comm_destroy": (_i, [_p]),
 }
 

@@ -50,6 +50,17 @@ class PeerAllReduce:
         _lib.call("npub_allreduce_f16", self._comm, t.data_ptr(), t.data_ptr(), t.numel(),
                   torch.cuda.current_stream(t.device).cuda_stream)
 
+    def all_reduce_rms(self, t: torch.Tensor, residual: torch.Tensor, gamma: torch.Tensor, out: torch.Tensor,
+                       g_out: torch.Tensor, ss_out: torch.Tensor) -> None:
+        """out = fp16(sum over ranks of t) + residual, g_out = fp16(out * gamma),
+        ss_out [d/32, rows] the sums of out^2 per 32 columns (t: [rows, d])."""
+        rows, d = t.shape
+        for x in (residual, out, g_out):
+            assert x.shape == t.shape and x.is_contiguous() and x.dtype == torch.float16
+        _lib.call("npub_allreduce_f16_rms", self._comm, t.data_ptr(), out.data_ptr(), rows, d, residual.data_ptr(),
+                  gamma.data_ptr(), g_out.data_ptr(), ss_out.data_ptr(), ss_out.stride(0),
+                  torch.cuda.current_stream(t.device).cuda_stream)
+
     def close(self) -> None:
         if self._comm:
             _lib.load().npub_comm_destroy(self._comm)

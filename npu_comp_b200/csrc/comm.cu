@@ -51,9 +51,22 @@ struct Comm {
 };
 
 // n elements (multiple of 8), 16-byte aligned in and out.
+// Optional RMSNorm inputs for the next projection (nrm.resid != NULL): out =
+// fp16(fp16(sum) + resid) -- the residual add of the separate RMSNorm -- and
+// G = fp16(out * gamma[col]), ss[(col / 32) * ss_ld + row] = sum over the 32
+// columns of out^2, for a [rows, d] message (npub_w8a16_gemm_rms consumes them).
+struct CommNorm {
+    const __half* resid;
+    const __half* gamma;
+    __half* G;
+    float* ss;
+    int64_t ss_ld;
+    int d;
+};
+
 __global__ void __launch_bounds__(kCommThreads) allreduce_oneshot_kernel(const CommDev c, const __half* in,
                                                                         __half* out, int64_t n, int* err,
-                                                                        uint64_t limit_ns) {
+                                                                        uint64_t limit_ns, const CommNorm nrm) {
     pdl_trigger();
     pdl_wait();
     __shared__ int ok_s;
@@ -92,7 +105,59 @@ __global__ void __launch_bounds__(kCommThreads) allreduce_oneshot_kernel(const C
         }
     }
     cta_sync_divergent();  // lanes < world spun alone
-    if (ok_s) {
+    if (ok_s && nrm.resid) {
+        // 4'. the sum, the residual add and the next RMSNorm's inputs; a warp
+        // walks 32 consecutive vectors per step (4 lanes = 32 columns)
+        const int lane = threadIdx.x & 31;
+        for (int64_t base = v0 + (threadIdx.x & ~31); base < v1; base += blockDim.x) {
+            const int64_t i = base + lane;
+            const bool valid = i < v1;
+            float h[8], sq = 0.0f;
+            if (valid) {
+                uint4 u[kCommMaxRanks];
+#pragma unroll
+                for (int r = 0; r < kCommMaxRanks; ++r)
+                    if (r < c.world) u[r] = ld_relaxed_sys_v4(reinterpret_cast<const uint4*>(c.data[r] + off) + i);
+                float acc[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) acc[k] = 0.0f;
+#pragma unroll
+                for (int r = 0; r < kCommMaxRanks; ++r) {
+                    if (r >= c.world) break;
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&u[r]);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float2 f = __half22float2(h2[k]);
+                        acc[2 * k] += f.x;
+                        acc[2 * k + 1] += f.y;
+                    }
+                }
+                const uint4 rv = reinterpret_cast<const uint4*>(nrm.resid)[i];
+                const __half* rh = reinterpret_cast<const __half*>(&rv);
+                uint4 o, g;
+                __half* oh = reinterpret_cast<__half*>(&o);
+                __half* gh = reinterpret_cast<__half*>(&g);
+                const int64_t col = (i * 8) % nrm.d;
+                const uint4 gv = *reinterpret_cast<const uint4*>(nrm.gamma + col);
+                const __half* gm = reinterpret_cast<const __half*>(&gv);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    oh[k] = __float2half_rn(__half2float(__float2half_rn(acc[k])) + __half2float(rh[k]));
+                    h[k] = __half2float(oh[k]);
+                    gh[k] = __float2half_rn(h[k] * __half2float(gm[k]));
+                    sq += h[k] * h[k];
+                }
+                reinterpret_cast<uint4*>(out)[i] = o;
+                reinterpret_cast<uint4*>(nrm.G)[i] = g;
+            }
+            sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+            sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+            if (valid && (lane & 3) == 0) {
+                const int64_t e = i * 8;
+                nrm.ss[(e % nrm.d) / 32 * nrm.ss_ld + e / nrm.d] = sq;
+            }
+        }
+    } else if (ok_s) {
         // 4. sum slice b over the ranks, in rank order
         for (int64_t i = v0 + threadIdx.x; i < v1; i += blockDim.x) {
             // every rank's vector in flight before the first is added
@@ -192,7 +257,7 @@ extern "C" int npub_comm_open(void* comm, const void* all_handles) {
     return NPUB_OK;
 }
 
-extern "C" int npub_allreduce_f16(void* comm, const void* in, void* out, int64_t n, void* stream) {
+static int allreduce_launch(void* comm, const void* in, void* out, int64_t n, const CommNorm& nrm, void* stream) {
     NPUB_CHECK_ARG(comm && n >= 0);
     if (n == 0) return NPUB_OK;
     Comm* c = reinterpret_cast<Comm*>(comm);
@@ -201,11 +266,34 @@ extern "C" int npub_allreduce_f16(void* comm, const void* in, void* out, int64_t
     NPUB_CHECK_ARG(c->d.data[0] != nullptr);  // npub_comm_open done
     // one block per fixed region the message reaches
     const int64_t region = (int64_t)(c->max_bytes / sizeof(__half)) / kCommMaxBlocks;
+    if (nrm.resid) NPUB_CHECK_ARG(region % 32 == 0);  // a block's slice is whole 32-column chunks
     const int64_t blocks = (n + region - 1) / region;
     return launch_pdl(allreduce_oneshot_kernel, dim3((unsigned)blocks), dim3(kCommThreads), 0,
                       reinterpret_cast<cudaStream_t>(stream), c->d, reinterpret_cast<const __half*>(in),
                       reinterpret_cast<__half*>(out), n, npub_internal_device_error_word(),
-                      npub_internal_wait_limit_ns());
+                      npub_internal_wait_limit_ns(), nrm);
+}
+
+extern "C" int npub_allreduce_f16(void* comm, const void* in, void* out, int64_t n, void* stream) {
+    CommNorm nrm;
+    memset(&nrm, 0, sizeof(nrm));
+    return allreduce_launch(comm, in, out, n, nrm, stream);
+}
+
+extern "C" int npub_allreduce_f16_rms(void* comm, const void* in, void* out, int rows, int d, const void* residual,
+                                      const void* gamma, void* G, float* ss, int64_t ss_ld, void* stream) {
+    NPUB_CHECK_ARG(rows >= 0 && d > 0 && d % 32 == 0);
+    if (rows == 0) return NPUB_OK;
+    NPUB_CHECK_ARG(residual && gamma && G && ss && ss_ld >= rows);
+    NPUB_CHECK_ARG(npub_aligned(residual, 16) && npub_aligned(gamma, 16) && npub_aligned(G, 16));
+    CommNorm nrm;
+    nrm.resid = reinterpret_cast<const __half*>(residual);
+    nrm.gamma = reinterpret_cast<const __half*>(gamma);
+    nrm.G = reinterpret_cast<__half*>(G);
+    nrm.ss = ss;
+    nrm.ss_ld = ss_ld;
+    nrm.d = d;
+    return allreduce_launch(comm, in, out, (int64_t)rows * d, nrm, stream);
 }
 
 extern "C" int npub_comm_destroy(void* comm) {

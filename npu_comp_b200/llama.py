@@ -372,7 +372,7 @@ def layer_decode(x: torch.Tensor, w: LayerWeights, cfg: LlamaConfig, k_cache: to
         g, ss = npu.rmsnorm_parts(x, w.g1, g_out=sc.get("dgA", (B, d), device=dev),
                                   ss_out=sc.get("dssA", (d // 32, B), torch.float32, dev))
         y, _, _ = layer_decode_folded(x, g, ss, w, cfg, k_cache, v_cache, pos, ctx_max=ctx_max, scratch=sc, out=out,
-                                      mk=mk)
+                                      mk=mk, tp=tp)
         mk.end()
         return y
     mk = _Marks(events)
@@ -420,23 +420,31 @@ def folded_norm_ok(cfg: LlamaConfig, batch: int, tp: TP) -> bool:
     (graph replay): a batch-32 Llama-7B decode layer step 222.7 -> 208.3 us,
     the stack's 128 decode steps 886.1 -> 835.8 ms; at batch 64, where the
     square and K-long projections run faster on the pair kernel, 752.8 ->
-    765.7 us (so not there).  NPUB_FOLD_RMSNORM=0 in the environment keeps the
-    separate RMSNorm launches."""
-    return (tp.size == 1 and batch <= 32 and cfg.d % 32 == 0 and
-            os.environ.get("NPUB_FOLD_RMSNORM", "1") != "0")
+    765.7 us (so not there).  Under tensor parallelism the folding needs the
+    peer all-reduce (npu_comp_b200.comm): it adds the residual and leaves the
+    next RMSNorm's inputs itself.  NPUB_FOLD_RMSNORM=0 in the environment keeps
+    the separate RMSNorm launches."""
+    if os.environ.get("NPUB_FOLD_RMSNORM", "1") == "0" or batch > 32 or cfg.d % 32:
+        return False
+    if tp.size == 1:
+        return True
+    return tp.peer is not None and batch * cfg.d * 2 <= tp.peer.max_bytes
 
 
 def layer_decode_folded(h: torch.Tensor, g: torch.Tensor, ss: torch.Tensor, w: LayerWeights, cfg: LlamaConfig,
                         k_cache: torch.Tensor, v_cache: torch.Tensor, pos: torch.Tensor, *, ctx_max: int,
                         scratch: Scratch, gamma_next: Optional[torch.Tensor] = None,
                         out: Optional[torch.Tensor] = None, out_g: Optional[torch.Tensor] = None,
-                        out_ss: Optional[torch.Tensor] = None, mk=None):
+                        out_ss: Optional[torch.Tensor] = None, mk=None, tp: TP = TP()):
     """One decode step of a layer (llama_layer.py:71-152) with both RMSNorms
     folded into the GEMMs: h is the residual stream entering the layer and
     (g, ss) = rmsnorm_parts(h, w.g1) or the previous layer's down projection's
     outputs.  The O projection adds h and leaves (h2, g2, ss2) for the gate|up
     projection; the down projection adds h2 and, with gamma_next (the next
-    RMSNorm's weight), leaves (g, ss) for the next layer.  Returns (y, g', ss')."""
+    RMSNorm's weight), leaves (g, ss) for the next layer.  Returns (y, g', ss').
+    Under tensor parallelism the row-parallel O and down projections store
+    their partial sums and the peer all-reduce adds the residual and makes
+    the next RMSNorm's inputs."""
     sc = scratch
     mk = mk or _Marks(None)
     dev = h.device
@@ -455,14 +463,27 @@ def layer_decode_folded(h: torch.Tensor, g: torch.Tensor, ss: torch.Tensor, w: L
     ctx = npu.attention_decode(q, k_cache, v_cache, heads=hq, kv_heads=hk, lens=lens, ctx_len=ctx_max,
                                out=sc.get("dctx", (B, hq * hd), device=dev))
     mk("o_gemm")
-    h2, g2, ss2 = npu.matmul_rms(ctx, w.wo, w.so, residual=h, gamma=w.g2, out=sc.get("dh", (B, d), device=dev),
-                                 g_out=sc.get("dg2", (B, d), device=dev),
-                                 ss_out=sc.get("dss2", (d // 32, B), torch.float32, dev))
+    h2, g2, ss2 = sc.get("dh", (B, d), device=dev), sc.get("dg2", (B, d), device=dev), \
+        sc.get("dss2", (d // 32, B), torch.float32, dev)
+    if tp.size > 1:
+        part = npu.matmul(ctx, w.wo, w.so, out=sc.get("dattn", (B, d), device=dev))
+        mk("all_reduce")
+        tp.peer.all_reduce_rms(part, h, w.g2, h2, g2, ss2)
+    else:
+        npu.matmul_rms(ctx, w.wo, w.so, residual=h, gamma=w.g2, out=h2, g_out=g2, ss_out=ss2)
     mk("gate_up_gemm")
     a = npu.matmul_rms(g2, w.wgu, w.sgu, swiglu=True, rs=(ss2, d), eps=cfg.eps,
                        out=sc.get("dact", (B, w.ffn), device=dev))
     mk("down_gemm")
     y = out if out is not None else torch.empty((B, d), dtype=torch.float16, device=dev)
+    if tp.size > 1:
+        part = npu.matmul(a, w.wd, w.sd, out=sc.get("dffn", (B, d), device=dev))
+        mk("all_reduce")
+        gn = out_g if out_g is not None else sc.get("dgn", (B, d), device=dev)
+        ssn = out_ss if out_ss is not None else sc.get("dssn", (d // 32, B), torch.float32, dev)
+        # without a next norm (the last layer) the inputs are made and not used
+        tp.peer.all_reduce_rms(part, h2, gamma_next if gamma_next is not None else w.g1, y, gn, ssn)
+        return (y, gn, ssn) if gamma_next is not None else (y, None, None)
     if gamma_next is None:
         npu.matmul_rms(a, w.wd, w.sd, residual=h2, out=y)
         return y, None, None
@@ -620,7 +641,7 @@ class LlamaStack:
                     h, g, ss, lw, cfg, self.kc[i], self.vc[i], self.pos, ctx_max=self.cap, scratch=sc,
                     gamma_next=nxt, out=sc.get(f"sh{j}", (B, d), device=dev),
                     out_g=sc.get(f"sg{j}", (B, d), device=dev),
-                    out_ss=sc.get(f"sss{j}", (d // 32, B), torch.float32, dev))
+                    out_ss=sc.get(f"sss{j}", (d // 32, B), torch.float32, dev), tp=self.tp)
             self._next_ids(h)
             self.pos.add_(1)
             return

@@ -225,3 +225,47 @@ def test_peer_wait_gives_up_and_both_gpus_stay_usable():
     assert r0[3] == 1                      # rank 0's output was left as it was
     assert r1[3] == 1                      # the late call completed with both ranks' data
     assert r0[2] == 1 and r1[2] == 1
+
+
+def _ar_rms_worker(rank, world, port, q):
+    import torch.distributed as dist
+    dev = _init(rank, world, port)
+    from npu_comp_b200 import comm
+    try:
+        peer = comm.PeerAllReduce(dist.group.WORLD, dev, max_bytes=1 << 20)
+        g = torch.Generator(device=dev).manual_seed(11)   # the same residual / gamma on every rank
+        rows, d = 32, 4096
+        res = torch.randn((rows, d), generator=g, device=dev).half()
+        gam = (1 + 0.1 * torch.randn(d, generator=g, device=dev)).half()
+        gr = torch.Generator(device=dev).manual_seed(100 + rank)
+        part = torch.randn((rows, d), generator=gr, device=dev).half()
+        out, G = torch.empty_like(part), torch.empty_like(part)
+        ss = torch.empty((d // 32, rows), dtype=torch.float32, device=dev)
+        peer.all_reduce_rms(part, res, gam, out, G, ss)
+        # the plain all-reduce of the same partials, then the residual add in torch
+        s = part.clone()
+        peer.all_reduce_(s)
+        torch.cuda.synchronize()
+        want = (s.float() + res.float()).half()
+        ok_out = torch.equal(out, want)
+        ok_g = torch.equal(G, (out.float() * gam.float()).half())
+        ssr = (out.double() ** 2).view(rows, d // 32, 32).sum(-1).t()
+        ss_err = ((ss.double() - ssr).abs().max() / ssr.abs().max()).item()
+        allo = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(allo, out)
+        same = all(torch.equal(allo[0], o) for o in allo)
+        dist.barrier()
+        peer.close()
+        if rank == 0:
+            q.put((ok_out, ok_g, ss_err, same))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_allreduce_rms_2gpu():
+    """npub_allreduce_f16_rms on 2 GPUs: out = fp16(sum) + residual bit for bit
+    against the plain all-reduce and a torch add, G = fp16(out * gamma) bit for
+    bit, the per-32-column sums of out^2, the same bits on every rank."""
+    ok_out, ok_g, ss_err, same = _run(_ar_rms_worker, 2, timeout=300)
+    assert ok_out and ok_g and same
+    assert ss_err <= 1e-5, ss_err
