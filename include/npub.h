@@ -104,14 +104,17 @@ int npub_w8a16_gemm_swiglu(const void* A, int64_t lda, const int8_t* Wq, int64_t
  *     plus G = fp16(C * gamma) [M, N] and ss[(n/32)*ss_ld + t] = sum of C[t, n]^2
  *     over the 32 columns n/32 -- the rs_part (rs_n = N / 32) of the next call.
  * npub_rmsnorm_parts() makes G and ss for a stream that no GEMM produced.
+ * Wq_next (may be NULL): the next GEMM of a decode chain (same M, int8
+ * [N_next, K_next], row stride ldw_next), whose first weight tiles this call
+ * prefetches to L2 while its own MMAs run.
  * Returns NPUB_ERR_UNSUPPORTED for M > 64.  Workspace:
  * npub_w8a16_gemm_rms_workspace(M, N, K) bytes whose first 64 KiB are zero
  * before the first call (every call leaves them zero). */
 int npub_w8a16_gemm_rms(const void* A, int64_t lda, const int8_t* Wq, int64_t ldw, const void* scale, void* C,
                         int64_t ldc, const void* R, int64_t ldr, int M, int N, int K, int swiglu,
                         const float* rs_part, int rs_n, int64_t rs_ld, int rs_d, float rs_eps, const void* gamma,
-                        void* G, int64_t ldg, float* ss, int64_t ss_ld, void* workspace, size_t workspace_bytes,
-                        void* stream);
+                        void* G, int64_t ldg, float* ss, int64_t ss_ld, const int8_t* Wq_next, int64_t ldw_next,
+                        int N_next, int K_next, void* workspace, size_t workspace_bytes, void* stream);
 size_t npub_w8a16_gemm_rms_workspace(int M, int N, int K);
 
 /* Name of the kernel npub_w8a16_gemm runs for this shape (static storage):

@@ -39,7 +39,7 @@ SIGNATURES = {
     "npub_w8a16_gemm_workspace": (_sz, [_i, _i, _i]),
     "npub_w8a16_gemm_swiglu": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _i, _i, _i, _p, _sz, _p]),
     "npub_w8a16_gemm_rms": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _p, _i64, _i, _i, _i, _i,
-                                 _p, _i, _i64, _i, _f, _p, _p, _i64, _p, _i64, _p, _sz, _p]),
+                                 _p, _i, _i64, _i, _f, _p, _p, _i64, _p, _i64, _p, _i64, _i, _i, _p, _sz, _p]),
     "npub_w8a16_gemm_rms_workspace": (_sz, [_i, _i, _i]),
     "npub_w8a16_kernel_name": (ctypes.c_char_p, [_i, _i, _i]),
     "npub_w8a16_gemm_noalloc": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _p, _i64, _i, _i, _i, _f, _p]),

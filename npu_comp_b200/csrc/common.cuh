@@ -164,6 +164,14 @@ __device__ __forceinline__ uint4 ld_relaxed_sys_v4(const void* p) {
     return v;
 }
 
+// L2 prefetch of one 3-D tile of a tensor map (no shared memory written).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* m, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                     reinterpret_cast<uint64_t>(m)),
+                 "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+
 // 3-D tiled TMA load (no multicast) completing on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, uint64_t* bar, int c0, int c1, int c2) {
     asm volatile(

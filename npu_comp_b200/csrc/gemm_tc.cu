@@ -611,7 +611,10 @@ extern "C" int npub_w8a16_gemm_swiglu(const void* A, int64_t lda, const int8_t* 
 //     result is scaled by rsqrt(sum_{i < rs_n} rs_part[i rs_ld + t] / rs_d + eps);
 //   producer: C = fp16(A Wq^T * scale + R) as npub_w8a16_gemm, plus
 //     G = fp16(C * gamma) and the sums of C^2 over every 32 output columns
-//     (ss[(n / 32) ss_ld + t]) for the next GEMM to consume.
+//     (ss[(n / 32) ss_ld + t]) for the next GEMM to consume;
+//   Wq_next (optional): the next W8A16 GEMM of the chain (same M, int8
+//     [N_next, K_next]); its first weight tiles are prefetched to L2 once this
+//     GEMM's own weights are requested.
 extern "C" size_t npub_w8a16_gemm_rms_workspace(int M, int N, int K) {
     return npub::w8a16_skinny_workspace(M, N, K);
 }
@@ -620,6 +623,7 @@ extern "C" int npub_w8a16_gemm_rms(const void* A, int64_t lda, const int8_t* Wq,
                                    void* C, int64_t ldc, const void* R, int64_t ldr, int M, int N, int K, int swiglu,
                                    const float* rs_part, int rs_n, int64_t rs_ld, int rs_d, float rs_eps,
                                    const void* gamma, void* G, int64_t ldg, float* ss, int64_t ss_ld,
+                                   const int8_t* Wq_next, int64_t ldw_next, int N_next, int K_next,
                                    void* workspace, size_t workspace_bytes, void* stream) {
     NPUB_CHECK_ARG(M >= 0 && N >= 0 && K >= 0);
     if (M == 0 || N == 0) return NPUB_OK;
@@ -646,8 +650,15 @@ extern "C" int npub_w8a16_gemm_rms(const void* A, int64_t lda, const int8_t* Wq,
     nrm.ldg = ldg;
     nrm.ss = ss;
     nrm.ss_ld = ss_ld;
+    npub::SkinnyNext nx;
+    nx.W = Wq_next;
+    nx.ldw = ldw_next;
+    nx.M = M;
+    nx.N = N_next;
+    nx.K = K_next;
     return npub::w8a16_skinny_run(A, lda, Wq, ldw, scale, C, ldc, R, ldr, M, N, K, 1.0f, workspace, workspace_bytes,
-                                  reinterpret_cast<cudaStream_t>(stream), swiglu ? 1 : 0, &nrm);
+                                  reinterpret_cast<cudaStream_t>(stream), swiglu ? 1 : 0, &nrm,
+                                  Wq_next ? &nx : nullptr);
 }
 
 extern "C" const char* npub_w8a16_kernel_name(int M, int N, int K) {

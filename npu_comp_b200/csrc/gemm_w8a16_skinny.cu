@@ -67,6 +67,7 @@ constexpr int kBK = 256;     // K per unit: two 128-byte swizzled int8 boxes per
 constexpr int kBox8 = 128;   // int8 bytes of a row per TMA box (the 128-byte swizzle span)
 constexpr int kS8 = 4;       // int8 ring depth (32 KB stages)
 constexpr int kSA = 3;       // fp16 weight stages in TMEM (kBK / 2 columns each)
+constexpr int kPfUnits = 2;  // units of the next GEMM's CTAs prefetched to L2
 constexpr int kConvWarps = 8;  // every converter warp works on every K step (half a row each)
 constexpr int kAcols = kBK / 2;
 constexpr int kAcol0 = 128;  // first TMEM column of the A stages (accumulators use [0, 2 BT) <= 128)
@@ -294,6 +295,29 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                         for (int c = 0; c < kBK / 64; ++c)
                             tma_load_3d(sTok + s * L::kTok + c * L::kTokChunk, &p.tmX, &full[s], k + 64 * c, 0, 0);
                     }
+                }
+            }
+            if (weights && p.pf_grid > 0 && ok) {
+                // this kernel's weights are all requested (it is MMA-bound, HBM has
+                // room): the first units of the next GEMM's CTAs
+                // [c G' / G, (c + 1) G' / G) go to L2 for its start
+                prefetch_tmap(&p.tmWn);
+                const int64_t G2 = p.pf_grid, KT2 = p.pf_ksteps, U2 = (int64_t)p.pf_tiles * KT2;
+                const int cs = p.pf_csplit;
+                for (int64_t c2 = (int64_t)blockIdx.x * G2 / G; c2 < ((int64_t)blockIdx.x + 1) * G2 / G; ++c2) {
+                    int64_t a, e;
+                    if (cs > 1) {
+                        const int64_t t2 = c2 / cs, r2 = c2 % cs;
+                        a = t2 * KT2 + r2 * KT2 / cs;
+                        e = t2 * KT2 + (r2 + 1) * KT2 / cs;
+                    } else {
+                        a = unit_start(c2, U2, G2);
+                        e = unit_start(c2 + 1, U2, G2);
+                    }
+                    for (int64_t u = a; u < e && u < a + kPfUnits; ++u)
+#pragma unroll
+                        for (int c = 0; c < kBK / kBox8; ++c)
+                            tma_prefetch_3d(&p.tmWn, (int)(u % KT2) * kBK + c * kBox8, (int)(u / KT2) * kRows, 0);
                 }
             }
             // Every load issued has landed before the CTA may exit.
@@ -834,7 +858,7 @@ size_t w8a16_skinny_workspace(int M, int N, int K) {
 
 int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C, int64_t ldc,
                      const void* R, int64_t ldr, int M, int N, int K, float alpha, void* ws, size_t ws_bytes,
-                     cudaStream_t st, int swiglu, const SkinnyNorm* nrm) {
+                     cudaStream_t st, int swiglu, const SkinnyNorm* nrm, const SkinnyNext* next) {
     if (!w8a16_skinny_fits(M, N)) return NPUB_ERR_INVALID_ARG;
     if (swiglu && (N % 2 || R)) return NPUB_ERR_INVALID_ARG;
     const size_t need = w8a16_skinny_workspace(M, N, K);
@@ -867,6 +891,16 @@ int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, con
     if (nrm) p.nrm = *nrm;
     p.csplit = skinny_csplit(bt, p.n_tiles, p.k_steps);
     const int grid = p.csplit > 1 ? p.n_tiles * p.csplit : skinny_grid(N, K);
+    if (next && next->W && w8a16_skinny_fits(next->M, next->N) && next->K > 0 && next->K % 16 == 0 &&
+        next->ldw >= next->K && next->ldw % 16 == 0 && npub_aligned(next->W, 16)) {
+        rc = make_tmap_3d(&p.tmWn, true, next->W, (uint64_t)next->K, (uint64_t)next->N, 1, (uint64_t)next->ldw,
+                          (uint64_t)next->ldw * next->N, skinny::kRows, 1, true, skinny::kBox8);
+        if (rc) return rc;
+        p.pf_tiles = (next->N + skinny::kRows - 1) / skinny::kRows;
+        p.pf_ksteps = (next->K + skinny::kBK - 1) / skinny::kBK;
+        p.pf_csplit = skinny_csplit(skinny_bt(next->M), p.pf_tiles, p.pf_ksteps);
+        p.pf_grid = p.pf_csplit > 1 ? p.pf_tiles * p.pf_csplit : skinny_grid(next->N, next->K);
+    }
     return bt == 32 ? skinny::launch<32>(p, grid, st) : skinny::launch<64>(p, grid, st);
 }
 

@@ -32,6 +32,14 @@ struct SkinnyNorm {
     int64_t ss_ld;
 };
 
+// The next stream-K GEMM of a chain (all null: none): its first weight tiles
+// are prefetched to L2 once this kernel's own weights are requested.
+struct SkinnyNext {
+    const void* W;
+    int64_t ldw;
+    int M, N, K;
+};
+
 struct SkinnyParams {
     CUtensorMap tmW;  // int8 weights [N, K]: box {128, 128, 1}, 128-byte swizzle
     CUtensorMap tmX;  // fp16 activations [M, K]: box {64, BT, 1}, 128-byte swizzle
@@ -49,6 +57,8 @@ struct SkinnyParams {
     int swiglu;     // 1: rows 2c / 2c+1 are gate / up; C [M, N/2] = fp16(silu(g) * u)
     SkinnyNorm nrm;
     int csplit;     // > 1: cluster split, grid = n_tiles * csplit (cluster t = tile t)
+    CUtensorMap tmWn;  // the next GEMM's weights (pf_grid > 0)
+    int pf_grid, pf_csplit, pf_tiles, pf_ksteps;
 };
 
 // Tile counters at the start of every workspace of this kernel: a fixed
@@ -61,6 +71,7 @@ bool w8a16_use_skinny(int M, int N, int K);
 size_t w8a16_skinny_workspace(int M, int N, int K);
 int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, const void* scale, void* C, int64_t ldc,
                      const void* R, int64_t ldr, int M, int N, int K, float alpha, void* ws, size_t ws_bytes,
-                     cudaStream_t st, int swiglu = 0, const SkinnyNorm* nrm = nullptr);
+                     cudaStream_t st, int swiglu = 0, const SkinnyNorm* nrm = nullptr,
+                     const SkinnyNext* next = nullptr);
 
 }  // namespace npub

@@ -435,7 +435,8 @@ def layer_decode_folded(h: torch.Tensor, g: torch.Tensor, ss: torch.Tensor, w: L
                         k_cache: torch.Tensor, v_cache: torch.Tensor, pos: torch.Tensor, *, ctx_max: int,
                         scratch: Scratch, gamma_next: Optional[torch.Tensor] = None,
                         out: Optional[torch.Tensor] = None, out_g: Optional[torch.Tensor] = None,
-                        out_ss: Optional[torch.Tensor] = None, mk=None, tp: TP = TP()):
+                        out_ss: Optional[torch.Tensor] = None, mk=None, tp: TP = TP(),
+                        w_next: Optional[LayerWeights] = None):
     """One decode step of a layer (llama_layer.py:71-152) with both RMSNorms
     folded into the GEMMs: h is the residual stream entering the layer and
     (g, ss) = rmsnorm_parts(h, w.g1) or the previous layer's down projection's
@@ -444,8 +445,11 @@ def layer_decode_folded(h: torch.Tensor, g: torch.Tensor, ss: torch.Tensor, w: L
     RMSNorm's weight), leaves (g, ss) for the next layer.  Returns (y, g', ss').
     Under tensor parallelism the row-parallel O and down projections store
     their partial sums and the peer all-reduce adds the residual and makes
-    the next RMSNorm's inputs."""
+    the next RMSNorm's inputs.  Each GEMM prefetches the first weight tiles of
+    the next one to L2 (w_next: the next layer, for its QKV projection);
+    NPUB_PREFETCH_NEXT=0 in the environment turns that off."""
     sc = scratch
+    pf = os.environ.get("NPUB_PREFETCH_NEXT", "1") != "0"
     mk = mk or _Marks(None)
     dev = h.device
     B, d = h.shape
@@ -470,10 +474,11 @@ def layer_decode_folded(h: torch.Tensor, g: torch.Tensor, ss: torch.Tensor, w: L
         mk("all_reduce")
         tp.peer.all_reduce_rms(part, h, w.g2, h2, g2, ss2)
     else:
-        npu.matmul_rms(ctx, w.wo, w.so, residual=h, gamma=w.g2, out=h2, g_out=g2, ss_out=ss2)
+        npu.matmul_rms(ctx, w.wo, w.so, residual=h, gamma=w.g2, out=h2, g_out=g2, ss_out=ss2,
+                       prefetch_next=w.wgu if pf else None)
     mk("gate_up_gemm")
     a = npu.matmul_rms(g2, w.wgu, w.sgu, swiglu=True, rs=(ss2, d), eps=cfg.eps,
-                       out=sc.get("dact", (B, w.ffn), device=dev))
+                       out=sc.get("dact", (B, w.ffn), device=dev), prefetch_next=w.wd if pf else None)
     mk("down_gemm")
     y = out if out is not None else torch.empty((B, d), dtype=torch.float16, device=dev)
     if tp.size > 1:
@@ -484,10 +489,12 @@ def layer_decode_folded(h: torch.Tensor, g: torch.Tensor, ss: torch.Tensor, w: L
         # without a next norm (the last layer) the inputs are made and not used
         tp.peer.all_reduce_rms(part, h2, gamma_next if gamma_next is not None else w.g1, y, gn, ssn)
         return (y, gn, ssn) if gamma_next is not None else (y, None, None)
+    nxt = w_next.wqkv if (pf and w_next is not None) else None
     if gamma_next is None:
-        npu.matmul_rms(a, w.wd, w.sd, residual=h2, out=y)
+        npu.matmul_rms(a, w.wd, w.sd, residual=h2, out=y, prefetch_next=nxt)
         return y, None, None
-    _, gn, ssn = npu.matmul_rms(a, w.wd, w.sd, residual=h2, gamma=gamma_next, out=y, g_out=out_g, ss_out=out_ss)
+    _, gn, ssn = npu.matmul_rms(a, w.wd, w.sd, residual=h2, gamma=gamma_next, out=y, g_out=out_g, ss_out=out_ss,
+                                prefetch_next=nxt)
     return y, gn, ssn
 
 
@@ -641,7 +648,8 @@ class LlamaStack:
                     h, g, ss, lw, cfg, self.kc[i], self.vc[i], self.pos, ctx_max=self.cap, scratch=sc,
                     gamma_next=nxt, out=sc.get(f"sh{j}", (B, d), device=dev),
                     out_g=sc.get(f"sg{j}", (B, d), device=dev),
-                    out_ss=sc.get(f"sss{j}", (d // 32, B), torch.float32, dev), tp=self.tp)
+                    out_ss=sc.get(f"sss{j}", (d // 32, B), torch.float32, dev), tp=self.tp,
+                    w_next=self.w.layers[i + 1] if i + 1 < L else None)
             self._next_ids(h)
             self.pos.add_(1)
             return

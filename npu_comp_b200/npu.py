@@ -225,7 +225,7 @@ def matmul_rms(A: torch.Tensor, Wq: torch.Tensor, scale: torch.Tensor, *, out: O
                residual: Optional[torch.Tensor] = None, swiglu: bool = False,
                rs: Optional[Tuple[torch.Tensor, int]] = None, eps: float = 1e-5,
                gamma: Optional[torch.Tensor] = None, g_out: Optional[torch.Tensor] = None,
-               ss_out: Optional[torch.Tensor] = None):
+               ss_out: Optional[torch.Tensor] = None, prefetch_next: Optional[torch.Tensor] = None):
     """W8A16 GEMM of a decode step (M <= 64) with an RMSNorm folded in
     (npub_w8a16_gemm_rms): the RMSNorm -> projection pairs of a decode layer
     without the normalised activations' round trip or their own launch.
@@ -235,7 +235,9 @@ def matmul_rms(A: torch.Tensor, Wq: torch.Tensor, scale: torch.Tensor, *, out: O
     1 / sqrt(sum(ss[:, t]) / d + eps) before rounding (before SwiGLU with
     swiglu=True, where Wq holds interleaved gate/up rows and out is [M, N/2]).
     gamma: also return (out, g_out, ss_out) -- g_out = fp16(out * gamma) and
-    ss_out [N/32, M] fp32, the next call's rs.  Raises NpubError for M > 64."""
+    ss_out [N/32, M] fp32, the next call's rs.  prefetch_next: the int8 weights
+    of the next GEMM of a decode chain (same M), whose first tiles go to L2
+    while this GEMM runs.  Raises NpubError for M > 64."""
     lda = _mat(A, "A", torch.float16)
     ldw = _mat(Wq, "Wq", torch.int8)
     M, K = A.shape
@@ -274,7 +276,10 @@ def matmul_rms(A: torch.Tensor, Wq: torch.Tensor, scale: torch.Tensor, *, out: O
     _lib.call("npub_w8a16_gemm_rms", A.data_ptr(), lda, Wq.data_ptr(), ldw, scale.data_ptr(), out.data_ptr(), ldc,
               _ptr(residual), ldr, M, N, K, 1 if swiglu else 0, _ptr(rs_p), rs_n, rs_ld, int(rs_d), float(eps),
               _ptr(gamma), _ptr(g_out if gamma is not None else None), ldg,
-              _ptr(ss_out if gamma is not None else None), ss_ld, _ptr(ws), wsb, _stream())
+              _ptr(ss_out if gamma is not None else None), ss_ld, _ptr(prefetch_next),
+              prefetch_next.stride(0) if prefetch_next is not None else 0,
+              prefetch_next.shape[0] if prefetch_next is not None else 0,
+              prefetch_next.shape[1] if prefetch_next is not None else 0, _ptr(ws), wsb, _stream())
     return out if gamma is None else (out, g_out, ss_out)
 
 
