@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_attn_kernel(const Decod
 //    its combine pass (measured 4-14 % faster where that needed splits).
 constexpr int kStKeys = 64;
 constexpr int kStBytes = kStKeys * kDecHd * 2;  // one of K or V per stage
-constexpr int kStStages = 3;
+// K/V ring depth NS (a template argument): 2 or 3 stages, chosen per call.
 constexpr int kStWarps = 8;                     // compute warps; warp 8 is the producer
 constexpr int kStKeysPerWarp = kStKeys / kStWarps;  // 8: four pairs of keys per stage
 constexpr int kStThreads = (kStWarps + 1) * 32;
@@ -235,20 +235,20 @@ constexpr int kPsMaxCtas = 1024;
 // item's finisher, so every completed call leaves them zero.
 __device__ uint32_t g_decode_piece_flag[kPsMaxCtas];
 
-template <int G>
+template <int G, int NS>
 constexpr int stream_smem() {
-    return kStStages * 2 * kStBytes + 16 * kStStages + 128;
+    return NS * 2 * kStBytes + 16 * NS + 128;
 }
 
-template <int G>
+template <int G, int NS>
 struct PsLayout {
     static constexpr int kQ = G * kDecHd * 2;  // query rows of one item
-    static constexpr int kQOff = kStStages * 2 * kStBytes;
-    static constexpr int kMergeOff = kQOff + kStStages * kQ;
+    static constexpr int kQOff = NS * 2 * kStBytes;
+    static constexpr int kMergeOff = kQOff + NS * kQ;
     static constexpr int kPreOff = kMergeOff + kStWarps * (kDecHd + 2) * 4;
     static constexpr int kLenOff = kPreOff + (kPsMaxSeq + 1) * 4;
     static constexpr int kBarOff = (kLenOff + kPsMaxSeq * 4 + 7) / 8 * 8;
-    static constexpr int kAbortOff = kBarOff + 2 * kStStages * 8;
+    static constexpr int kAbortOff = kBarOff + 2 * NS * 8;
     static constexpr int kTotal = kAbortOff + 16 + 128;  // + 128: base alignment
 };
 
@@ -359,21 +359,21 @@ __device__ __forceinline__ void stream_stage(const uint8_t* Ks, const uint8_t* V
 }
 
 // ------------------------------------------------ one CTA per (sequence, kv head)
-template <int G>
+template <int G, int NS>
 __global__ void __launch_bounds__(kStThreads, G <= 4 ? 2 : 1) decode_attn_stream_kernel(const DecodeArgs a) {
     pdl_trigger();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-    uint64_t* full = reinterpret_cast<uint64_t*>(ring + kStStages * 2 * kStBytes);
-    uint64_t* empty = full + kStStages;
-    static_assert(kStWarps * G * (kDecHd + 2) * 4 <= kStStages * 2 * kStBytes, "merge area reuses the ring");
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + NS * 2 * kStBytes);
+    uint64_t* empty = full + NS;
+    static_assert(kStWarps * G * (kDecHd + 2) * 4 <= NS * 2 * kStBytes, "merge area reuses the ring");
 
     const int bk = blockIdx.x;  // sequence * kv_heads + kv head
     const int b = bk / a.kv_heads, kvh = bk % a.kv_heads;
     const int split = blockIdx.y;  // context split (a.splits > 1: partials for decode_combine_kernel)
     if (threadIdx.x == kStWarps * 32) {
         const int64_t k0 = (int64_t)split * a.chunk;
-        prefetch_kv_l2(a, b, kvh, k0, min(min(k0 + kStStages * kStKeys, k0 + (int64_t)a.chunk), a.cap));
+        prefetch_kv_l2(a, b, kvh, k0, min(min(k0 + NS * kStKeys, k0 + (int64_t)a.chunk), a.cap));
     }
     pdl_wait();  // lens, q and the caches come from earlier kernels
     const int len = (int)min((int64_t)(a.lens ? a.lens[b] : a.ctx), a.cap);
@@ -384,7 +384,7 @@ __global__ void __launch_bounds__(kStThreads, G <= 4 ? 2 : 1) decode_attn_stream
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStStages; ++s) {
+        for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kStWarps);
         }
@@ -410,9 +410,9 @@ __global__ void __launch_bounds__(kStThreads, G <= 4 ? 2 : 1) decode_attn_stream
             const __half* vbase = a.vc + (((int64_t)b * a.kv_heads + kvh) * a.cap + c0) * kDecHd;
             int i = 0;
             for (; i < nst; ++i) {
-                const int slot = i % kStStages;
-                if (i >= kStStages &&
-                    !mbar_wait_bounded(&empty[slot], ((uint32_t)(i / kStStages) & 1u) ^ 1u, no_abort)) {
+                const int slot = i % NS;
+                if (i >= NS &&
+                    !mbar_wait_bounded(&empty[slot], ((uint32_t)(i / NS) & 1u) ^ 1u, no_abort)) {
                     if (a.err) atomicCAS(a.err, 0, 0x401);
                     break;
                 }
@@ -423,8 +423,8 @@ __global__ void __launch_bounds__(kStThreads, G <= 4 ? 2 : 1) decode_attn_stream
                 bulk_load(ring + slot * 2 * kStBytes + kStBytes, vbase + (int64_t)k0 * kDecHd, bytes, &full[slot]);
             }
             // every copy issued has landed before the ring is reused or the CTA exits
-            for (int j = i - kStStages < 0 ? 0 : i - kStStages; j < i; ++j)
-                if (!mbar_wait_bounded(&full[j % kStStages], (uint32_t)(j / kStStages) & 1u, no_abort, 200000000ull) &&
+            for (int j = i - NS < 0 ? 0 : i - NS; j < i; ++j)
+                if (!mbar_wait_bounded(&full[j % NS], (uint32_t)(j / NS) & 1u, no_abort, 200000000ull) &&
                     a.err)
                     atomicCAS(a.err, 0, 0x402);
         }
@@ -440,8 +440,8 @@ __global__ void __launch_bounds__(kStThreads, G <= 4 ? 2 : 1) decode_attn_stream
             for (int e = 0; e < 8; ++e) q[g][e] = f[e] * a.scale_log2;
         }
         for (int i = 0; i < nst; ++i) {
-            const int slot = i % kStStages;
-            const bool ok = mbar_wait_bounded(&full[slot], (uint32_t)(i / kStStages) & 1u, no_abort);
+            const int slot = i % NS;
+            const bool ok = mbar_wait_bounded(&full[slot], (uint32_t)(i / NS) & 1u, no_abort);
             if (!__all_sync(0xffffffffu, ok)) {
                 if (lane == 0 && a.err) atomicCAS(a.err, 0, 0x403);
                 break;
@@ -498,10 +498,10 @@ __global__ void __launch_bounds__(kStThreads, G <= 4 ? 2 : 1) decode_attn_stream
     }
 }
 
-template <int G>
+template <int G, int NS>
 static int launch_stream(const DecodeArgs& a, int batch, int kv_heads, int splits, cudaStream_t st) {
-    auto kern = decode_attn_stream_kernel<G>;
-    constexpr int smem = stream_smem<G>();
+    auto kern = decode_attn_stream_kernel<G, NS>;
+    constexpr int smem = stream_smem<G, NS>();
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) {
         npub_internal_set_cuda_error(e);
@@ -549,9 +549,9 @@ __device__ __forceinline__ bool ps_empty(int cc, int S, int nctas) {
     return (int64_t)cc * S / nctas == (int64_t)(cc + 1) * S / nctas;
 }
 
-template <int G>
+template <int G, int NS>
 __global__ void __launch_bounds__(kStThreads, G > 4 ? 1 : 2) decode_attn_persist_kernel(const DecodeArgs a) {
-    using L = PsLayout<G>;
+    using L = PsLayout<G, NS>;
     pdl_trigger();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
@@ -561,14 +561,14 @@ __global__ void __launch_bounds__(kStThreads, G > 4 ? 1 : 2) decode_attn_persist
     int* pre = reinterpret_cast<int*>(base + L::kPreOff);
     int* lens = reinterpret_cast<int*>(base + L::kLenOff);
     uint64_t* full = reinterpret_cast<uint64_t*>(base + L::kBarOff);
-    uint64_t* empty = full + kStStages;
+    uint64_t* empty = full + NS;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(base + L::kAbortOff);
     static_assert(L::kTotal <= 227 * 1024, "shared memory budget");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int batch = a.batch, kvh = a.kv_heads;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStStages; ++s) {
+        for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kStWarps);
         }
@@ -581,7 +581,7 @@ __global__ void __launch_bounds__(kStThreads, G > 4 ? 1 : 2) decode_attn_persist
         const int64_t n = (min((int64_t)a.ctx, a.cap) + kStKeys - 1) / kStKeys;
         const int64_t S = (int64_t)batch * kvh * n;
         int64_t f = (int64_t)blockIdx.x * S / gridDim.x;
-        const int64_t fe = min(f + kStStages, ((int64_t)blockIdx.x + 1) * S / gridDim.x);
+        const int64_t fe = min(f + NS, ((int64_t)blockIdx.x + 1) * S / gridDim.x);
         while (f < fe) {
             const int64_t item = f / n, st = f % n;
             const int64_t k0 = st * kStKeys, k1 = min(min((int64_t)a.ctx, a.cap), k0 + (fe - f) * kStKeys);
@@ -624,9 +624,9 @@ __global__ void __launch_bounds__(kStThreads, G > 4 ? 1 : 2) decode_attn_persist
             PsCursor cu = ps_locate(f0, pre, batch, kvh);
             int i = 0;
             for (int f = f0; f < f1; ++f, ++i) {
-                const int slot = i % kStStages;
-                if (i >= kStStages &&
-                    !mbar_wait_bounded(&empty[slot], ((uint32_t)(i / kStStages) & 1u) ^ 1u, abort_flag)) {
+                const int slot = i % NS;
+                if (i >= NS &&
+                    !mbar_wait_bounded(&empty[slot], ((uint32_t)(i / NS) & 1u) ^ 1u, abort_flag)) {
                     if (a.err) atomicCAS(a.err, 0, 0x401);
                     break;
                 }
@@ -644,8 +644,8 @@ __global__ void __launch_bounds__(kStThreads, G > 4 ? 1 : 2) decode_attn_persist
             }
             // every copy issued has landed before the ring is reused or the CTA exits
             int never = 0;
-            for (int j = i - kStStages < 0 ? 0 : i - kStStages; j < i; ++j)
-                if (!mbar_wait_bounded(&full[j % kStStages], (uint32_t)(j / kStStages) & 1u, &never, 200000000ull) &&
+            for (int j = i - NS < 0 ? 0 : i - NS; j < i; ++j)
+                if (!mbar_wait_bounded(&full[j % NS], (uint32_t)(j / NS) & 1u, &never, 200000000ull) &&
                     a.err)
                     atomicCAS(a.err, 0, 0x402);
         }
@@ -659,9 +659,9 @@ __global__ void __launch_bounds__(kStThreads, G > 4 ? 1 : 2) decode_attn_persist
     if (f0 < f1) {
         PsCursor cu = ps_locate(f0, pre, batch, kvh);
         for (int f = f0, i = 0; f < f1; ++f, ++i) {
-            const int slot = i % kStStages;
+            const int slot = i % NS;
             const bool good =
-                __all_sync(0xffffffffu, mbar_wait_bounded(&full[slot], (uint32_t)(i / kStStages) & 1u, abort_flag));
+                __all_sync(0xffffffffu, mbar_wait_bounded(&full[slot], (uint32_t)(i / NS) & 1u, abort_flag));
             if (!good && lane == 0) {
                 if (a.err) atomicCAS(a.err, 0, 0x403);
                 *abort_flag = 1;
@@ -767,7 +767,7 @@ __global__ void __launch_bounds__(kStThreads, G > 4 ? 1 : 2) decode_attn_persist
                         // compute threads, then merged in CTA order
                         float* stg = reinterpret_cast<float*>(ring);
                         constexpr int kPiece = G * (kDecHd + 2);
-                        constexpr int kChunk = kStStages * 2 * kStBytes / (kPiece * 4);
+                        constexpr int kChunk = NS * 2 * kStBytes / (kPiece * 4);
                         static_assert(kPiece % 2 == 0, "pieces are copied as float2");
                         for (int cc0 = c + 1; cc0 <= c_last; cc0 += kChunk) {
                             const int np = min(kChunk, c_last - cc0 + 1);
@@ -837,13 +837,13 @@ __global__ void __launch_bounds__(kStThreads, G > 4 ? 1 : 2) decode_attn_persist
                 a.out[(int64_t)b * a.ldo + x] = __float2half_rn(0.0f);
 }
 
-template <int G>
+template <int G, int NS>
 static int ps_occupancy() {
     static int occ = 0;
     if (occ == 0) {
         int o = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, decode_attn_persist_kernel<G>, kStThreads,
-                                                          PsLayout<G>::kTotal) != cudaSuccess ||
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, decode_attn_persist_kernel<G, NS>, kStThreads,
+                                                          PsLayout<G, NS>::kTotal) != cudaSuccess ||
             o <= 0) {
             cudaGetLastError();
             o = 1;
@@ -857,20 +857,49 @@ static int ps_occupancy() {
 // least ~4 stages per CTA.
 static int ps_max_ctas() { return min(kPsMaxCtas, num_sms() * 2); }
 
-template <int G>
+template <int G, int NS>
 static int launch_persist(DecodeArgs a, int64_t stages_max, size_t workspace_bytes, cudaStream_t st) {
-    auto kern = decode_attn_persist_kernel<G>;
-    constexpr int smem = PsLayout<G>::kTotal;
+    auto kern = decode_attn_persist_kernel<G, NS>;
+    constexpr int smem = PsLayout<G, NS>::kTotal;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) {
         npub_internal_set_cuda_error(e);
         return NPUB_ERR_CUDA;
     }
-    int64_t grid = (int64_t)num_sms() * ps_occupancy<G>();
+    int64_t grid = (int64_t)num_sms() * ps_occupancy<G, NS>();
     grid = min(grid, (int64_t)ps_max_ctas());
     grid = min(grid, max((int64_t)1, (stages_max + 3) / 4));
     if ((size_t)grid * G * (kDecHd + 2) * sizeof(float) > workspace_bytes || !a.part) return NPUB_ERR_WORKSPACE;
     return launch_pdl(kern, dim3((unsigned)grid), dim3(kStThreads), smem, st, a);
+}
+
+template <int NS>
+static int stream_by_group(int group, const DecodeArgs& a, int batch, int kv_heads, int splits, cudaStream_t st) {
+    switch (group) {
+        case 1: return launch_stream<1, NS>(a, batch, kv_heads, splits, st);
+        case 2: return launch_stream<2, NS>(a, batch, kv_heads, splits, st);
+        case 3: return launch_stream<3, NS>(a, batch, kv_heads, splits, st);
+        case 4: return launch_stream<4, NS>(a, batch, kv_heads, splits, st);
+        case 5: return launch_stream<5, NS>(a, batch, kv_heads, splits, st);
+        case 6: return launch_stream<6, NS>(a, batch, kv_heads, splits, st);
+        case 7: return launch_stream<7, NS>(a, batch, kv_heads, splits, st);
+        default: return launch_stream<8, NS>(a, batch, kv_heads, splits, st);
+    }
+}
+
+template <int NS>
+static int persist_by_group(int group, const DecodeArgs& a, int64_t stages, size_t workspace_bytes,
+                            cudaStream_t st) {
+    switch (group) {
+        case 1: return launch_persist<1, NS>(a, stages, workspace_bytes, st);
+        case 2: return launch_persist<2, NS>(a, stages, workspace_bytes, st);
+        case 3: return launch_persist<3, NS>(a, stages, workspace_bytes, st);
+        case 4: return launch_persist<4, NS>(a, stages, workspace_bytes, st);
+        case 5: return launch_persist<5, NS>(a, stages, workspace_bytes, st);
+        case 6: return launch_persist<6, NS>(a, stages, workspace_bytes, st);
+        case 7: return launch_persist<7, NS>(a, stages, workspace_bytes, st);
+        default: return launch_persist<8, NS>(a, stages, workspace_bytes, st);
+    }
 }
 
 __global__ void decode_combine_kernel(const float* __restrict__ part, int splits, int heads, __half* __restrict__ out,
@@ -1086,6 +1115,12 @@ extern "C" int npub_attention_decode(const void* q, int64_t ldq, const void* k_c
     const int group = heads / kv_heads;
     const int64_t items = (int64_t)batch * kv_heads;
     const bool streaming = group >= 1 && group <= 8;
+    // Ring depth (kernel A/B on one B200, L2 flushed): two 32 KB stages beat
+    // three for grouped heads (64 seq x 8 kv heads x 4096 keys 363 -> 343 us,
+    // 16 x 8 x 4096 112 -> 103 us) and for short contexts (128 x 32 x 512 keys
+    // 166 -> 160 us; the batch-32 x 1088-key layer step -0.9 %), three for one
+    // head per group at long contexts (64 x 32 x 4096 keys 596 vs 606 us).
+    const int ns = (group > 1 || ctx_max <= 2048) ? 2 : 3;
     // Schedules, by the number of (sequence, kv head) items (measured on B200):
     //  * >= 6 per SM: one streaming CTA per item;
     //  * 32 .. 6 per SM: the persistent grid over the stage list (4-24 % faster
@@ -1096,16 +1131,8 @@ extern "C" int npub_attention_decode(const void* q, int64_t ldq, const void* k_c
         items * ((cap + kStKeys - 1) / kStKeys) < 0x7fffffffLL) {
         a.part = reinterpret_cast<float*>(workspace);
         const int64_t stages = items * (((ctx_len > 0 ? (int64_t)ctx_len : cap) + kStKeys - 1) / kStKeys);
-        switch (group) {
-            case 1: return launch_persist<1>(a, stages, workspace_bytes, st);
-            case 2: return launch_persist<2>(a, stages, workspace_bytes, st);
-            case 3: return launch_persist<3>(a, stages, workspace_bytes, st);
-            case 4: return launch_persist<4>(a, stages, workspace_bytes, st);
-            case 5: return launch_persist<5>(a, stages, workspace_bytes, st);
-            case 6: return launch_persist<6>(a, stages, workspace_bytes, st);
-            case 7: return launch_persist<7>(a, stages, workspace_bytes, st);
-            default: return launch_persist<8>(a, stages, workspace_bytes, st);
-        }
+        return ns == 2 ? persist_by_group<2>(group, a, stages, workspace_bytes, st)
+                       : persist_by_group<3>(group, a, stages, workspace_bytes, st);
     }
     if (splits > 1) {
         const size_t need = (size_t)bh * splits * (kDecHd + 2) * sizeof(float);
@@ -1114,16 +1141,8 @@ extern "C" int npub_attention_decode(const void* q, int64_t ldq, const void* k_c
     }
     int rc;
     if (streaming) {
-        switch (group) {
-            case 1: rc = launch_stream<1>(a, batch, kv_heads, splits, st); break;
-            case 2: rc = launch_stream<2>(a, batch, kv_heads, splits, st); break;
-            case 3: rc = launch_stream<3>(a, batch, kv_heads, splits, st); break;
-            case 4: rc = launch_stream<4>(a, batch, kv_heads, splits, st); break;
-            case 5: rc = launch_stream<5>(a, batch, kv_heads, splits, st); break;
-            case 6: rc = launch_stream<6>(a, batch, kv_heads, splits, st); break;
-            case 7: rc = launch_stream<7>(a, batch, kv_heads, splits, st); break;
-            default: rc = launch_stream<8>(a, batch, kv_heads, splits, st); break;
-        }
+        rc = ns == 2 ? stream_by_group<2>(group, a, batch, kv_heads, splits, st)
+                     : stream_by_group<3>(group, a, batch, kv_heads, splits, st);
     } else {
         decode_attn_kernel<<<dim3(bh, splits), kDecWarps * 32, 0, st>>>(a);
         rc = npub_internal_launch_status();
