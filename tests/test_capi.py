@@ -83,3 +83,33 @@ def test_fused_entry_points_validate_before_any_device_work(libnpub_path):
     assert lib.npub_rope_kv_store(p, 512, 8, 4, 2, 1, 120, p, 1e4, p, p, 16, None) == -1  # head_dim % 16
     assert lib.npub_rope_kv_store(p, 256, 8, 4, 2, 1, 128, p, 1e4, p, p, 16, None) == -1  # ldx too small
     assert lib.npub_rope_kv_store(None, 0, 0, 1, 2, 1, 128, None, 1e4, None, None, 0, None) == 0  # no rows
+
+
+def test_folded_norm_entry_points_validate_before_any_device_work(libnpub_path):
+    """The RMSNorm-folded decode GEMM, its input kernel and the norm-folding
+    all-reduce reject bad shapes before touching a device; empty work is a
+    no-op and more than 64 tokens is NPUB_ERR_UNSUPPORTED."""
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    f = ctypes.c_float(1e-5)
+
+    def rms(A, lda, M, N, K, swiglu=0, rs=None, rs_n=0, rs_ld=0, rs_d=0, gamma=None, G=None, ldg=0, ss=None,
+            ss_ld=0, R=None, ldr=0, ldc=None):
+        return lib.npub_w8a16_gemm_rms(A, lda, p, 16 * ((K + 15) // 16), p, p, ldc if ldc is not None else N, R,
+                                       ldr, M, N, K, swiglu, rs, rs_n, rs_ld, rs_d, f, gamma, G, ldg, ss, ss_ld,
+                                       None, 0, 0, 0, None, 0, None)
+    assert rms(p, 16, 0, 128, 16) == 0                          # no tokens
+    assert rms(p, 16, 65, 128, 16) == -2                        # more than 64 tokens
+    assert rms(p, 24, 4, 128, 24) == -1                         # K % 16
+    assert rms(p, 16, 4, 128, 16, rs=p, rs_n=4, rs_ld=2, rs_d=128) == -1   # rs_ld < M
+    assert rms(p, 16, 4, 128, 16, G=p, gamma=None, ldg=128) == -1          # G without gamma
+    assert rms(p, 16, 4, 100, 16, ss=p, ss_ld=4) == -1                     # N % 32 with ss
+    assert rms(p, 16, 4, 128, 16, swiglu=1, R=p, ldr=128) == -1            # SwiGLU with a residual
+    # npub_rmsnorm_parts(x, ldx, gamma, G, ldg, ss, ss_ld, rows, d, stream)
+    assert lib.npub_rmsnorm_parts(p, 48, p, p, 48, p, 4, 4, 48, None) == -1   # d % 32
+    assert lib.npub_rmsnorm_parts(p, 64, p, p, 64, p, 2, 4, 64, None) == -1   # ss_ld < rows
+    assert lib.npub_rmsnorm_parts(None, 64, None, None, 64, None, 4, 0, 64, None) == 0
+    # npub_allreduce_f16_rms(comm, in, out, rows, d, residual, gamma, G, ss, ss_ld, stream)
+    assert lib.npub_allreduce_f16_rms(p, p, p, 4, 48, p, p, p, p, 4, None) == -1   # d % 32
+    assert lib.npub_allreduce_f16_rms(p, p, p, 4, 64, None, p, p, p, 4, None) == -1  # no residual
+    assert lib.npub_allreduce_f16_rms(None, None, None, 0, 64, None, None, None, None, 0, None) == 0
