@@ -443,7 +443,6 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
         : "r"(taddr)
         : "memory");
 }
-// Named barrier over `nthreads` threads (multiple of 32).
 // Hardware base-2 exponential (MUFU ex2, approximate, flush-to-zero).
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
