@@ -11,6 +11,8 @@
 // grouped-query groups of 1 to 8 heads, scheduled by the number of (sequence,
 // kv head) items; larger groups run a split kernel with 4 lanes per key and a
 // combine pass.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "gemm_tc.h"
 
@@ -63,6 +65,7 @@ struct DecodeArgs {
     float* part;       // split kernel: [bh, splits, hd + 2]; persistent kernel: [CTA, group, hd + 2]
     int* err;          // device error word
     uint64_t wait_ns;  // bound of the finishers' waits
+    int tail_first, tail_parts;  // one CTA per item: items >= tail_first run in tail_parts pieces
 };
 
 __device__ __forceinline__ void ld8f(const __half* p, float (&f)[8]) {
@@ -234,6 +237,19 @@ constexpr int kPsMaxCtas = 1024;
 // piece (of an item started by an earlier CTA) is published, cleared by the
 // item's finisher, so every completed call leaves them zero.
 __device__ uint32_t g_decode_piece_flag[kPsMaxCtas];
+// Pieces of the split tail items of the one-CTA-per-item schedule that have
+// arrived (the last one merges them and clears the count).
+__device__ int g_decode_tail_cnt[kPsMaxCtas];
+constexpr int kTailPartsMax = 4;
+
+// NPUB_DECODE_TAIL_SPLIT=0 keeps every item in one CTA.
+static bool tail_split_enabled() {
+    static const int on = [] {
+        const char* v = getenv("NPUB_DECODE_TAIL_SPLIT");
+        return v && v[0] == '0' ? 0 : 1;
+    }();
+    return on != 0;
+}
 
 template <int G, int NS>
 constexpr int stream_smem() {
@@ -368,17 +384,34 @@ __global__ void __launch_bounds__(kStThreads, G <= 4 ? 2 : 1) decode_attn_stream
     uint64_t* empty = full + NS;
     static_assert(kStWarps * G * (kDecHd + 2) * 4 <= NS * 2 * kStBytes, "merge area reuses the ring");
 
-    const int bk = blockIdx.x;  // sequence * kv_heads + kv head
-    const int b = bk / a.kv_heads, kvh = bk % a.kv_heads;
+    // item = sequence * kv_heads + kv head; the items of the last, partial
+    // wave (>= tail_first) run in tail_parts pieces of whole 64-key stages
+    int item = blockIdx.x, part = 0, parts = 1;
+    if (a.tail_parts > 1 && (int)blockIdx.x >= a.tail_first) {
+        const int t = (int)blockIdx.x - a.tail_first;
+        item = a.tail_first + t / a.tail_parts;
+        part = t % a.tail_parts;
+        parts = a.tail_parts;
+    }
+    const int b = item / a.kv_heads, kvh = item % a.kv_heads;
     const int split = blockIdx.y;  // context split (a.splits > 1: partials for decode_combine_kernel)
     if (threadIdx.x == kStWarps * 32) {
-        const int64_t k0 = (int64_t)split * a.chunk;
+        int64_t k0 = (int64_t)split * a.chunk;
+        if (parts > 1) {  // the guess: every length is the largest (ctx)
+            const int64_t n = (min((int64_t)a.ctx, a.cap) + kStKeys - 1) / kStKeys;
+            k0 = part * n / parts * kStKeys;
+        }
         prefetch_kv_l2(a, b, kvh, k0, min(min(k0 + NS * kStKeys, k0 + (int64_t)a.chunk), a.cap));
     }
     pdl_wait();  // lens, q and the caches come from earlier kernels
     const int len = (int)min((int64_t)(a.lens ? a.lens[b] : a.ctx), a.cap);
-    const int c0 = split * a.chunk;
-    const int c1 = min(len, c0 + a.chunk);
+    int c0 = split * a.chunk;
+    int c1 = min(len, c0 + a.chunk);
+    if (parts > 1) {
+        const int n = (len + kStKeys - 1) / kStKeys;
+        c0 = part * n / parts * kStKeys;
+        c1 = min(len, (part + 1) * n / parts * kStKeys);
+    }
     const int nkeys = c1 > c0 ? c1 - c0 : 0;
     const int nst = (nkeys + kStKeys - 1) / kStKeys;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -484,7 +517,15 @@ __global__ void __launch_bounds__(kStThreads, G <= 4 ? 2 : 1) decode_attn_stream
                 A += row[d] * c;
             }
             const int h = kvh * G + g;
-            if (a.splits == 1) {
+            if (parts > 1) {
+                // this piece's (acc, m, l) for the item's last piece to merge
+                float* pp = a.part + ((int64_t)((int)blockIdx.x - a.tail_first) * G + g) * (kDecHd + 2);
+                pp[d] = A;
+                if (d == 0) {
+                    pp[kDecHd] = M;
+                    pp[kDecHd + 1] = L;
+                }
+            } else if (a.splits == 1) {
                 a.out[(int64_t)b * a.ldo + (int64_t)h * kDecHd + d] = __float2half_rn(L > 0.0f ? A / L : 0.0f);
             } else {
                 float* pp = a.part + (((int64_t)b * a.heads + h) * a.splits + split) * (kDecHd + 2);
@@ -496,18 +537,75 @@ __global__ void __launch_bounds__(kStThreads, G <= 4 ? 2 : 1) decode_attn_stream
             }
         }
     }
+    if (parts == 1) return;
+    // ---------------------------------------------------- tail item: last piece merges
+    __shared__ int last_piece;
+    const int ti = (item - a.tail_first);  // tail item index
+    __threadfence();                        // this piece's rows before its arrival
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int seen = atomicAdd(&g_decode_tail_cnt[ti], 1);
+        last_piece = seen == parts - 1;
+        if (last_piece) g_decode_tail_cnt[ti] = 0;  // every piece of the item has arrived
+        __threadfence();
+    }
+    __syncthreads();
+    if (!last_piece || threadIdx.x >= kDecHd) return;
+    const int d = threadIdx.x;
+    const float* base = a.part + (int64_t)ti * parts * G * (kDecHd + 2);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        // pieces in part order, whichever arrived last: the same sums every run
+        float M = -INFINITY;
+        for (int p = 0; p < parts; ++p) M = fmaxf(M, __ldcg(base + (p * G + g) * (kDecHd + 2) + kDecHd));
+        float L = 0.0f, A = 0.0f;
+        for (int p = 0; p < parts; ++p) {
+            const float* row = base + (p * G + g) * (kDecHd + 2);
+            const float mp = __ldcg(row + kDecHd);
+            const float c = mp == -INFINITY ? 0.0f : exp2f(mp - M);
+            L += __ldcg(row + kDecHd + 1) * c;
+            A += __ldcg(row + d) * c;
+        }
+        a.out[(int64_t)b * a.ldo + (int64_t)(kvh * G + g) * kDecHd + d] =
+            __float2half_rn(L > 0.0f ? A / L : 0.0f);
+    }
 }
 
 template <int G, int NS>
-static int launch_stream(const DecodeArgs& a, int batch, int kv_heads, int splits, cudaStream_t st) {
+static int launch_stream(DecodeArgs a, int batch, int kv_heads, int splits, void* workspace, size_t workspace_bytes,
+                         cudaStream_t st) {
     auto kern = decode_attn_stream_kernel<G, NS>;
     constexpr int smem = stream_smem<G, NS>();
+    static int occ = 0;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess && occ == 0) {
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kStThreads, smem);
+        if (e == cudaSuccess && occ <= 0) occ = 1;
+    }
     if (e != cudaSuccess) {
+        occ = 0;
         npub_internal_set_cuda_error(e);
         return NPUB_ERR_CUDA;
     }
-    return launch_pdl(kern, dim3(batch * kv_heads, splits), dim3(kStThreads), smem, st, a);
+    // The items past the last whole wave of resident CTAs would run alone, each
+    // CTA's stream bound by its ring's latency: run them in pieces that fill
+    // the idle slots and let each item's last piece merge them.
+    const int items = batch * kv_heads;
+    const int slots = num_sms() * occ;
+    const int tail = items > slots ? items % slots : 0;
+    const int stages = (int)((max(a.ctx, 1) + kStKeys - 1) / kStKeys);
+    int parts = tail > 0 ? min(kTailPartsMax, slots / tail) : 1;
+    parts = min(parts, stages / 2);
+    a.tail_first = items - tail;
+    a.tail_parts = 1;
+    int grid = items;
+    if (splits == 1 && parts >= 2 && tail <= kPsMaxCtas && workspace &&
+        (size_t)tail * parts * G * (kDecHd + 2) * sizeof(float) <= workspace_bytes && tail_split_enabled()) {
+        a.tail_parts = parts;
+        a.part = reinterpret_cast<float*>(workspace);
+        grid = items - tail + tail * parts;
+    }
+    return launch_pdl(kern, dim3(grid, splits), dim3(kStThreads), smem, st, a);
 }
 
 // ------------------------------------------------ persistent grid over the stage list
@@ -874,16 +972,17 @@ static int launch_persist(DecodeArgs a, int64_t stages_max, size_t workspace_byt
 }
 
 template <int NS>
-static int stream_by_group(int group, const DecodeArgs& a, int batch, int kv_heads, int splits, cudaStream_t st) {
+static int stream_by_group(int group, const DecodeArgs& a, int batch, int kv_heads, int splits, void* ws,
+                           size_t ws_bytes, cudaStream_t st) {
     switch (group) {
-        case 1: return launch_stream<1, NS>(a, batch, kv_heads, splits, st);
-        case 2: return launch_stream<2, NS>(a, batch, kv_heads, splits, st);
-        case 3: return launch_stream<3, NS>(a, batch, kv_heads, splits, st);
-        case 4: return launch_stream<4, NS>(a, batch, kv_heads, splits, st);
-        case 5: return launch_stream<5, NS>(a, batch, kv_heads, splits, st);
-        case 6: return launch_stream<6, NS>(a, batch, kv_heads, splits, st);
-        case 7: return launch_stream<7, NS>(a, batch, kv_heads, splits, st);
-        default: return launch_stream<8, NS>(a, batch, kv_heads, splits, st);
+        case 1: return launch_stream<1, NS>(a, batch, kv_heads, splits, ws, ws_bytes, st);
+        case 2: return launch_stream<2, NS>(a, batch, kv_heads, splits, ws, ws_bytes, st);
+        case 3: return launch_stream<3, NS>(a, batch, kv_heads, splits, ws, ws_bytes, st);
+        case 4: return launch_stream<4, NS>(a, batch, kv_heads, splits, ws, ws_bytes, st);
+        case 5: return launch_stream<5, NS>(a, batch, kv_heads, splits, ws, ws_bytes, st);
+        case 6: return launch_stream<6, NS>(a, batch, kv_heads, splits, ws, ws_bytes, st);
+        case 7: return launch_stream<7, NS>(a, batch, kv_heads, splits, ws, ws_bytes, st);
+        default: return launch_stream<8, NS>(a, batch, kv_heads, splits, ws, ws_bytes, st);
     }
 }
 
@@ -1112,6 +1211,8 @@ extern "C" int npub_attention_decode(const void* q, int64_t ldq, const void* k_c
     a.batch = batch;
     a.err = npub_internal_device_error_word();
     a.wait_ns = npub_internal_wait_limit_ns();
+    a.tail_first = 0;
+    a.tail_parts = 1;
     const int group = heads / kv_heads;
     const int64_t items = (int64_t)batch * kv_heads;
     const bool streaming = group >= 1 && group <= 8;
@@ -1141,8 +1242,8 @@ extern "C" int npub_attention_decode(const void* q, int64_t ldq, const void* k_c
     }
     int rc;
     if (streaming) {
-        rc = ns == 2 ? stream_by_group<2>(group, a, batch, kv_heads, splits, st)
-                     : stream_by_group<3>(group, a, batch, kv_heads, splits, st);
+        rc = ns == 2 ? stream_by_group<2>(group, a, batch, kv_heads, splits, workspace, workspace_bytes, st)
+                     : stream_by_group<3>(group, a, batch, kv_heads, splits, workspace, workspace_bytes, st);
     } else {
         decode_attn_kernel<<<dim3(bh, splits), kDecWarps * 32, 0, st>>>(a);
         rc = npub_internal_launch_status();
@@ -1157,6 +1258,7 @@ extern "C" int npub_attention_decode(const void* q, int64_t ldq, const void* k_c
 int npub_internal_decode_flags_reset() {
     const uint32_t zero[kPsMaxCtas] = {};
     cudaError_t e = cudaMemcpyToSymbol(g_decode_piece_flag, zero, sizeof(zero));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_decode_tail_cnt, zero, sizeof(zero));
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         npub_internal_set_cuda_error(e);

@@ -87,18 +87,25 @@ def test_decode_attention(cuda_device, rng, B, H, KV, ctx, cap):
     (6, 48, 8, 900, 904, None),                     # groups of 6, persistent
     (120, 40, 8, 50, 64, None),                     # groups of 5, one CTA per item
     (3, 21, 3, 2000, 2000, None),                   # groups of 7, context splits
+    (32, 32, 32, 1088, 1088, None),                 # one CTA per item, the last partial wave in pieces
+    (120, 32, 8, 700, 704, "tail-edge"),            # the same, groups of 4, tail items with 0, 1, 130 keys
+    (152, 64, 8, 600, 600, None),                   # the same, groups of 8
 ])
 def test_decode_attention_work_split(cuda_device, rng, B, H, KV, ctx, cap, lens):
     """The three schedules of the streaming kernel (persistent grid over the
     stage list with items cut between CTAs, CTAs without stages and sequences
-    without keys; context splits and a combine pass; one CTA per item) match
-    the oracle, and a second call on new data (the piece flags left zero)
-    does too."""
+    without keys; context splits and a combine pass; one CTA per item, the
+    items past the last whole wave cut in pieces merged by the last to
+    finish) match the oracle, and a second call on new data (the piece flags
+    and counts left zero) does too."""
     hd = 128
     if lens is None:
         lens = rng.integers(1, ctx + 1, B)
     elif lens == "with-empty":
         lens = rng.integers(1, ctx + 1, B) * (rng.random(B) > 0.1)
+    elif lens == "tail-edge":
+        lens = rng.integers(1, ctx + 1, B)
+        lens[-3:] = [0, 1, 130]
     lens = np.asarray(lens, dtype=np.int32)
     kc = torch.empty((B, KV, cap, hd), dtype=torch.float16, device=cuda_device)
     vc = torch.empty_like(kc)
