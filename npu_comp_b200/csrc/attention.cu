@@ -66,6 +66,7 @@ struct DecodeArgs {
     int* err;          // device error word
     uint64_t wait_ns;  // bound of the finishers' waits
     int tail_first, tail_parts;  // one CTA per item: items >= tail_first run in tail_parts pieces
+    int kv_evict_first;          // K/V stage loads marked evict-first in L2 (each key is read once)
 };
 
 __device__ __forceinline__ void ld8f(const __half* p, float (&f)[8]) {
@@ -275,6 +276,15 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                  : "memory");
 }
 
+// bulk_load with an L2 cache policy.
+__device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
 // L2 prefetch of the first stages of a (sequence, kv head)'s keys [k0, k1),
 // issued before griddepcontrol.wait: only the newest key is written by the
 // kernels this one follows, and L2 stays coherent with that write.
@@ -441,6 +451,7 @@ __global__ void __launch_bounds__(kStThreads, G <= 4 ? 2 : 1) decode_attn_stream
         if (lane == 0) {
             const __half* kbase = a.kc + (((int64_t)b * a.kv_heads + kvh) * a.cap + c0) * kDecHd;
             const __half* vbase = a.vc + (((int64_t)b * a.kv_heads + kvh) * a.cap + c0) * kDecHd;
+            const uint64_t pol = l2_evict_first_policy();
             int i = 0;
             for (; i < nst; ++i) {
                 const int slot = i % NS;
@@ -452,8 +463,14 @@ __global__ void __launch_bounds__(kStThreads, G <= 4 ? 2 : 1) decode_attn_stream
                 const int k0 = i * kStKeys;
                 const uint32_t bytes = (uint32_t)min(kStKeys, nkeys - k0) * kDecHd * 2;
                 mbar_arrive_expect_tx(&full[slot], 2 * bytes);
-                bulk_load(ring + slot * 2 * kStBytes, kbase + (int64_t)k0 * kDecHd, bytes, &full[slot]);
-                bulk_load(ring + slot * 2 * kStBytes + kStBytes, vbase + (int64_t)k0 * kDecHd, bytes, &full[slot]);
+                if (a.kv_evict_first) {
+                    bulk_load_hint(ring + slot * 2 * kStBytes, kbase + (int64_t)k0 * kDecHd, bytes, &full[slot], pol);
+                    bulk_load_hint(ring + slot * 2 * kStBytes + kStBytes, vbase + (int64_t)k0 * kDecHd, bytes,
+                                   &full[slot], pol);
+                } else {
+                    bulk_load(ring + slot * 2 * kStBytes, kbase + (int64_t)k0 * kDecHd, bytes, &full[slot]);
+                    bulk_load(ring + slot * 2 * kStBytes + kStBytes, vbase + (int64_t)k0 * kDecHd, bytes, &full[slot]);
+                }
             }
             // every copy issued has landed before the ring is reused or the CTA exits
             for (int j = i - NS < 0 ? 0 : i - NS; j < i; ++j)
@@ -720,6 +737,7 @@ __global__ void __launch_bounds__(kStThreads, G > 4 ? 1 : 2) decode_attn_persist
         // ------------------------------------------------------------ producer
         if (lane == 0 && f0 < f1) {
             PsCursor cu = ps_locate(f0, pre, batch, kvh);
+            const uint64_t pol = l2_evict_first_policy();
             int i = 0;
             for (int f = f0; f < f1; ++f, ++i) {
                 const int slot = i % NS;
@@ -733,8 +751,13 @@ __global__ void __launch_bounds__(kStThreads, G > 4 ? 1 : 2) decode_attn_persist
                 const uint32_t bytes = (uint32_t)min(kStKeys, lens[cu.b] - k0) * kDecHd * 2;
                 const int64_t kv = (((int64_t)cu.b * kvh + cu.h) * a.cap + k0) * kDecHd;
                 mbar_arrive_expect_tx(&full[slot], 2 * bytes + (qload ? (uint32_t)L::kQ : 0u));
-                bulk_load(ring + slot * 2 * kStBytes, a.kc + kv, bytes, &full[slot]);
-                bulk_load(ring + slot * 2 * kStBytes + kStBytes, a.vc + kv, bytes, &full[slot]);
+                if (a.kv_evict_first) {
+                    bulk_load_hint(ring + slot * 2 * kStBytes, a.kc + kv, bytes, &full[slot], pol);
+                    bulk_load_hint(ring + slot * 2 * kStBytes + kStBytes, a.vc + kv, bytes, &full[slot], pol);
+                } else {
+                    bulk_load(ring + slot * 2 * kStBytes, a.kc + kv, bytes, &full[slot]);
+                    bulk_load(ring + slot * 2 * kStBytes + kStBytes, a.vc + kv, bytes, &full[slot]);
+                }
                 if (qload)
                     bulk_load(base + L::kQOff + slot * L::kQ, a.q + (int64_t)cu.b * a.ldq + (int64_t)cu.h * G * kDecHd,
                               (uint32_t)L::kQ, &full[slot]);
@@ -1213,6 +1236,7 @@ extern "C" int npub_attention_decode(const void* q, int64_t ldq, const void* k_c
     a.wait_ns = npub_internal_wait_limit_ns();
     a.tail_first = 0;
     a.tail_parts = 1;
+    a.kv_evict_first = npub_internal_l2_evict_first() ? 1 : 0;
     const int group = heads / kv_heads;
     const int64_t items = (int64_t)batch * kv_heads;
     const bool streaming = group >= 1 && group <= 8;

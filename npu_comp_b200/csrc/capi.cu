@@ -42,6 +42,14 @@ uint64_t npub_internal_wait_limit_ns() {
     return ns;
 }
 
+bool npub_internal_l2_evict_first() {
+    static const bool on = [] {
+        const char* v = getenv("NPUB_L2_EVICT_FIRST");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
 int* npub_internal_device_error_word() {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_npub_device_error) != cudaSuccess) {

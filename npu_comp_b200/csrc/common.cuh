@@ -33,6 +33,9 @@ int* npub_internal_device_error_word();
 // pieces, peer flags of the all-reduces): NPUB_WAIT_LIMIT_MS in the
 // environment when the library loads (1 ms .. 60 s), else 2 s.
 uint64_t npub_internal_wait_limit_ns();
+// Streamed-once loads (decode weights, K/V stages) carry an evict-first L2
+// policy unless NPUB_L2_EVICT_FIRST=0 is set in the environment.
+bool npub_internal_l2_evict_first();
 // Re-zeroes the allocation-free entry point's tile counters on the current
 // device (after a wait gave up, they may hold counts of the aborted call).
 int npub_internal_noalloc_reset();
@@ -178,6 +181,25 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, uin
         "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
             smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+// L2 policy for data read once per pass (streamed weights, K/V stages): its
+// lines leave L2 first, so what the epilogues and the next kernel read
+// (instructions, residual rows, partial sums, prefetched tiles) stays.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// tma_load_3d with an L2 cache policy.
+__device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* m, uint64_t* bar, int c0, int c1, int c2,
+                                                 uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, "
+        "%4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "l"(pol)
         : "memory");
 }
 

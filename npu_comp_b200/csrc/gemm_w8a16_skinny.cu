@@ -266,6 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
         if (lane == 0) {
             const bool weights = warp == 0;
             if (!weights) pdl_wait();
+            const uint64_t pol = l2_evict_first_policy();  // each weight is read once
             const int depth = weights ? kS8 : kST;
             uint64_t* full = weights ? full8 : tok_full;
             uint64_t* empty = weights ? empty8 : tok_empty;
@@ -286,9 +287,14 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                     if (weights) {
                         mbar_arrive_expect_tx(&full[s], (uint32_t)L::kA8);
 #pragma unroll
-                        for (int c = 0; c < kBK / kBox8; ++c)
-                            tma_load_3d(sA8 + s * L::kA8 + c * L::kA8Box, &p.tmW, &full[s], k + c * kBox8,
-                                        sg.tile * kRows, 0);
+                        for (int c = 0; c < kBK / kBox8; ++c) {
+                            if (p.w_evict_first)
+                                tma_load_3d_hint(sA8 + s * L::kA8 + c * L::kA8Box, &p.tmW, &full[s], k + c * kBox8,
+                                                 sg.tile * kRows, 0, pol);
+                            else
+                                tma_load_3d(sA8 + s * L::kA8 + c * L::kA8Box, &p.tmW, &full[s], k + c * kBox8,
+                                            sg.tile * kRows, 0);
+                        }
                     } else {
                         mbar_arrive_expect_tx(&full[s], (uint32_t)L::kTok);
 #pragma unroll
@@ -875,6 +881,7 @@ int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, con
     if (rc) return rc;
     p.M = M;
     p.N = N;
+    p.w_evict_first = npub_internal_l2_evict_first() ? 1 : 0;
     p.k_steps = (K + skinny::kBK - 1) / skinny::kBK;
     p.n_tiles = (N + skinny::kRows - 1) / skinny::kRows;
     p.C = reinterpret_cast<__half*>(C);

@@ -59,6 +59,7 @@ struct SkinnyParams {
     int csplit;     // > 1: cluster split, grid = n_tiles * csplit (cluster t = tile t)
     CUtensorMap tmWn;  // the next GEMM's weights (pf_grid > 0)
     int pf_grid, pf_csplit, pf_tiles, pf_ksteps;
+    int w_evict_first;  // weight loads marked evict-first in L2
 };
 
 // Tile counters at the start of every workspace of this kernel: a fixed
