@@ -68,6 +68,7 @@ constexpr int kBox8 = 128;   // int8 bytes of a row per TMA box (the 128-byte sw
 constexpr int kS8 = 2;       // int8 ring depth (32 KB stages; 3 and 4 measured 0.3-0.7 % slower in decode)
 constexpr int kSA = 3;       // fp16 weight stages in TMEM (kBK / 2 columns each)
 constexpr int kPfUnits = 2;  // units of the next GEMM's CTAs prefetched to L2
+constexpr int kRecvPad = 4;  // fp32 padding of each row of the cluster pieces in shared memory
 constexpr int kConvWarps = 8;  // every converter warp works on every K step (half a row each)
 constexpr int kAcols = kBK / 2;
 constexpr int kAcol0 = 128;  // first TMEM column of the A stages (accumulators use [0, 2 BT) <= 128)
@@ -81,8 +82,9 @@ struct Smem {
     static constexpr int kTok = (kBK / 64) * kTokChunk;
     static constexpr int kA8Box = kRows * kBox8;
     static constexpr int kA8 = kRows * kBK;
+    static constexpr int kRes = BT == 32 ? BT * kRows * 2 : 0;  // staged residual rows, fp16 [BT][kRows]
     static constexpr int kBars = 8 * (2 * kS8 + 2 * kST + 2 * kSA + 6) + 16 + 4 * BT;  // + row scales
-    static constexpr int kTotal = kST * kTok + kS8 * kA8 + kBars + 1024;
+    static constexpr int kTotal = kST * kTok + kS8 * kA8 + kRes + kBars + 1024;
 };
 
 // L2 (.cg) float4 store / load of the fp32 partials.  Volatile asm with a
@@ -93,6 +95,14 @@ __device__ __forceinline__ void st_cg_f4(float4* ptr, float4 v) {
     asm volatile("st.global.cg.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
                  : "memory");
 }
+// 16-byte global -> shared copy that bypasses registers (the residual rows
+// are staged while the accumulator is waited for).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __device__ __forceinline__ float4 ld_cg_f4(const float4* ptr) {
     float4 v;
     asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];"
@@ -181,7 +191,8 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sTok = smem;                      // kST x kTok (1024-aligned)
     uint8_t* sA8 = sTok + kST * L::kTok;       // kS8 x kA8  (1024-aligned)
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sA8 + kS8 * L::kA8);
+    __half* sRes = reinterpret_cast<__half*>(sA8 + kS8 * L::kA8);  // kRes: staged residual rows
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sA8 + kS8 * L::kA8 + L::kRes);
     uint64_t* full8 = bars;                    // [kS8] int8 tile landed
     uint64_t* empty8 = full8 + kS8;            // [kS8] int8 tile read by the 8 converter warps
     uint64_t* tok_full = empty8 + kS8;         // [kST] token tile landed
@@ -458,8 +469,27 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
             const uint32_t b = (uint32_t)t & 1u, bph = ((uint32_t)t >> 1) & 1u;
             const int n = sg.tile * kRows + r;
             const bool nrow = n < p.N;
-            // the scale load is in flight while the accumulator is waited for
+            // the scale and gamma loads and the residual rows' copy into shared
+            // memory are in flight while the accumulator is waited for (read
+            // in the epilogue, each was a dependent round trip of several
+            // microseconds behind the memory traffic of the launch's end)
             const float sc = p.alpha * ((p.scale && nrow) ? __half2float(__ldg(p.scale + n)) : 1.0f);
+            // (32-token tiles; the 64-token kernel has no registers to spare)
+            constexpr bool kEarly = BT == 32;
+            const float gm_early = (kEarly && nm.G && nrow) ? __half2float(__ldg(nm.gamma + n)) : 0.0f;
+            if (kEarly && p.r_stage) {
+                // this warp's 32 rows of the tile for every token: 64 bytes per token
+                cp_async_wait_all();  // the previous segment's copy (same buffer) has landed
+                __syncwarp();
+                const int n0 = sg.tile * kRows + 32 * q;
+                for (int id = lane; id < 4 * M; id += 32) {
+                    const int tok = id >> 2, part = id & 3;
+                    if (n0 + 8 * part < p.N)
+                        cp_async16(sRes + tok * kRows + 32 * q + 8 * part, p.R + (int64_t)tok * p.ldr + n0 + 8 * part);
+                }
+                cp_async_commit();
+            }
+            bool res_ready = false;
             // The finished fp32 sums of this warp's 32 rows leave through
             // emit(): scaled (+ residual) and stored as fp16, or SwiGLU pairs.
             auto emit = [&](int c0, const float (&v)[16]) {
@@ -482,10 +512,22 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                     return;
                 }
                 float rv[16];
+                if (kEarly && p.r_stage) {
+                    if (!res_ready) {
+                        cp_async_wait_all();
+                        __syncwarp();
+                        res_ready = true;
+                    }
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    rv[j] = (p.R && nrow && c0 + j < M) ? __half2float(__ldg(p.R + (int64_t)(c0 + j) * p.ldr + n))
-                                                       : 0.0f;
+                    for (int j = 0; j < 16; ++j)
+                        rv[j] = (nrow && c0 + j < M) ? __half2float(sRes[(c0 + j) * kRows + r]) : 0.0f;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        rv[j] = (p.R && nrow && c0 + j < M)
+                                    ? __half2float(__ldg(p.R + (int64_t)(c0 + j) * p.ldr + n))
+                                    : 0.0f;
+                }
                 __half o[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) o[j] = __float2half_rn(v[j] * sc * rs[j] + rv[j]);
@@ -503,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                         nm.ss[(int64_t)(sg.tile * 4 + q) * nm.ss_ld + c0 + col] = tot;
                 }
                 if (!nrow) return;
-                const float gm = nm.G ? __half2float(__ldg(nm.gamma + n)) : 0.0f;
+                const float gm = kEarly ? gm_early : (nm.G ? __half2float(__ldg(nm.gamma + n)) : 0.0f);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     if (c0 + j < M) {
@@ -520,7 +562,10 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                     *abort_flag = 1;
                 }
                 tc_fence_after();
-                float* recv = reinterpret_cast<float*>(sA8);  // [C - 1][kRows][BT] fp32 pieces (rank 0)
+                // [C - 1][kRows][BT + 4] fp32 pieces (rank 0); the padded rows put the
+                // 32 lanes' 16-byte accesses on different banks
+                float* recv = reinterpret_cast<float*>(sA8);
+                constexpr int RL = BT + kRecvPad;
                 if (crank != 0) {
                     // wait until rank 0's MMAs are done (its ring is free), then write this
                     // piece into it and arrive on its barrier (release at cluster scope)
@@ -532,7 +577,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                         continue;
                     }
                     const uint32_t dst =
-                        mapa_shared(smem_u32(recv + ((int64_t)(crank - 1) * kRows + r) * BT), 0u);
+                        mapa_shared(smem_u32(recv + ((int64_t)(crank - 1) * kRows + r) * RL), 0u);
                     for (int c0 = 0; c0 < BT && c0 < M; c0 += 16) {
                         float v[16];
                         tmem_ld16(lane_base + b * (uint32_t)BT + (uint32_t)c0, v);
@@ -559,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                     float v[16];
                     tmem_ld16(lane_base + b * (uint32_t)BT + (uint32_t)c0, v);
                     for (int rr = 1; rr < C; ++rr) {  // the pieces in rank order
-                        const float4* pc = reinterpret_cast<const float4*>(recv + ((int64_t)(rr - 1) * kRows + r) * BT + c0);
+                        const float4* pc = reinterpret_cast<const float4*>(recv + ((int64_t)(rr - 1) * kRows + r) * RL + c0);
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
                             const float4 x = pc[j];
@@ -702,6 +747,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[b]);
         }
+        if (BT == 32 && p.r_stage) cp_async_wait_all();  // no copy into shared memory outlives the CTA
     }
 
     // Lane 0 alone ran some warps' role loops: a thread-counting barrier.
@@ -812,7 +858,8 @@ static int skinny_csplit(int bt, int n_tiles, int k_steps) {
     const int c = std::min(8, sms / n_tiles);
     if (c < 2 || n_tiles * c * 5 < sms * 4 || k_steps < 2 * c) return 1;
     // the other pieces land in the finisher's int8 ring
-    if ((size_t)(c - 1) * skinny::kRows * bt * sizeof(float) > (size_t)skinny::kS8 * skinny::kRows * skinny::kBK)
+    if ((size_t)(c - 1) * skinny::kRows * (bt + skinny::kRecvPad) * sizeof(float) >
+        (size_t)skinny::kS8 * skinny::kRows * skinny::kBK)
         return 1;
     static std::mutex mu;
     static int cache[2][9];
@@ -888,6 +935,11 @@ int w8a16_skinny_run(const void* A, int64_t lda, const void* W, int64_t ldw, con
     p.ldc = ldc;
     p.R = reinterpret_cast<const __half*>(R);
     p.ldr = ldr;
+    static const bool r_stage_off = [] {
+        const char* e = getenv("NPUB_SKINNY_RSTAGE");
+        return e && e[0] == '0';
+    }();
+    p.r_stage = (R && !r_stage_off && npub_aligned(R, 16) && ldr % 8 == 0 && N % 8 == 0) ? 1 : 0;
     p.scale = reinterpret_cast<const __half*>(scale);
     p.alpha = alpha;
     p.cnt = reinterpret_cast<unsigned*>(ws);

@@ -60,6 +60,7 @@ struct SkinnyParams {
     CUtensorMap tmWn;  // the next GEMM's weights (pf_grid > 0)
     int pf_grid, pf_csplit, pf_tiles, pf_ksteps;
     int w_evict_first;  // weight loads marked evict-first in L2
+    int r_stage;        // R staged in shared memory by 16-byte copies (R, ldr and N multiples of 8 halves)
 };
 
 // Tile counters at the start of every workspace of this kernel: a fixed
