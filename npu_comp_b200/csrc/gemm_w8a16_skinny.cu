@@ -226,6 +226,10 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
         u1 = unit_start((int64_t)blockIdx.x + 1, U, G);
     }
     const Range rg = make_range(u0, u1, KT);
+    // Cluster split with more than 16 tokens: converter warps 8-11 finish the
+    // second 16-token block of the tile while epilogue warps 4-7 finish the
+    // first (the epilogue's instruction latency, not its work, bounds it).
+    const bool helpers = BT == 32 && C > 1 && p.M > 16;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kS8; ++s) {
@@ -245,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
             mbar_init(&acc_empty[b], 4);
         }
         mbar_init(cl_go, 1);
-        mbar_init(cl_recv, 4 * (C - 1));
+        mbar_init(cl_recv, (helpers ? 8 : 4) * (C - 1));
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -421,15 +425,19 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
             __syncwarp();
             if (lane == 0) mbar_arrive(&a_full[sa]);
         }
-    } else if (warp >= 4) {
+    }
+    if ((warp >= 4 && warp < 8) || (helpers && warp >= 8 && warp < 12)) {
         // ------------------------------------------------------------ epilogue
         pdl_wait();
+        const bool helper = warp >= 8;
+        // token blocks [c_lo, c_hi) of 16 that this warp finishes
+        const int c_lo = helper ? 16 : 0, c_hi = helpers && !helper ? 16 : BT;
         const int q = warp & 3;
         const int r = 32 * q + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
         const int M = p.M;
         const SkinnyNorm& nm = p.nrm;
-        if (nm.rs_part) {
+        if (nm.rs_part && !helper) {
             // row scales of the folded RMSNorm, while the first MMAs run: 128 / BT
             // threads per token sum its partials (8 loads in flight each) and
             // combine in a fixed order
@@ -453,7 +461,14 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
             if (part == 0 && tt < BT) rstd_s[tt] = tt < M ? 1.0f / sqrtf(s / nm.rs_d + nm.rs_eps) : 0.0f;
             epi_bar();
         }
-        if (p.R || nm.G) {
+        if (nm.rs_part && helpers) {
+            // the helpers read the row scales the epilogue warps wrote
+            if (helper)
+                asm volatile("barrier.sync 2, 256;" ::: "memory");
+            else
+                asm volatile("barrier.arrive 2, 256;" ::: "memory");
+        }
+        if ((p.R || nm.G) && !helper) {
             // the residual rows (and gamma) the stores will read go to L2 now,
             // while the MMAs run: read at the end, after the weight stream
             // has filled HBM's queues, they cost several microseconds
@@ -482,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                 cp_async_wait_all();  // the previous segment's copy (same buffer) has landed
                 __syncwarp();
                 const int n0 = sg.tile * kRows + 32 * q;
-                for (int id = lane; id < 4 * M; id += 32) {
+                for (int id = 4 * c_lo + lane; id < 4 * min(M, c_hi); id += 32) {
                     const int tok = id >> 2, part = id & 3;
                     if (n0 + 8 * part < p.N)
                         cp_async16(sRes + tok * kRows + 32 * q + 8 * part, p.R + (int64_t)tok * p.ldr + n0 + 8 * part);
@@ -578,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                     }
                     const uint32_t dst =
                         mapa_shared(smem_u32(recv + ((int64_t)(crank - 1) * kRows + r) * RL), 0u);
-                    for (int c0 = 0; c0 < BT && c0 < M; c0 += 16) {
+                    for (int c0 = c_lo; c0 < c_hi && c0 < M; c0 += 16) {
                         float v[16];
                         tmem_ld16(lane_base + b * (uint32_t)BT + (uint32_t)c0, v);
 #pragma unroll
@@ -588,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) {
-                        mbar_arrive(&acc_empty[b]);
+                        if (!helper) mbar_arrive(&acc_empty[b]);
                         mbar_arrive_rel_cluster(mapa_shared(smem_u32(cl_recv), 0u));
                     }
                     cluster_arrive();  // this CTA's remote work is done
@@ -600,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                 if (!mbar_wait_acq_cluster(cl_recv, 0, abort_flag) && lane == 0) set_err(p.err, 0x30c);
                 cluster_arrive();  // every piece is in: the other ranks may leave
                 cl_arrived = true;
-                for (int c0 = 0; c0 < BT && c0 < M; c0 += 16) {
+                for (int c0 = c_lo; c0 < c_hi && c0 < M; c0 += 16) {
                     float v[16];
                     tmem_ld16(lane_base + b * (uint32_t)BT + (uint32_t)c0, v);
                     for (int rr = 1; rr < C; ++rr) {  // the pieces in rank order
@@ -618,7 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a16_skinny_kernel(const __grid_
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[b]);
+                if (lane == 0 && !helper) mbar_arrive(&acc_empty[b]);
                 continue;
             }
             // A tile cut between CTAs: its finisher is the CTA holding its first
