@@ -1,6 +1,6 @@
 // One-shot all-reduce over NVLink peer memory for the small messages of
 // tensor-parallel decode (the two per-layer reductions of a [batch, d] fp16
-// activation; BASELINE's TP sharding of the Llama layer).  NCCL stays in use
+// activation under the Llama layer's TP sharding).  NCCL stays in use
 // for large messages (prefill), where its bandwidth-optimal algorithms win;
 // at a few hundred KB its per-call latency inside a CUDA graph (21 us on 2
 // B200s, 36 us on 8, measured) is most of a decode layer.

@@ -25,7 +25,7 @@
 //
 // Reference semantics: the NPU matmul (_poc/mysim.cpp:109-113,
 // b_program_examples/npu.py:41-47) with float32 accumulation and an fp16 store;
-// the int8 weights and per-channel scale are the W8A16 scheme of this build.
+// the int8 weights and per-output-channel fp16 scales are the W8A16 scheme.
 #include "common.cuh"
 #include "gemm_tc.h"
 #include "gemm_w8a16_pair.h"
